@@ -1,0 +1,75 @@
+"""Loads libtelmo_b200.so and declares the C ABI of include/telmo_b200.h for ctypes.
+
+There is no fallback: if the library is missing or cannot load, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtelmo_b200.so")
+
+TELMO_OK = 0
+TELMO_ERR_ARGUMENT = -1
+TELMO_ERR_CUDA = -2
+TELMO_ERR_DEVICE_TIMEOUT = -3
+TELMO_ERR_UNSUPPORTED = -4
+TELMO_ERR_MODEL = -5
+
+_c = ctypes
+_vp = _c.c_void_p
+_sz = _c.c_size_t
+_int = _c.c_int
+_float = _c.c_float
+
+# name -> (restype, argtypes); every function include/telmo_b200.h declares.
+SIGNATURES = {
+    "telmo_ctx_create": (_int, [_int, _c.POINTER(_vp)]),
+    "telmo_ctx_destroy": (None, [_vp]),
+    "telmo_last_error": (_c.c_char_p, [_vp]),
+    "telmo_ctx_check": (_int, [_vp, _vp]),
+    "telmo_ctx_device": (_int, [_vp]),
+    "telmo_encode_int8": (_int, [_vp, _sz, _sz, _vp, _vp]),
+    "telmo_weights_upload": (_int, [_vp, _int, _sz, _sz, _vp, _vp, _c.POINTER(_vp)]),
+    "telmo_weights_free": (None, [_vp]),
+    "telmo_weights_shape": (_int, [_vp, _c.POINTER(_sz), _c.POINTER(_sz)]),
+    "telmo_linear": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _int, _float, _int, _vp, _int, _sz,
+                            _vp]),
+    "telmo_quantize_x2": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
+    "telmo_linear_q": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp, _vp, _int, _float, _int, _vp,
+                              _int, _sz, _vp]),
+}
+
+_lib = None
+
+
+class TelmoError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"telmo status {status}: {message}")
+        self.status = status
+
+
+def load():
+    """The loaded library. Raises when it is missing: there is no CPU path behind it."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing; build it with `python -m telmo_b200.build` (the CUDA path "
+            "has no fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, ctx=None) -> None:
+    if status != TELMO_OK:
+        msg = load().telmo_last_error(ctx)
+        raise TelmoError(status, msg.decode() if msg else "")

@@ -1,0 +1,328 @@
+// api.cu -- the C ABI of libtelmo_b200: contexts, weights and the matrix product.
+#include "../../include/telmo_b200.h"
+#include "api_internal.h"
+#include "kernels.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+using namespace telmo;
+
+namespace {
+thread_local std::string g_create_error;
+}  // namespace
+
+namespace telmo {
+
+int Ctx::fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    last_error = buf;
+    return code;
+}
+
+int Ctx::cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return TELMO_OK;
+    return fail(TELMO_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int Ctx::use_device() {
+    cudaError_t e = cudaSetDevice(device);
+    return cuda(e, "cudaSetDevice");
+}
+
+void* Ctx::workspace(size_t bytes, cudaStream_t stream) {
+    if (bytes <= ws_bytes) return ws;
+    // Growing: wait for work that may still read the old buffer, then replace it.
+    cudaStreamSynchronize(stream);
+    if (ws) cudaFree(ws);
+    ws = nullptr;
+    ws_bytes = 0;
+    size_t want = bytes + bytes / 4 + (1 << 20);
+    if (cudaMalloc(&ws, want) != cudaSuccess) return nullptr;
+    ws_bytes = want;
+    return ws;
+}
+
+}  // namespace telmo
+
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+extern "C" int telmo_ctx_create(int device, telmo_ctx** out) {
+    if (!out) {
+        g_create_error = "telmo_ctx_create: out is NULL";
+        return TELMO_ERR_ARGUMENT;
+    }
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || device < 0 || device >= count) {
+        g_create_error = "telmo_ctx_create: no CUDA device " + std::to_string(device) +
+                         (e != cudaSuccess ? std::string(" (") + cudaGetErrorString(e) + ")" : "");
+        return e != cudaSuccess ? TELMO_ERR_CUDA : TELMO_ERR_ARGUMENT;
+    }
+    cudaDeviceProp prop;
+    if ((e = cudaSetDevice(device)) != cudaSuccess || (e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+        g_create_error = std::string("telmo_ctx_create: ") + cudaGetErrorString(e);
+        return TELMO_ERR_CUDA;
+    }
+    if (prop.major != 10 || prop.minor != 0) {
+        g_create_error = "telmo_ctx_create: device " + std::to_string(device) + " is sm_" +
+                         std::to_string(prop.major) + std::to_string(prop.minor) +
+                         "; this build runs on sm_100a (B200) only";
+        return TELMO_ERR_UNSUPPORTED;
+    }
+    Ctx* ctx = new Ctx();
+    ctx->device = device;
+    ctx->sms = prop.multiProcessorCount;
+    if ((e = cudaMalloc(&ctx->error_word, sizeof(uint32_t))) != cudaSuccess ||
+        (e = cudaMemset(ctx->error_word, 0, sizeof(uint32_t))) != cudaSuccess) {
+        g_create_error = std::string("telmo_ctx_create: ") + cudaGetErrorString(e);
+        delete ctx;
+        return TELMO_ERR_CUDA;
+    }
+    *out = reinterpret_cast<telmo_ctx*>(ctx);
+    return TELMO_OK;
+}
+
+extern "C" void telmo_ctx_destroy(telmo_ctx* c) {
+    Ctx* ctx = as_ctx(c);
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->error_word) cudaFree(ctx->error_word);
+    delete ctx;
+}
+
+extern "C" const char* telmo_last_error(const telmo_ctx* c) {
+    const Ctx* ctx = reinterpret_cast<const Ctx*>(c);
+    return ctx ? ctx->last_error.c_str() : g_create_error.c_str();
+}
+
+extern "C" int telmo_ctx_device(const telmo_ctx* c) {
+    const Ctx* ctx = reinterpret_cast<const Ctx*>(c);
+    return ctx ? ctx->device : -1;
+}
+
+extern "C" int telmo_ctx_check(telmo_ctx* c, void* stream) {
+    Ctx* ctx = as_ctx(c);
+    if (!ctx) return TELMO_ERR_ARGUMENT;
+    if (int rc = ctx->use_device()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "telmo_ctx_check")) return rc;
+    uint32_t word = 0;
+    if (int rc = ctx->cuda(cudaMemcpy(&word, ctx->error_word, sizeof word, cudaMemcpyDeviceToHost),
+                           "telmo_ctx_check"))
+        return rc;
+    if (word != 0) {
+        cudaMemset(ctx->error_word, 0, sizeof(uint32_t));
+        return ctx->fail(TELMO_ERR_DEVICE_TIMEOUT,
+                         "a kernel gave up on a bounded wait (device error %u); its results are invalid",
+                         word);
+    }
+    return TELMO_OK;
+}
+
+extern "C" int telmo_encode_int8(const float* rows, size_t n, size_t k, int8_t* values, float* scales) {
+    if (!rows || !values || !scales) return TELMO_ERR_ARGUMENT;
+    encode_int8_panels(rows, n, k, values, scales);
+    return TELMO_OK;
+}
+
+namespace telmo {
+
+void encode_int8_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales) {
+    // quant::encode, Precision::Int8 (src/quant.rs:202-269): quantize_row_int8 per output row,
+    // then panel p = o / 16 holds k runs of 16 outputs.
+    const size_t panels = (n + 15) / 16;
+    memset(values, 0, panels * 16 * k);
+    memset(scales, 0, panels * 16 * sizeof(float));
+    for (size_t o = 0; o < n; ++o) {
+        const float* x = rows + o * k;
+        float amax = 0.0f;
+        for (size_t i = 0; i < k; ++i) amax = std::fmax(amax, std::fabs(x[i]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const size_t p = o / 16, j = o % 16;
+        for (size_t i = 0; i < k; ++i) {
+            float q = std::round(x[i] * id);
+            q = std::fmin(std::fmax(q, -127.0f), 127.0f);
+            values[(p * k + i) * 16 + j] = static_cast<int8_t>(q);
+        }
+        scales[p * 16 + j] = d;
+    }
+}
+
+int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
+                   const float* scales, DevWeights* out) {
+    if (precision != TELMO_PRECISION_INT8)
+        return ctx->fail(TELMO_ERR_UNSUPPORTED,
+                         "precision %d: this build runs int8 weights (TELMO_PRECISION_INT8) only",
+                         precision);
+    if (!panel_values || !scales || n == 0 || k == 0 || n > (1u << 30) || k > (1u << 30))
+        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: bad sizes n=%zu k=%zu or null data", n, k);
+    const size_t ld = round_up(k, 16);
+    std::vector<int8_t> rows(n * ld, 0);
+    std::vector<float> sc(n);
+    const int8_t* v = static_cast<const int8_t*>(panel_values);
+    for (size_t o = 0; o < n; ++o) {
+        const size_t p = o / 16, j = o % 16;
+        const int8_t* src = v + p * k * 16 + j;
+        int8_t* dst = rows.data() + o * ld;
+        for (size_t i = 0; i < k; ++i) dst[i] = src[i * 16];
+        sc[o] = scales[p * 16 + j];
+    }
+    out->n = static_cast<int>(n);
+    out->k = static_cast<int>(k);
+    out->ld = static_cast<int64_t>(ld);
+    if (int rc = ctx->cuda(cudaMalloc(&out->values, rows.size()), "weights")) return rc;
+    if (int rc = ctx->cuda(cudaMalloc(&out->scales, n * sizeof(float)), "weights")) return rc;
+    if (int rc = ctx->cuda(cudaMemcpy(out->values, rows.data(), rows.size(), cudaMemcpyHostToDevice), "weights"))
+        return rc;
+    return ctx->cuda(cudaMemcpy(out->scales, sc.data(), n * sizeof(float), cudaMemcpyHostToDevice), "weights");
+}
+
+void free_weights(DevWeights* w) {
+    if (w->values) cudaFree(w->values);
+    if (w->scales) cudaFree(w->scales);
+    w->values = nullptr;
+    w->scales = nullptr;
+}
+
+}  // namespace telmo
+
+extern "C" int telmo_weights_upload(telmo_ctx* c, int precision, size_t n, size_t k,
+                                    const void* panel_values, const float* scales, telmo_weights** out) {
+    Ctx* ctx = as_ctx(c);
+    if (!ctx || !out) return TELMO_ERR_ARGUMENT;
+    *out = nullptr;
+    if (int rc = ctx->use_device()) return rc;
+    auto* w = new Weights();
+    w->ctx = ctx;
+    if (int rc = upload_weights(ctx, precision, n, k, panel_values, scales, &w->dev)) {
+        free_weights(&w->dev);
+        delete w;
+        return rc;
+    }
+    *out = reinterpret_cast<telmo_weights*>(w);
+    return TELMO_OK;
+}
+
+extern "C" void telmo_weights_free(telmo_weights* wp) {
+    auto* w = reinterpret_cast<Weights*>(wp);
+    if (!w) return;
+    cudaSetDevice(w->ctx->device);
+    free_weights(&w->dev);
+    delete w;
+}
+
+extern "C" int telmo_weights_shape(const telmo_weights* wp, size_t* n, size_t* k) {
+    auto* w = reinterpret_cast<const Weights*>(wp);
+    if (!w) return TELMO_ERR_ARGUMENT;
+    if (n) *n = static_cast<size_t>(w->dev.n);
+    if (k) *k = static_cast<size_t>(w->dev.k);
+    return TELMO_OK;
+}
+
+static int check_out(Ctx* ctx, int c_dtype, size_t ldc, size_t n, const void* c) {
+    if (!c) return ctx->fail(TELMO_ERR_ARGUMENT, "c is NULL");
+    if (c_dtype != TELMO_DTYPE_F32 && c_dtype != TELMO_DTYPE_BF16 && c_dtype != TELMO_DTYPE_I32_PAIR)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "unknown output dtype %d", c_dtype);
+    if (ldc < n) return ctx->fail(TELMO_ERR_ARGUMENT, "ldc %zu is below n %zu", ldc, n);
+    return TELMO_OK;
+}
+
+extern "C" int telmo_quantize_x2(telmo_ctx* c, const float* a, size_t lda, size_t m, size_t k,
+                                 int8_t* hi, int8_t* lo, size_t ldq, float* scale, void* stream) {
+    Ctx* ctx = as_ctx(c);
+    if (!ctx) return TELMO_ERR_ARGUMENT;
+    if (m == 0) return TELMO_OK;
+    if (!a || !hi || !lo || !scale || k == 0 || lda < k || ldq < k || ldq % 16 || m > (1u << 30))
+        return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_quantize_x2: bad arguments (m=%zu k=%zu lda=%zu ldq=%zu)",
+                         m, k, lda, ldq);
+    if (int rc = ctx->use_device()) return rc;
+    QuantAct q;
+    q.hi = hi;
+    q.lo = lo;
+    q.scale = scale;
+    q.ld = static_cast<int64_t>(ldq);
+    return ctx->cuda(quantize_x2(a, static_cast<int64_t>(lda), static_cast<int>(m), static_cast<int>(k), q,
+                                 static_cast<cudaStream_t>(stream)),
+                     "telmo_quantize_x2");
+}
+
+static int run_gemm(Ctx* ctx, const QuantAct& q, size_t m, const Weights* w, const float* bias, int act,
+                    float scale, int accumulate, void* c, int c_dtype, size_t ldc, cudaStream_t stream) {
+    GemmArgs g;
+    g.m = static_cast<int>(m);
+    g.a = q;
+    g.w = &w->dev;
+    g.bias = bias;
+    g.act = act;
+    g.scale = scale;
+    g.accumulate = accumulate;
+    g.out = c;
+    g.ldc = static_cast<int64_t>(ldc);
+    g.out_kind = c_dtype == TELMO_DTYPE_F32 ? kOutF32 : c_dtype == TELMO_DTYPE_BF16 ? kOutBF16 : kOutI32Pair;
+    g.error = ctx->error_word;
+    return ctx->cuda(gemm_i8x2(g, stream), "telmo_linear");
+}
+
+extern "C" int telmo_linear_q(telmo_ctx* c, const int8_t* hi, const int8_t* lo, size_t ldq,
+                              const float* row_scale, size_t m, const telmo_weights* wp, const float* bias,
+                              int act, float scale, int accumulate, void* out, int c_dtype, size_t ldc,
+                              void* stream) {
+    Ctx* ctx = as_ctx(c);
+    auto* w = reinterpret_cast<const Weights*>(wp);
+    if (!ctx || !w) return TELMO_ERR_ARGUMENT;
+    if (w->ctx != ctx) return ctx->fail(TELMO_ERR_ARGUMENT, "the weights belong to another context");
+    if (m == 0) return TELMO_OK;
+    if (int rc = check_out(ctx, c_dtype, ldc, static_cast<size_t>(w->dev.n), out)) return rc;
+    if (!hi || !lo || !row_scale || ldq < static_cast<size_t>(w->dev.k) || ldq % 16 || m > (1u << 30))
+        return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_linear_q: bad activations (ldq=%zu, k=%d)", ldq, w->dev.k);
+    if (act < TELMO_ACT_NONE || act > TELMO_ACT_SILU) return ctx->fail(TELMO_ERR_ARGUMENT, "unknown act %d", act);
+    if (int rc = ctx->use_device()) return rc;
+    QuantAct q;
+    q.hi = const_cast<int8_t*>(hi);
+    q.lo = const_cast<int8_t*>(lo);
+    q.scale = const_cast<float*>(row_scale);
+    q.ld = static_cast<int64_t>(ldq);
+    return run_gemm(ctx, q, m, w, bias, act, scale, accumulate, out, c_dtype, ldc,
+                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_linear(telmo_ctx* c, const float* a, size_t lda, size_t m, const telmo_weights* wp,
+                            const float* bias, int act, float scale, int accumulate, void* out, int c_dtype,
+                            size_t ldc, void* stream) {
+    Ctx* ctx = as_ctx(c);
+    auto* w = reinterpret_cast<const Weights*>(wp);
+    if (!ctx || !w) return TELMO_ERR_ARGUMENT;
+    if (w->ctx != ctx) return ctx->fail(TELMO_ERR_ARGUMENT, "the weights belong to another context");
+    if (m == 0) return TELMO_OK;
+    const size_t k = static_cast<size_t>(w->dev.k), n = static_cast<size_t>(w->dev.n);
+    if (!a || lda < k || m > (1u << 30))
+        return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_linear: a is NULL or lda %zu < k %zu", lda, k);
+    if (int rc = check_out(ctx, c_dtype, ldc, n, out)) return rc;
+    if (act < TELMO_ACT_NONE || act > TELMO_ACT_SILU) return ctx->fail(TELMO_ERR_ARGUMENT, "unknown act %d", act);
+    if (int rc = ctx->use_device()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t ldq = round_up(k, 16);
+    const size_t plane = round_up(m * ldq, 256);
+    auto* base = static_cast<uint8_t*>(ctx->workspace(2 * plane + round_up(m * sizeof(float), 256), s));
+    if (!base) return ctx->fail(TELMO_ERR_CUDA, "telmo_linear: workspace allocation failed");
+    QuantAct q;
+    q.hi = reinterpret_cast<int8_t*>(base);
+    q.lo = reinterpret_cast<int8_t*>(base + plane);
+    q.scale = reinterpret_cast<float*>(base + 2 * plane);
+    q.ld = static_cast<int64_t>(ldq);
+    if (int rc = ctx->cuda(quantize_x2(a, static_cast<int64_t>(lda), static_cast<int>(m), static_cast<int>(k), q, s),
+                           "telmo_linear"))
+        return rc;
+    return run_gemm(ctx, q, m, w, bias, act, scale, accumulate, out, c_dtype, ldc, s);
+}

@@ -1,0 +1,39 @@
+// api_internal.h -- the structures behind the C ABI's opaque handles.
+#pragma once
+
+#include "kernels.h"
+
+#include <cstdarg>
+#include <string>
+
+struct telmo_ctx;
+
+namespace telmo {
+
+struct Ctx {
+    int device = 0;
+    int sms = 148;
+    uint32_t* error_word = nullptr;  // device error word the kernels record into
+    void* ws = nullptr;              // growable workspace for telmo_linear's quantized operand
+    size_t ws_bytes = 0;
+    std::string last_error;
+
+    int fail(int code, const char* fmt, ...);
+    int cuda(cudaError_t e, const char* what);
+    int use_device();
+    void* workspace(size_t bytes, cudaStream_t stream);
+};
+
+struct Weights {
+    Ctx* ctx = nullptr;
+    DevWeights dev;
+};
+
+inline Ctx* as_ctx(telmo_ctx* c) { return reinterpret_cast<Ctx*>(c); }
+
+void encode_int8_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales);
+int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
+                   const float* scales, DevWeights* out);
+void free_weights(DevWeights* w);
+
+}  // namespace telmo

@@ -1,0 +1,52 @@
+// kernels.h -- host-side launchers of the CUDA kernels (internal to libtelmo_b200).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace telmo {
+
+enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutI32Pair = 2 };
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
+
+// Quantized activations for the split-int8 GEMM: two int8 levels and one scale per row, rows
+// `ld` bytes apart (ld a multiple of 16, at least K).
+struct QuantAct {
+    int8_t* hi = nullptr;
+    int8_t* lo = nullptr;
+    float* scale = nullptr;
+    int64_t ld = 0;
+};
+
+// Device weights of one linear layer: int8 row-major [n, ld] (ld = k rounded up to 16 bytes,
+// zero padded), per-output f32 scales.
+struct DevWeights {
+    int n = 0, k = 0;
+    int64_t ld = 0;
+    int8_t* values = nullptr;
+    float* scales = nullptr;
+};
+
+struct GemmArgs {
+    int m = 0;
+    QuantAct a;
+    const DevWeights* w = nullptr;
+    const float* bias = nullptr;  // [n] or null
+    int act = kActNone;
+    float scale = 1.0f;
+    int accumulate = 0;
+    void* out = nullptr;          // [m, ldc] of out_kind; kOutI32Pair writes acc_hi then acc_lo
+    int64_t ldc = 0;              // planes, each [m, ldc] int32
+    int out_kind = kOutF32;
+    uint32_t* error = nullptr;    // device error word
+};
+
+int num_sms();
+cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream);
+
+// x f32 [m, k] (rows ldx floats apart) -> hi, lo, scale (the oracle's quantize_x2 rule).
+cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,
+                        cudaStream_t stream);
+
+}  // namespace telmo

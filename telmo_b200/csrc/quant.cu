@@ -1,0 +1,83 @@
+// quant.cu -- split-int8 quantization of activation rows, the A operand of the int8 GEMM.
+//
+// Each row x of k values becomes s * (hi + lo / 254): s = amax / 127 and hi = round(x / s)
+// clamped to [-127, 127], exactly as quantize_row_int8 computes a weight row
+// (src/quant.rs:190-198), then lo = round((x - hi * s) * 254 / s), the residual at 254 times
+// finer steps. One warp per row; the f32 steps match oracle_quantize_x2 bit for bit.
+#include "kernels.h"
+
+namespace telmo {
+
+namespace {
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ void quant_one(float x, float d, float id, float id_lo, int8_t& h8,
+                                          int8_t& l8) {
+    float h = roundf(__fmul_rn(x, id));
+    h = fminf(fmaxf(h, -127.0f), 127.0f);
+    const float e = __fmaf_rn(-h, d, x);
+    float l = roundf(__fmul_rn(e, id_lo));
+    l = fminf(fmaxf(l, -127.0f), 127.0f);
+    h8 = static_cast<int8_t>(h);
+    l8 = static_cast<int8_t>(l);
+}
+
+__global__ void quantize_x2_kernel(const float* __restrict__ x, int64_t ldx, int m, int k,
+                                   int8_t* __restrict__ hi, int8_t* __restrict__ lo, int64_t ldq,
+                                   float* __restrict__ scale) {
+    const int warps = blockDim.x / 32;
+    const int row = blockIdx.x * warps + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    const float* xr = x + row * ldx;
+    const bool vec = (k % 4 == 0) && (ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    float amax = 0.0f;
+    if (vec) {
+        for (int i = lane * 4; i < k; i += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int i = lane; i < k; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
+    }
+    amax = warp_max(amax);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float id_lo = __fmul_rn(id, 254.0f);
+    int8_t* hr = hi + row * ldq;
+    int8_t* lr = lo + row * ldq;
+    if (vec && (ldq % 4 == 0)) {
+        for (int i = lane * 4; i < k; i += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            char4 h, l;
+            quant_one(v.x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
+            quant_one(v.y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
+            quant_one(v.z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
+            quant_one(v.w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
+            *reinterpret_cast<char4*>(hr + i) = h;
+            *reinterpret_cast<char4*>(lr + i) = l;
+        }
+    } else {
+        for (int i = lane; i < k; i += 32) quant_one(xr[i], d, id, id_lo, hr[i], lr[i]);
+    }
+    for (int i = k + lane; i < ldq; i += 32) hr[i] = lr[i] = 0;
+    if (lane == 0) scale[row] = d;
+}
+
+}  // namespace
+
+cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,
+                        cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    constexpr int kWarps = 8;
+    const int grid = (m + kWarps - 1) / kWarps;
+    quantize_x2_kernel<<<grid, kWarps * 32, 0, stream>>>(x, ldx, m, k, q.hi, q.lo, q.ld, q.scale);
+    return cudaGetLastError();
+}
+
+}  // namespace telmo

@@ -1,0 +1,136 @@
+"""Seeded synthetic inputs for the benchmark configurations (random-init weights, synthetic audio).
+
+The reference measures on LibriSpeech and FLEURS with real checkpoints; neither is available
+here, so every workload uses seeded synthetic data of the configured shapes:
+
+* config 1: one int8-weight linear, A f32 [1500, 1024] ~ N(0, 1), W int8 [4096, 1024] uniform in
+  [-127, 127], per-row scales U(1e-3, 1e-2), bias N(0, 0.02), all from seed 0.
+* Granite-shaped model: every linear int8 with per-row scales U(1e-3, 1e-2) and biases
+  N(0, 0.02); layer-norm gamma 1 + N(0, 0.02) and beta N(0, 0.02); depthwise weights
+  N(0, 1/kernel) with bias N(0, 0.02).
+* audio: 16 kHz, the sum of 8 sinusoids with frequencies U(50, 4000) Hz, amplitudes
+  U(0.02, 0.12) and phases U(0, 2 pi), plus N(0, 0.05) noise.
+
+All draws use numpy's PCG64 generator.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+SAMPLE_RATE = 16000
+
+
+def rng(seed: int) -> np.random.Generator:
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+def panels_from_rows(q: np.ndarray, scales: np.ndarray):
+    """Lays out int8 rows [n, k] and their scales [n] in the reference's 16-output panels
+    (src/quant.rs:1-13): panel p holds k runs of 16 outputs. Returns (values, scales)."""
+    n, k = q.shape
+    panels = (n + 15) // 16
+    padded = np.zeros((panels * 16, k), np.int8)
+    padded[:n] = q
+    values = padded.reshape(panels, 16, k).transpose(0, 2, 1).reshape(-1)
+    s = np.zeros(panels * 16, np.float32)
+    s[:n] = scales
+    return np.ascontiguousarray(values), s
+
+
+def rows_from_panels(values: np.ndarray, n: int, k: int) -> np.ndarray:
+    panels = (n + 15) // 16
+    return np.ascontiguousarray(values.reshape(panels, k, 16).transpose(0, 2, 1).reshape(-1, k)[:n])
+
+
+def int8_matrix(g: np.random.Generator, n: int, k: int):
+    """An int8 weight matrix in panels: values uniform in [-127, 127], scales U(1e-3, 1e-2)."""
+    q = g.integers(-127, 128, size=(n, k), dtype=np.int8)
+    scales = g.uniform(1e-3, 1e-2, size=n).astype(np.float32)
+    values, s = panels_from_rows(q, scales)
+    return values, s, n, k
+
+
+def config1(seed: int = 0, m: int = 1500, k: int = 1024, n: int = 4096):
+    """Config 1: (a [m, k] f32, (values, scales, n, k) int8 panels, bias [n] f32)."""
+    g = rng(seed)
+    a = g.standard_normal((m, k), dtype=np.float32)
+    w = int8_matrix(g, n, k)
+    bias = (g.standard_normal(n) * 0.02).astype(np.float32)
+    return a, w, bias
+
+
+GRANITE = dict(d_model=1024, heads=8, head_dim=128, layers=16, ff=4096, conv_kernel=15,
+               conv_channels=2048, n_mels=80, context=128, max_relative=512,
+               subsample_layers=[0, 1], vocab=2049, blank=0)
+
+
+def granite_config(**overrides) -> dict:
+    c = dict(GRANITE)
+    c.update(overrides)
+    return c
+
+
+def granite_entries(config: dict, seed: int = 1) -> dict:
+    """Random-init weights of a Granite-shaped model, named as the reference's pack entries
+    (src/granite.rs:224-371): matrices as (values, scales, n, k), vectors as f32 arrays."""
+    g = rng(seed)
+    c = config
+    d, cc, ff, k = c["d_model"], c["conv_channels"], c["ff"], c["conv_kernel"]
+    e = {}
+
+    def lin(name, n, kk):
+        e[name] = int8_matrix(g, n, kk)
+        e[name + ".b"] = (g.standard_normal(n) * 0.02).astype(np.float32)
+
+    def norm(name):
+        e[name + ".w"] = (1.0 + g.standard_normal(d) * 0.02).astype(np.float32)
+        e[name + ".b"] = (g.standard_normal(d) * 0.02).astype(np.float32)
+
+    lin("input", d, 4 * c["n_mels"])
+    for i in range(c["layers"]):
+        o = f"blocks.{i}"
+        for f in ("ff1", "ff2"):
+            norm(f"{o}.{f}.norm")
+            lin(f"{o}.{f}.up", ff, d)
+            lin(f"{o}.{f}.down", d, ff)
+        norm(f"{o}.norm_att")
+        e[f"{o}.qkv"] = int8_matrix(g, 3 * d, d)
+        e[f"{o}.rel"] = int8_matrix(g, 2 * c["context"] - 1, c["head_dim"])
+        lin(f"{o}.out", d, d)
+        norm(f"{o}.norm_conv")
+        lin(f"{o}.pw1", 2 * cc, d)
+        e[f"{o}.dw.w"] = (g.standard_normal((k, cc)) / math.sqrt(k)).astype(np.float32)
+        e[f"{o}.dw.b"] = (g.standard_normal(cc) * 0.02).astype(np.float32)
+        lin(f"{o}.pw2", d, cc)
+        norm(f"{o}.norm_out")
+    lin("head", c["vocab"], d)
+    lin("mid", d, c["vocab"])
+    return e
+
+
+def audio(seconds: float, seed: int = 2) -> np.ndarray:
+    """16 kHz f32 audio: 8 random sinusoids (50-4000 Hz) plus N(0, 0.05) noise."""
+    g = rng(seed)
+    n = int(round(seconds * SAMPLE_RATE))
+    t = np.arange(n, dtype=np.float64) / SAMPLE_RATE
+    freq = g.uniform(50.0, 4000.0, 8)
+    amp = g.uniform(0.02, 0.12, 8)
+    phase = g.uniform(0.0, 2 * math.pi, 8)
+    x = np.zeros(n, np.float64)
+    for f, a, p in zip(freq, amp, phase):
+        x += a * np.sin(2 * math.pi * f * t + p)
+    x += g.standard_normal(n) * 0.05
+    return x.astype(np.float32)
+
+
+def lengths_uniform(count: int, lo: float, hi: float, seed: int) -> np.ndarray:
+    """Utterance lengths in seconds, uniform in [lo, hi] (config 3)."""
+    return rng(seed).uniform(lo, hi, count)
+
+
+def lengths_log_uniform(count: int, lo: float, hi: float, seed: int) -> np.ndarray:
+    """Utterance lengths in seconds, log-uniform in [lo, hi] (config 5)."""
+    return np.exp(rng(seed).uniform(math.log(lo), math.log(hi), count))

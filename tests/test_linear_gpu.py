@@ -1,0 +1,156 @@
+"""Parity of the CUDA linear (split-int8 tcgen05 GEMM) with the oracle.
+
+Mirrors the reference's matrix-product tests (src/kernels/mod.rs:962-1128): shapes with ragged
+edges, every epilogue, accumulate, and the config-1 shape. Three bars:
+  * the quantized activations and the two int32 sums are bit-exact against the oracle;
+  * the scaled output equals the oracle's step-for-step restatement of the CUDA epilogue bit for
+    bit (act none/relu) or within 2 ulp-scale (SiLU, whose exp differs between libm and CUDA);
+  * against the reference's own f32 path (int8 weights widened, f32 activations), each output
+    matrix is within 1e-3 max-relative: max|got - ref| / max|ref| <= 1e-3.
+"""
+
+import numpy as np
+import pytest
+
+from telmo_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 1, 1), (1, 7, 5), (5, 13, 17), (6, 64, 16), (7, 33, 31), (13, 100, 50),
+          (64, 128, 96), (129, 300, 257), (200, 1024, 384), (300, 2049, 130)]
+
+
+def _case(m, k, n, seed):
+    g = synthetic.rng(seed)
+    a = g.standard_normal((m, k), dtype=np.float32)
+    values, scales, _, _ = synthetic.int8_matrix(g, n, k)
+    bias = (g.standard_normal(n) * 0.02).astype(np.float32)
+    c0 = g.standard_normal((m, n), dtype=np.float32)
+    return a, values, scales, bias, c0
+
+
+def _dev(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def _upload(ctx, values, scales, n, k):
+    from telmo_b200 import PackedWeights, Precision
+    return PackedWeights(n, k, Precision.INT8, values, scales).upload(ctx)
+
+
+def max_rel(got, ref):
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_quantized_activations_are_bit_exact(ctx, oracle_lib, m, k, n):
+    import torch
+    from telmo_b200 import Kernels
+    a, *_ = _case(m, k, n, 1)
+    ldq = (k + 15) // 16 * 16
+    hi = torch.zeros((m, ldq), dtype=torch.int8, device="cuda")
+    lo = torch.zeros_like(hi)
+    s = torch.zeros(m, dtype=torch.float32, device="cuda")
+    Kernels(ctx).quantize_x2(_dev(a), k, m, k, hi, lo, ldq, s)
+    ctx.check()
+    whi, wlo, ws = oracle_lib.quantize_x2(a)
+    assert np.array_equal(hi.cpu().numpy()[:, :k], whi)
+    assert np.array_equal(lo.cpu().numpy()[:, :k], wlo)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ws.view(np.uint32))
+    assert not hi.cpu().numpy()[:, k:].any()
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_int32_sums_are_bit_exact(ctx, oracle_lib, m, k, n):
+    import torch
+    from telmo_b200 import DType, Kernels
+    a, values, scales, bias, _ = _case(m, k, n, 2)
+    w = _upload(ctx, values, scales, n, k)
+    out = torch.zeros((2, m, n), dtype=torch.int32, device="cuda")
+    Kernels(ctx).matmul(_dev(a), k, m, w, out, n, out_dtype=DType.I32_PAIR)
+    ctx.check()
+    hi, lo, _ = oracle_lib.quantize_x2(a)
+    want_hi, want_lo = oracle_lib.gemm_i8_x2_acc(hi, lo, values, n, k)
+    got = out.cpu().numpy()
+    assert np.array_equal(got[0], want_hi)
+    assert np.array_equal(got[1], want_lo)
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+@pytest.mark.parametrize("act,accumulate,with_bias,scale", [
+    (0, False, False, 1.0), (1, False, True, 0.5), (2, True, True, 0.5), (0, True, False, 0.5)])
+def test_linear_matches_the_oracle(ctx, oracle_lib, m, k, n, act, accumulate, with_bias, scale):
+    from telmo_b200 import Act, Epilogue, Kernels
+    a, values, scales, bias, c0 = _case(m, k, n, 3)
+    w = _upload(ctx, values, scales, n, k)
+    b = bias if with_bias else None
+    c = _dev(c0)
+    Kernels(ctx).linear(_dev(a), m, w, c, Epilogue(bias=None if b is None else _dev(b),
+                                                   act=Act(act), scale=scale,
+                                                   accumulate=accumulate))
+    ctx.check()
+    got = c.cpu().numpy()
+    exact = oracle_lib.linear_x2(a, values, scales, n, k, b, act, scale, c0, accumulate)
+    if act == 2:
+        assert np.allclose(got, exact, rtol=2e-6, atol=1e-6)
+    else:
+        assert np.array_equal(got.view(np.uint32), exact.view(np.uint32))
+    ref = oracle_lib.linear_int8(a, values, scales, n, k, b, act, scale, c0, accumulate)
+    assert max_rel(got, ref) <= 1e-3
+
+
+def test_config1_full_size(ctx, oracle_lib):
+    """Config 1 (benches/matmul.rs shape): A [1500, 1024] f32, W int8 [4096, 1024], bias."""
+    import torch
+    from telmo_b200 import DType, Epilogue, Kernels
+    a, (values, scales, n, k), bias = synthetic.config1()
+    m = a.shape[0]
+    w = _upload(ctx, values, scales, n, k)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    kern = Kernels(ctx)
+    kern.linear(_dev(a), m, w, c, Epilogue(bias=_dev(bias)))
+    sums = torch.zeros((2, m, n), dtype=torch.int32, device="cuda")
+    kern.matmul(_dev(a), k, m, w, sums, n, out_dtype=DType.I32_PAIR)
+    ctx.check()
+    got = c.cpu().numpy()
+    ref = oracle_lib.linear_int8(a, values, scales, n, k, bias, threads=8)
+    assert max_rel(got, ref) <= 1e-3
+    # int32 sums bit-exact on a sample of rows (the full oracle triple loop takes minutes).
+    rows = np.array([0, 1, 127, 128, 500, 1023, 1499])
+    hi, lo, s = oracle_lib.quantize_x2(a[rows])
+    want_hi, want_lo = oracle_lib.gemm_i8_x2_acc(hi, lo, values, n, k)
+    got_sums = sums.cpu().numpy()
+    assert np.array_equal(got_sums[0][rows], want_hi)
+    assert np.array_equal(got_sums[1][rows], want_lo)
+
+
+def test_bf16_output(ctx, oracle_lib):
+    import torch
+    from telmo_b200 import Epilogue, Kernels
+    m, k, n = 77, 256, 200
+    a, values, scales, bias, _ = _case(m, k, n, 4)
+    w = _upload(ctx, values, scales, n, k)
+    c = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+    Kernels(ctx).linear(_dev(a), m, w, c, Epilogue(bias=_dev(bias)))
+    ctx.check()
+    exact = oracle_lib.linear_x2(a, values, scales, n, k, bias)
+    want = torch.from_numpy(exact).to(torch.bfloat16).float().numpy()
+    assert np.array_equal(c.float().cpu().numpy(), want)
+
+
+def test_bad_arguments_are_errors_not_crashes(ctx):
+    import torch
+    from telmo_b200 import Epilogue, Kernels, TelmoError
+    a, values, scales, bias, _ = _case(4, 32, 16, 5)
+    w = _upload(ctx, values, scales, 16, 32)
+    c = torch.zeros((4, 16), dtype=torch.float32, device="cuda")
+    kern = Kernels(ctx)
+    with pytest.raises(TelmoError):
+        kern.matmul(_dev(a), 31, 4, w, c, 16)           # lda below k
+    with pytest.raises(TelmoError):
+        kern.matmul(_dev(a), 32, 4, w, c, 15)           # ldc below n
+    with pytest.raises(TelmoError):
+        kern.linear(None, 4, w, c)                       # null input
+    kern.linear(_dev(a), 0, w, c, Epilogue.PLAIN)        # m = 0 is a no-op
+    ctx.check()
