@@ -105,6 +105,60 @@ int telmo_linear_q(telmo_ctx *ctx, const int8_t *hi, const int8_t *lo, size_t ld
                    int act, float scale, int accumulate, void *c, int c_dtype, size_t ldc,
                    void *stream);
 
+/* ---- the Granite Speech CTC encoder --------------------------------------------------------- */
+
+/* The architecture, as Granite's Config (src/granite.rs:37-164): config.json's sizes. */
+typedef struct telmo_granite_config {
+    int d_model, heads, head_dim, layers, ff, conv_kernel, conv_channels, n_mels, context,
+        max_relative;
+    int n_subsample;          /* entries used in subsample_layers */
+    int subsample_layers[8];  /* the blocks that halve the frame rate, increasing */
+    int vocab, blank;
+} telmo_granite_config;
+
+typedef struct telmo_granite telmo_granite;
+
+/* A model shell on the context, checked as Config::from_json checks a config
+ * (src/granite.rs:132-146). Its weights come next, entry by entry. */
+int telmo_granite_create(telmo_ctx *ctx, const telmo_granite_config *config, telmo_granite **out);
+void telmo_granite_free(telmo_granite *g);
+/* Pack entries by their names in a telmo pack (src/granite.rs:224-371, read back by
+ * Granite::from_pack, :424-500): matrices "input", "head", "mid", "blocks.<i>.{ff1.up, ff1.down,
+ * ff2.up, ff2.down, qkv, rel, out, pw1, pw2}" in the panel layout of telmo_weights_upload, and
+ * f32 vectors "input.b", "head.b", "mid.b", "blocks.<i>.{ff1.norm.w, ff1.norm.b, ff1.up.b,
+ * ff1.down.b, ff2..., norm_att.w/.b, out.b, norm_conv.w/.b, pw1.b, dw.w, dw.b, pw2.b,
+ * norm_out.w/.b}". A wrong name or size is TELMO_ERR_MODEL. */
+int telmo_granite_set_matrix(telmo_granite *g, const char *name, int precision, size_t n, size_t k,
+                             const void *panel_values, const float *scales);
+int telmo_granite_set_vector(telmo_granite *g, const char *name, size_t len, const float *data);
+/* Checks that every entry is present (Granite::from_pack's lookups). */
+int telmo_granite_finalize(telmo_granite *g);
+/* Config::frames_for (src/granite.rs:155-158): encoder frames for `rows` feature rows. */
+size_t telmo_granite_frames_for(const telmo_granite *g, size_t rows);
+
+/* Granite::encode (src/granite.rs:609-654) over a batch: features holds every utterance's rows
+ * [rows[u], 4 * n_mels] one after the other (device f32); out receives every utterance's
+ * frames [frames[u], d_model] one after the other (device f32, sized for the sum of
+ * telmo_granite_frames_for(rows[u])). rows is a host array; frames (host) receives the counts.
+ * tap_layer >= 0 stops after that block and returns its output (the reference's `tap`); -1 runs
+ * the whole encoder. An utterance with too few rows is TELMO_ERR_MODEL, as in the reference. */
+int telmo_granite_encode(telmo_granite *g, const float *features, const int *rows, int n_utt,
+                         float *out, int *frames, int tap_layer, void *stream);
+/* Granite::ctc_logits (src/granite.rs:657-673): logits [frames, ld] of encoder output. */
+int telmo_granite_logits(telmo_granite *g, const float *encoded, size_t frames, float *logits,
+                         size_t ld, void *stream);
+/* Granite::frame_ids (src/granite.rs:677-716): each frame's most likely token, the first where
+ * several tie (argmax, :1139-1147), into device ids; margin (device, may be NULL) receives the
+ * gap between the best and the second-best logit. */
+int telmo_granite_frame_ids(telmo_granite *g, const float *encoded, size_t frames, uint32_t *ids,
+                            float *margin, void *stream);
+
+/* ctc_tokens (src/granite.rs:1074-1094) on the device for n_utt utterances: utterance u's ids
+ * are ids[first[u] .. first[u] + frames[u]) (first, frames: device int arrays); its tokens go to
+ * tokens + 3 * first[u] as (id, frame, duration) triples and their number to counts[u]. */
+int telmo_ctc_tokens(telmo_ctx *ctx, const uint32_t *ids, const int *first, const int *frames,
+                     int n_utt, uint32_t blank, uint32_t *tokens, int *counts, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -283,9 +283,12 @@ class Granite:
             raise ValueError(f"missing entry {buf.value.decode()}")
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().oracle_granite_free(self._h)
-            self._h = None
+        try:
+            if getattr(self, "_h", None):
+                lib().oracle_granite_free(self._h)
+                self._h = None
+        except Exception:
+            pass
 
     def frames_for(self, rows):
         return lib().oracle_granite_frames_for(self._h, rows)

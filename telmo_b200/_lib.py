@@ -40,7 +40,25 @@ SIGNATURES = {
     "telmo_quantize_x2": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
     "telmo_linear_q": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp, _vp, _int, _float, _int, _vp,
                               _int, _sz, _vp]),
+    "telmo_granite_create": (_int, [_vp, _vp, _c.POINTER(_vp)]),
+    "telmo_granite_free": (None, [_vp]),
+    "telmo_granite_set_matrix": (_int, [_vp, _c.c_char_p, _int, _sz, _sz, _vp, _vp]),
+    "telmo_granite_set_vector": (_int, [_vp, _c.c_char_p, _sz, _vp]),
+    "telmo_granite_finalize": (_int, [_vp]),
+    "telmo_granite_frames_for": (_sz, [_vp, _sz]),
+    "telmo_granite_encode": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp]),
+    "telmo_granite_logits": (_int, [_vp, _vp, _sz, _vp, _sz, _vp]),
+    "telmo_granite_frame_ids": (_int, [_vp, _vp, _sz, _vp, _vp, _vp]),
+    "telmo_ctc_tokens": (_int, [_vp, _vp, _vp, _vp, _int, _c.c_uint32, _vp, _vp, _vp]),
 }
+
+
+class GraniteConfig(ctypes.Structure):
+    """telmo_granite_config (include/telmo_b200.h)."""
+    _fields_ = [(name, ctypes.c_int) for name in (
+        "d_model", "heads", "head_dim", "layers", "ff", "conv_kernel", "conv_channels", "n_mels",
+        "context", "max_relative", "n_subsample")] + [
+        ("subsample_layers", ctypes.c_int * 8), ("vocab", ctypes.c_int), ("blank", ctypes.c_int)]
 
 _lib = None
 

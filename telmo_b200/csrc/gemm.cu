@@ -7,38 +7,47 @@
 // row and weight scales and the reference's Epilogue (bias, act, scale, accumulate;
 // src/kernels/mod.rs:366-398) and stores f32 or bf16.
 //
+// The MMA computes the transposed tile: its A operand is 128 weight rows (output features) and
+// its B operand is 128 activation rows of the high level followed by the same 128 rows of the low
+// level (N = 256), so one tcgen05.mma (M=128, N=256, K=32) produces both levels' sums and the
+// weight tile is read once per K step. TMEM lane i holds feature n0 + i; columns 0..127 hold the
+// high sums of rows m0.., columns 128..255 the low sums.
+//
 // Structure: a persistent, warp-specialised kernel, one CTA per SM.
-//   warp 0      TMA producer: 128x128-byte boxes of A_hi, A_lo and W per stage, 128-byte swizzle
-//   warp 1      MMA issuer: tcgen05.mma kind::i8, M=128, N=BN, K=32, two accumulators per tile
-//   warps 2-5   epilogue: tcgen05.ld from TMEM, fused scale/bias/act/residual, global stores
-// TMEM holds two tiles' accumulators (2 x 2 x BN columns), so the epilogue of one tile overlaps
-// the main loop of the next. Every mbarrier wait is bounded; on timeout the kernel records
-// kErrWaitTimeout in the error word and returns.
+//   warp 0      TMA producer: 128 x 128-byte boxes of W, A_hi and A_lo per stage (128B swizzle)
+//   warp 1      MMA issuer: 4 x tcgen05.mma kind::i8 per 128-byte K step
+//   warps 2-5   epilogue: tcgen05.ld, fused scale/bias/act/residual, coalesced global stores
+// TMEM holds two tiles (2 x 256 columns), so the epilogue of one tile overlaps the main loop of
+// the next. Every mbarrier wait is bounded; on timeout the kernel records kErrWaitTimeout in the
+// error word and returns.
 #include "kernels.h"
 #include "ptx.cuh"
 
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cstring>
 #include <mutex>
 
 namespace telmo {
 
 namespace {
 
-constexpr int BM = 128;
+constexpr int BN = 128;  // output features per tile (MMA M)
+constexpr int BM = 128;  // activation rows per tile (MMA N = 2 * BM)
 constexpr int BK = 128;  // bytes = int8 elements per stage along K (one 128-byte swizzle row)
 constexpr int UMMA_K = 32;
 constexpr int kThreads = 192;
+constexpr int kStages = 4;
+constexpr int kTileBytes = 128 * BK;  // one 128-row operand box
+constexpr int kStageBytes = 3 * kTileBytes;
+constexpr int kTmemCols = 2 * 2 * BM;  // 2 buffers x (hi, lo) x BM columns
+constexpr int kStageOutBytes = 32 * 32 * 4;   // one 32 x 32 f32 output chunk
+constexpr int kOutStaging = 4 * 2 * kStageOutBytes;  // 4 epilogue warps x 2 buffers
+constexpr int kSmemBytes = kStages * kStageBytes + kOutStaging + 1024 + 256;
 
-template <int BN>
-struct Cfg {
-    static constexpr int kStages = BN == 128 ? 4 : 3;
-    static constexpr int kABytes = BM * BK;         // one level of A
-    static constexpr int kBBytes = BN * BK;
-    static constexpr int kStageBytes = 2 * kABytes + kBBytes;
-    static constexpr int kTmemCols = 4 * BN;        // 2 buffers x 2 levels x BN
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
-};
+// How the epilogue writes: TMA store of staged chunks, TMA reduce-add (accumulate), or direct
+// global stores when the output's alignment rules out TMA.
+enum OutPath : int { kDirect = 0, kTmaStore = 1, kTmaReduce = 2 };
 
 struct Params {
     int m, n, k;
@@ -51,6 +60,7 @@ struct Params {
     void* out;
     int64_t ldc;
     int out_kind;
+    int out_path;
     uint32_t* error;
 };
 
@@ -58,29 +68,95 @@ __device__ __forceinline__ void record_error(uint32_t* error, uint32_t code) {
     if (error) atomicCAS(error, 0u, code);
 }
 
-__device__ __forceinline__ float epilogue_value(int32_t acc_hi, int32_t acc_lo, float rs, float ws,
-                                                bool has_bias, float bias, int act, float scale) {
-    // Step for step what oracle_epilogue_x2 computes, with no contraction into FMA.
+// Step for step what oracle_epilogue_x2 computes, with no contraction into FMA. A missing bias
+// is passed as 0, which leaves every value unchanged (the sums are never -0).
+template <int ACT>
+__device__ __forceinline__ float epilogue_value(uint32_t acc_hi, uint32_t acc_lo, float rs, float ws,
+                                                float bias, float scale) {
     const float inv254 = 1.0f / 254.0f;
-    float v = __fadd_rn(__int2float_rn(acc_hi), __fmul_rn(__int2float_rn(acc_lo), inv254));
+    float v = __fadd_rn(__int2float_rn(static_cast<int32_t>(acc_hi)),
+                        __fmul_rn(__int2float_rn(static_cast<int32_t>(acc_lo)), inv254));
     v = __fmul_rn(v, rs);
     v = __fmul_rn(v, ws);
-    if (has_bias) v = __fadd_rn(v, bias);
-    if (act == kActRelu) v = fmaxf(v, 0.0f);
-    else if (act == kActSilu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    v = __fadd_rn(v, bias);
+    if (ACT == kActRelu) v = fmaxf(v, 0.0f);
+    if (ACT == kActSilu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
     return __fmul_rn(v, scale);
 }
 
-template <int BN>
+// One 32-row chunk of one thread's output column: 32 values computed branch-free, then stored
+// (rows_valid of them, each warp store covering 32 consecutive features of one row).
+template <int ACT, bool ACC, typename OutT>
+__device__ __forceinline__ void store_chunk(const uint32_t (&hi)[32], const uint32_t (&lo)[32], float my_rs,
+                                            float ws, float bs, float scale, OutT* o, int64_t ldc,
+                                            int rows_valid, bool n_ok) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        v[j] = epilogue_value<ACT>(hi[j], lo[j], __shfl_sync(0xffffffffu, my_rs, j), ws, bs, scale);
+    if (!n_ok) return;
+    if (rows_valid == 32) {
+        if (ACC) {
+            float old[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) old[j] = static_cast<float>(o[j * ldc]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(old[j], v[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j * ldc] = static_cast<OutT>(v[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < rows_valid) {
+                float x = v[j];
+                if (ACC) x = __fadd_rn(static_cast<float>(o[j * ldc]), x);
+                o[j * ldc] = static_cast<OutT>(x);
+            }
+    }
+}
+
+template <int ACT>
+__device__ __forceinline__ void compute_chunk(const uint32_t (&hi)[32], const uint32_t (&lo)[32], float my_rs,
+                                              float ws, float bs, float scale, float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        v[j] = epilogue_value<ACT>(hi[j], lo[j], __shfl_sync(0xffffffffu, my_rs, j), ws, bs, scale);
+}
+
+__device__ __forceinline__ void compute_chunk_any(int act, const uint32_t (&hi)[32], const uint32_t (&lo)[32],
+                                                  float my_rs, float ws, float bs, float scale, float (&v)[32]) {
+    if (act == kActNone) compute_chunk<kActNone>(hi, lo, my_rs, ws, bs, scale, v);
+    else if (act == kActRelu) compute_chunk<kActRelu>(hi, lo, my_rs, ws, bs, scale, v);
+    else compute_chunk<kActSilu>(hi, lo, my_rs, ws, bs, scale, v);
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_t (&hi)[32],
+                                                const uint32_t (&lo)[32], float my_rs, float ws, float bs,
+                                                float scale, OutT* o, int64_t ldc, int rows_valid, bool n_ok) {
+    if (act == kActNone) {
+        if (acc) store_chunk<kActNone, true>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+        else store_chunk<kActNone, false>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+    } else if (act == kActRelu) {
+        if (acc) store_chunk<kActRelu, true>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+        else store_chunk<kActRelu, false>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+    } else {
+        if (acc) store_chunk<kActSilu, true>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+        else store_chunk<kActSilu, false>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
-                 const __grid_constant__ CUtensorMap map_w, const Params p) {
-    using C = Cfg<BN>;
+gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
+                 const __grid_constant__ CUtensorMap map_lo, const __grid_constant__ CUtensorMap map_out,
+                 const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
-    uint64_t* empty = full + C::kStages;
-    uint64_t* tmem_full = empty + C::kStages;
+    uint8_t* staging = smem + kStages * kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kOutStaging);
+    uint64_t* empty = full + kStages;
+    uint64_t* tmem_full = empty + kStages;
     uint64_t* tmem_empty = tmem_full + 2;
     uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
@@ -91,7 +167,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
     const int kblocks = (p.k + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -101,12 +177,13 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
         }
         *abort_flag = 0;
         fence_barrier_init();
+        prefetch_tensormap(&map_w);
         prefetch_tensormap(&map_hi);
         prefetch_tensormap(&map_lo);
-        prefetch_tensormap(&map_w);
+        if (p.out_path != kDirect) prefetch_tensormap(&map_out);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_base_slot, C::kTmemCols);
+        tmem_alloc(tmem_base_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -114,6 +191,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
     tc_fence_after();
     const uint32_t tmem_base = *tmem_base_slot;
 
+    // Tiles run feature-block-major: consecutive CTAs share a weight tile, which L2 then serves.
     if (warp == 0) {
         // ---- TMA producer ------------------------------------------------------------------
         if (lane == 0) {
@@ -127,18 +205,18 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
                         *abort_flag = 1;
                         break;
                     }
-                    uint8_t* st = smem + stage * C::kStageBytes;
-                    mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-                    tma_load_2d(&map_hi, &full[stage], st, kb * BK, m0);
-                    tma_load_2d(&map_lo, &full[stage], st + C::kABytes, kb * BK, m0);
-                    tma_load_2d(&map_w, &full[stage], st + 2 * C::kABytes, kb * BK, n0);
-                    if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+                    uint8_t* st = smem + stage * kStageBytes;
+                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    tma_load_2d(&map_w, &full[stage], st, kb * BK, n0);
+                    tma_load_2d(&map_hi, &full[stage], st + kTileBytes, kb * BK, m0);
+                    tma_load_2d(&map_lo, &full[stage], st + 2 * kTileBytes, kb * BK, m0);
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         // ---- MMA issuer ----------------------------------------------------------------------
-        constexpr uint32_t idesc = idesc_i8(BM, BN);
+        constexpr uint32_t idesc = idesc_i8(128, 2 * BM);
         int stage = 0;
         uint32_t phase = 0;
         int it = 0;
@@ -151,27 +229,22 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
                 break;
             }
             tc_fence_after();
-            const uint32_t d_hi = tmem_base + static_cast<uint32_t>(buf * 2 * BN);
-            const uint32_t d_lo = d_hi + BN;
+            const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 2 * BM);
             bool ok = true;
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t a_hi = smem_u32(smem + stage * C::kStageBytes);
-                    const uint32_t a_lo = a_hi + C::kABytes;
-                    const uint32_t b = a_hi + 2 * C::kABytes;
+                    const uint32_t w = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t x = w + kTileBytes;  // hi rows, then lo rows: N = 256
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-                        const uint64_t db = sw128_desc(b + kk * UMMA_K);
-                        mma_i8(d_hi, sw128_desc(a_hi + kk * UMMA_K), db, idesc, acc);
-                        mma_i8(d_lo, sw128_desc(a_lo + kk * UMMA_K), db, idesc, acc);
-                    }
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
+                        mma_i8(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc,
+                               (kb > 0 || kk > 0) ? 1u : 0u);
                     mma_commit(&empty[stage]);
                 }
                 __syncwarp();
-                if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+                if (++stage == kStages) { stage = 0; phase ^= 1; }
             }
             if (!ok) {
                 record_error(p.error, kErrWaitTimeout);
@@ -182,88 +255,94 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_consta
             __syncwarp();
         }
     } else {
-        // ---- epilogue (warps 2..5) -------------------------------------------------------------
+        // ---- epilogue (warps 2..5): thread = one output feature, 32 rows per TMEM load ----------
         const int quad = warp & 3;  // TMEM lanes this warp may access: 32 * quad ..
-        const int r_in_tile = quad * 32 + lane;
+        const bool has_bias = p.bias != nullptr;
+        uint8_t* my_staging = staging + quad * 2 * kStageOutBytes;
+        int chunk_count = 0;
         int it = 0;
         for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
             const int buf = it & 1;
             const uint32_t use = static_cast<uint32_t>(it >> 1);
             const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
+            const int n = n0 + quad * 32 + lane;
+            const bool n_ok = n < p.n;
+            const float ws = n_ok ? __ldg(p.w_scale + n) : 0.0f;
+            const float bs = (has_bias && n_ok) ? __ldg(p.bias + n) : 0.0f;
             if (!mbar_wait(&tmem_full[buf], use & 1)) {
                 record_error(p.error, kErrWaitTimeout);
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const int row = m0 + r_in_tile;
-            const bool row_ok = row < p.m;
-            const float rs = row_ok ? p.row_scale[row] : 0.0f;
-            const uint32_t t_hi = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                  static_cast<uint32_t>(buf * 2 * BN);
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(buf * 2 * BM);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = 0; c < BM / 32; ++c) {
                 uint32_t hi[32], lo[32];
-                tmem_ld32(t_hi + c * 32, hi);
-                tmem_ld32(t_hi + BN + c * 32, lo);
+                tmem_ld32(taddr + c * 32, hi);
+                tmem_ld32(taddr + BM + c * 32, lo);
                 tmem_ld_wait();
-                const int col0 = n0 + c * 32;
-                if (!row_ok || col0 >= p.n) continue;
-                const int cols = min(32, p.n - col0);
-                if (p.out_kind == kOutI32Pair) {
-                    int32_t* o_hi = static_cast<int32_t*>(p.out) + row * p.ldc + col0;
-                    int32_t* o_lo = o_hi + static_cast<int64_t>(p.m) * p.ldc;
-                    for (int j = 0; j < cols; ++j) {
-                        o_hi[j] = static_cast<int32_t>(hi[j]);
-                        o_lo[j] = static_cast<int32_t>(lo[j]);
-                    }
-                    continue;
-                }
-                float v[32];
+                const int mc = m0 + c * 32;
+                if (mc >= p.m) continue;
+                const float my_rs = (mc + lane < p.m) ? __ldg(p.row_scale + mc + lane) : 0.0f;
+                const int rows_valid = p.m - mc < 32 ? p.m - mc : 32;
+                const int64_t off = static_cast<int64_t>(mc) * p.ldc + n;
+                if (p.out_path != kDirect) {
+                    // Stage the 32 x 32 chunk (row = activation row, column = feature) and let one
+                    // lane hand it to TMA; the buffer is reused two chunks later.
+                    float v[32];
+                    compute_chunk_any(p.act, hi, lo, my_rs, ws, bs, p.scale, v);
+                    uint8_t* sbuf = my_staging + (chunk_count & 1) * kStageOutBytes;
+                    ++chunk_count;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                    if (p.out_kind == kOutF32) {
+                        float* sf = reinterpret_cast<float*>(sbuf);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = min(col0 + j, p.n - 1);
-                    const float ws = __ldg(p.w_scale + col);
-                    const float bs = p.bias ? __ldg(p.bias + col) : 0.0f;
-                    v[j] = epilogue_value(static_cast<int32_t>(hi[j]), static_cast<int32_t>(lo[j]),
-                                          rs, ws, p.bias != nullptr, bs, p.act, p.scale);
-                }
-                if (p.out_kind == kOutF32) {
-                    float* o = static_cast<float*>(p.out) + row * p.ldc + col0;
-                    const bool vec = cols == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0;
-                    if (vec) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                            if (p.accumulate) {
-                                const float4 y = *reinterpret_cast<const float4*>(o + j);
-                                x.x = __fadd_rn(y.x, x.x); x.y = __fadd_rn(y.y, x.y);
-                                x.z = __fadd_rn(y.z, x.z); x.w = __fadd_rn(y.w, x.w);
-                            }
-                            *reinterpret_cast<float4*>(o + j) = x;
-                        }
+                        for (int j = 0; j < 32; ++j) sf[j * 32 + lane] = v[j];
                     } else {
-                        for (int j = 0; j < cols; ++j)
-                            o[j] = p.accumulate ? __fadd_rn(o[j], v[j]) : v[j];
+                        __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(sbuf);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sb[j * 32 + lane] = __float2bfloat16_rn(v[j]);
                     }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    const int x0 = n0 + quad * 32;
+                    if (lane == 0 && x0 < p.n) {
+                        if (p.out_path == kTmaReduce) tma_reduce_add_2d(&map_out, sbuf, x0, mc);
+                        else tma_store_2d(&map_out, sbuf, x0, mc);
+                        bulk_commit();
+                    }
+                } else if (p.out_kind == kOutF32) {
+                    store_chunk_any(p.act, p.accumulate != 0, hi, lo, my_rs, ws, bs, p.scale,
+                                    static_cast<float*>(p.out) + off, p.ldc, rows_valid, n_ok);
+                } else if (p.out_kind == kOutBF16) {
+                    store_chunk_any(p.act, p.accumulate != 0, hi, lo, my_rs, ws, bs, p.scale,
+                                    static_cast<__nv_bfloat16*>(p.out) + off, p.ldc, rows_valid, n_ok);
                 } else {
-                    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + row * p.ldc + col0;
-                    for (int j = 0; j < cols; ++j) {
-                        const float x = p.accumulate ? __fadd_rn(__bfloat162float(o[j]), v[j]) : v[j];
-                        o[j] = __float2bfloat16_rn(x);
+                    int32_t* o_hi = static_cast<int32_t*>(p.out) + static_cast<int64_t>(mc) * p.ldc + n;
+                    int32_t* o_lo = o_hi + static_cast<int64_t>(p.m) * p.ldc;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (mc + j < p.m && n_ok) {
+                            o_hi[j * p.ldc] = static_cast<int32_t>(hi[j]);
+                            o_lo[j * p.ldc] = static_cast<int32_t>(lo[j]);
+                        }
                     }
                 }
             }
             tc_fence_before();
             mbar_arrive(&tmem_empty[buf]);
         }
+        if (lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
@@ -280,15 +359,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// A 2-D int8 tensor map over rows of `cols` bytes, `ld` bytes apart, boxes of 128 bytes x
-// box_rows rows with the 128-byte swizzle. Reads past `cols` or `rows` fill zeros.
-bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
-              uint32_t box_rows) {
+// A 2-D int8 tensor map over rows of `cols` bytes, `ld` bytes apart, boxes of 128 bytes x 128
+// rows with the 128-byte swizzle. Reads past `cols` or `rows` fill zeros.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 128};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -296,29 +374,19 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
     return r == CUDA_SUCCESS;
 }
 
-template <int BN>
-cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
-    using C = Cfg<BN>;
-    const DevWeights& w = *g.w;
-    CUtensorMap mh, ml, mw;
-    if (!make_map(&mh, g.a.hi, g.m, w.k, g.a.ld, BM) || !make_map(&ml, g.a.lo, g.m, w.k, g.a.ld, BM) ||
-        !make_map(&mw, w.values, w.n, w.k, w.ld, BN))
-        return cudaErrorInvalidValue;
-    static uint64_t configured = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 64 || !(configured >> dev & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel<BN>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        if (dev < 64) configured |= uint64_t(1) << dev;
-    }
-    Params p{g.m, w.n, w.k, g.a.scale, w.scales, g.bias, g.act, g.scale, g.accumulate,
-             g.out, g.ldc, g.out_kind, g.error};
-    const int tiles = ((g.m + BM - 1) / BM) * ((w.n + BN - 1) / BN);
-    const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8x2_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(mh, ml, mw, p);
-    return cudaGetLastError();
+// The output tensor map: rows of n elements, ldc apart, 32 x 32 boxes without swizzle.
+bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t ldc) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const bool bf = kind == kOutBF16;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * (bf ? 2 : 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -337,7 +405,35 @@ int num_sms() {
 cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     if (g.m <= 0 || !g.w || g.w->n <= 0) return cudaSuccess;
     if ((g.a.ld % 16) || (g.w->ld % 16)) return cudaErrorInvalidValue;
-    return launch<128>(g, stream);
+    const DevWeights& w = *g.w;
+    CUtensorMap mw, mh, ml;
+    if (!make_map(&mw, w.values, w.n, w.k, w.ld) || !make_map(&mh, g.a.hi, g.m, w.k, g.a.ld) ||
+        !make_map(&ml, g.a.lo, g.m, w.k, g.a.ld))
+        return cudaErrorInvalidValue;
+    static uint64_t configured = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !(configured >> dev & 1)) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBytes);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured |= uint64_t(1) << dev;
+    }
+    // The output goes through TMA when its rows are 16-byte aligned.
+    CUtensorMap mo;
+    memset(&mo, 0, sizeof mo);
+    int path = kDirect;
+    const size_t esize = g.out_kind == kOutBF16 ? 2 : 4;
+    const bool aligned = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldc * esize) % 16 == 0);
+    if (aligned && g.out_kind == kOutF32) path = g.accumulate ? kTmaReduce : kTmaStore;
+    if (aligned && g.out_kind == kOutBF16 && !g.accumulate) path = kTmaStore;
+    if (path != kDirect && !make_out_map(&mo, g.out, g.out_kind, g.m, w.n, g.ldc)) path = kDirect;
+    Params p{g.m, w.n, w.k, g.a.scale, w.scales, g.bias, g.act, g.scale, g.accumulate,
+             g.out, g.ldc, g.out_kind, path, g.error};
+    const int tiles = ((g.m + BM - 1) / BM) * ((w.n + BN - 1) / BN);
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    gemm_i8x2_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mh, ml, mo, p);
+    return cudaGetLastError();
 }
 
 }  // namespace telmo

@@ -1,0 +1,498 @@
+// granite.cu -- the Granite Speech CTC encoder on the GPU, behind the C ABI.
+//
+// Host orchestration of Granite::encode (src/granite.rs:609-654) and Granite::block_span
+// (:802-952) for a batch of utterances whose frames are packed along the rows of every
+// activation matrix: each matrix product runs once over all utterances' rows, and only
+// attention (128-frame blocks), the depthwise convolution (zero padding at each utterance's
+// edges) and the stride-2 pooling see utterance boundaries, through task lists built here.
+#include "../../include/telmo_b200.h"
+#include "api_internal.h"
+#include "granite_internal.h"
+#include "kernels.h"
+#include "rowops.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace telmo {
+
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int Granite::fail(int code, const char* msg) { return ctx->fail(code, "%s", msg); }
+
+static void free_vec(DevVec& v) {
+    if (v.p) cudaFree(v.p);
+    v.p = nullptr;
+}
+
+Granite::~Granite() {
+    cudaSetDevice(ctx->device);
+    auto lin = [](Lin& l) { free_weights(&l.w); free_vec(l.b); };
+    auto nrm = [](Norm& n) { free_vec(n.g); free_vec(n.b); };
+    lin(input); lin(head); lin(mid);
+    for (auto& b : blocks) {
+        lin(b.ff1.up); lin(b.ff1.down); nrm(b.ff1.norm);
+        lin(b.ff2.up); lin(b.ff2.down); nrm(b.ff2.norm);
+        nrm(b.norm_att); nrm(b.norm_conv); nrm(b.norm_out);
+        free_weights(&b.qkv); free_weights(&b.rel);
+        lin(b.out); lin(b.pw1); lin(b.pw2);
+        free_vec(b.dw_w); free_vec(b.dw_b);
+    }
+    release_buffers();
+}
+
+void Granite::release_buffers() {
+    for (void* p : {static_cast<void*>(x), static_cast<void*>(y), static_cast<void*>(big), static_cast<void*>(att),
+                    static_cast<void*>(conv), static_cast<void*>(q.hi), static_cast<void*>(q.lo),
+                    static_cast<void*>(q.scale), static_cast<void*>(tasks_dev)})
+        if (p) cudaFree(p);
+    x = y = big = att = conv = nullptr;
+    q = QuantAct();
+    tasks_dev = nullptr;
+    cap_rows = 0;
+    tasks_cap = 0;
+}
+
+// Config::from_json's checks (src/granite.rs:132-146), plus the limits of these kernels.
+int Granite::validate(const telmo_granite_config& c, std::string& why) {
+    char buf[256];
+    auto bad = [&](const char* m) { why = m; return TELMO_ERR_MODEL; };
+    if (c.heads <= 0 || c.head_dim <= 0 || c.heads * c.head_dim != c.d_model) return bad("heads * head_dim != d_model");
+    if (c.head_dim % 16) return bad("head_dim is not a multiple of 16");
+    if (c.conv_kernel % 2 == 0 || c.conv_kernel <= 0) return bad("conv_kernel is not odd");
+    if (c.context <= 0 || c.context > c.max_relative) return bad("context is 0 or above max_relative");
+    if (c.layers < 2) return bad("fewer than 2 layers");
+    if (c.blank < 0 || c.blank >= c.vocab) return bad("blank is outside the vocabulary");
+    if (c.n_subsample < 0 || c.n_subsample > 8) return bad("too many subsample layers");
+    for (int i = 0; i < c.n_subsample; ++i) {
+        if (c.subsample_layers[i] < 0 || c.subsample_layers[i] >= c.layers) return bad("a subsample layer is out of range");
+        if (i && c.subsample_layers[i] <= c.subsample_layers[i - 1]) return bad("subsample layers are not increasing");
+    }
+    if (c.d_model % 128 || c.d_model > 2048) {
+        snprintf(buf, sizeof buf, "d_model %d: this build needs a multiple of 128 up to 2048", c.d_model);
+        why = buf;
+        return TELMO_ERR_UNSUPPORTED;
+    }
+    if (c.context > 128) return TELMO_ERR_UNSUPPORTED;
+    if (c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128) {
+        why = "head_dim must be 16, 32, 64 or 128";
+        return TELMO_ERR_UNSUPPORTED;
+    }
+    if (c.ff <= 0 || c.conv_channels <= 0 || c.n_mels <= 0 || c.vocab <= 0) return bad("a size is not positive");
+    return TELMO_OK;
+}
+
+Granite::Entry Granite::find(const std::string& name) {
+    const int d = c.d_model, cc = c.conv_channels;
+    Entry e;
+    auto mat = [&](DevWeights* w, int n, int k) { e.mat = w; e.n = n; e.k = k; };
+    auto vec = [&](DevVec* v, int len) { e.vec = v; e.len = len; };
+    if (name == "input") { mat(&input.w, d, 4 * c.n_mels); return e; }
+    if (name == "input.b") { vec(&input.b, d); return e; }
+    if (name == "head") { mat(&head.w, c.vocab, d); return e; }
+    if (name == "head.b") { vec(&head.b, c.vocab); return e; }
+    if (name == "mid") { mat(&mid.w, d, c.vocab); return e; }
+    if (name == "mid.b") { vec(&mid.b, d); return e; }
+    int i = -1;
+    char rest[64] = {0};
+    if (sscanf(name.c_str(), "blocks.%d.%63s", &i, rest) != 2 || i < 0 || i >= c.layers) return e;
+    Block& b = blocks[i];
+    const std::string r(rest);
+    if (r == "ff1.up") mat(&b.ff1.up.w, c.ff, d);
+    else if (r == "ff1.down") mat(&b.ff1.down.w, d, c.ff);
+    else if (r == "ff2.up") mat(&b.ff2.up.w, c.ff, d);
+    else if (r == "ff2.down") mat(&b.ff2.down.w, d, c.ff);
+    else if (r == "qkv") mat(&b.qkv, 3 * d, d);
+    else if (r == "rel") mat(&b.rel, 2 * c.context - 1, c.head_dim);
+    else if (r == "out") mat(&b.out.w, d, d);
+    else if (r == "pw1") mat(&b.pw1.w, 2 * cc, d);
+    else if (r == "pw2") mat(&b.pw2.w, d, cc);
+    else if (r == "ff1.norm.w") vec(&b.ff1.norm.g, d);
+    else if (r == "ff1.norm.b") vec(&b.ff1.norm.b, d);
+    else if (r == "ff1.up.b") vec(&b.ff1.up.b, c.ff);
+    else if (r == "ff1.down.b") vec(&b.ff1.down.b, d);
+    else if (r == "ff2.norm.w") vec(&b.ff2.norm.g, d);
+    else if (r == "ff2.norm.b") vec(&b.ff2.norm.b, d);
+    else if (r == "ff2.up.b") vec(&b.ff2.up.b, c.ff);
+    else if (r == "ff2.down.b") vec(&b.ff2.down.b, d);
+    else if (r == "norm_att.w") vec(&b.norm_att.g, d);
+    else if (r == "norm_att.b") vec(&b.norm_att.b, d);
+    else if (r == "out.b") vec(&b.out.b, d);
+    else if (r == "norm_conv.w") vec(&b.norm_conv.g, d);
+    else if (r == "norm_conv.b") vec(&b.norm_conv.b, d);
+    else if (r == "pw1.b") vec(&b.pw1.b, 2 * cc);
+    else if (r == "dw.w") vec(&b.dw_w, c.conv_kernel * cc);
+    else if (r == "dw.b") vec(&b.dw_b, cc);
+    else if (r == "pw2.b") vec(&b.pw2.b, d);
+    else if (r == "norm_out.w") vec(&b.norm_out.g, d);
+    else if (r == "norm_out.b") vec(&b.norm_out.b, d);
+    return e;
+}
+
+std::string Granite::missing() const {
+    auto* self = const_cast<Granite*>(this);
+    std::vector<std::string> names = {"input", "input.b", "head", "head.b", "mid", "mid.b"};
+    static const char* mats[] = {"ff1.up", "ff1.down", "ff2.up", "ff2.down", "qkv", "rel", "out", "pw1", "pw2"};
+    static const char* vecs[] = {"ff1.norm.w", "ff1.norm.b", "ff1.up.b", "ff1.down.b", "ff2.norm.w", "ff2.norm.b",
+                                 "ff2.up.b", "ff2.down.b", "norm_att.w", "norm_att.b", "out.b", "norm_conv.w",
+                                 "norm_conv.b", "pw1.b", "dw.w", "dw.b", "pw2.b", "norm_out.w", "norm_out.b"};
+    for (int i = 0; i < c.layers; ++i) {
+        for (auto m : mats) names.push_back("blocks." + std::to_string(i) + "." + m);
+        for (auto v : vecs) names.push_back("blocks." + std::to_string(i) + "." + v);
+    }
+    for (auto& n : names) {
+        Entry e = self->find(n);
+        if ((e.mat && !e.mat->values) || (e.vec && !e.vec->p)) return n;
+    }
+    return "";
+}
+
+int Granite::ensure(int rows, int tasks) {
+    if (rows <= cap_rows && tasks <= tasks_cap) return TELMO_OK;
+    cudaDeviceSynchronize();
+    const int d = c.d_model, cc = c.conv_channels;
+    const int R = rows > cap_rows ? static_cast<int>(rows * 1.1) + 64 : cap_rows;
+    const int TK = tasks > tasks_cap ? static_cast<int>(tasks * 1.1) + 64 : tasks_cap;
+    release_buffers();
+    vocab_ld = static_cast<int64_t>(round_up(c.vocab, 4));
+    big_ld = std::max(std::max<int64_t>(c.ff, 3 * d), std::max<int64_t>(2 * cc, vocab_ld));
+    const int64_t kmax = std::max(std::max<int64_t>(4 * c.n_mels, d), std::max<int64_t>(std::max(c.ff, cc), c.vocab));
+    q.ld = static_cast<int64_t>(round_up(kmax, 16));
+    auto alloc = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes) == cudaSuccess; };
+    bool ok = alloc(reinterpret_cast<void**>(&x), sizeof(float) * R * d) &&
+              alloc(reinterpret_cast<void**>(&y), sizeof(float) * R * d) &&
+              alloc(reinterpret_cast<void**>(&att), sizeof(float) * R * d) &&
+              alloc(reinterpret_cast<void**>(&big), sizeof(float) * R * big_ld) &&
+              alloc(reinterpret_cast<void**>(&conv), sizeof(float) * R * cc) &&
+              alloc(reinterpret_cast<void**>(&q.hi), static_cast<size_t>(R) * q.ld) &&
+              alloc(reinterpret_cast<void**>(&q.lo), static_cast<size_t>(R) * q.ld) &&
+              alloc(reinterpret_cast<void**>(&q.scale), sizeof(float) * R) &&
+              alloc(reinterpret_cast<void**>(&tasks_dev), sizeof(int) * 8 * static_cast<size_t>(TK));
+    if (!ok) {
+        release_buffers();
+        return ctx->fail(TELMO_ERR_CUDA, "granite: cannot allocate buffers for %d rows", rows);
+    }
+    cap_rows = R;
+    tasks_cap = TK;
+    return TELMO_OK;
+}
+
+int Granite::gemm(const QuantAct& a, int m, const Lin& l, float* out, int64_t ldc, int act, float scale, int acc,
+                  cudaStream_t s) {
+    return gemm_w(a, m, l.w, l.b.p, out, ldc, act, scale, acc, s);
+}
+
+int Granite::gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, float* out, int64_t ldc,
+                    int act, float scale, int acc, cudaStream_t s) {
+    GemmArgs g;
+    g.m = m;
+    g.a = a;
+    g.w = &w;
+    g.bias = bias;
+    g.act = act;
+    g.scale = scale;
+    g.accumulate = acc;
+    g.out = out;
+    g.ldc = ldc;
+    g.out_kind = kOutF32;
+    g.error = ctx->error_word;
+    ++launches;
+    return ctx->cuda(gemm_i8x2(g, s), "granite gemm");
+}
+
+int Granite::feed_forward(const FF& f, float* xb, int m, cudaStream_t s) {
+    // Granite::feed_forward (src/granite.rs:752-793).
+    const int d = c.d_model;
+    if (int rc = ctx->cuda(ln_chain(xb, m, d, f.norm.g.p, f.norm.b.p, nullptr, nullptr, nullptr, &q, s), "ln")) return rc;
+    ++launches;
+    if (int rc = gemm(q, m, f.up, big, big_ld, kActSilu, 1.0f, 0, s)) return rc;
+    if (int rc = ctx->cuda(quantize_x2(big, big_ld, m, c.ff, q, s), "quant")) return rc;
+    ++launches;
+    return gemm(q, m, f.down, xb, d, kActNone, 0.5f, 1, s);
+}
+
+int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap,
+                    cudaStream_t s) {
+    if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "granite: the model is not finalized");
+    if (n_utt <= 0 || !feats || !rows || !out) return ctx->fail(TELMO_ERR_ARGUMENT, "granite_encode: bad arguments");
+    const int d = c.d_model, cc = c.conv_channels, ctxn = c.context;
+    // Per-utterance frame counts at every stage.
+    std::vector<int> t(rows, rows + n_utt);
+    int64_t total = 0;
+    for (int u = 0; u < n_utt; ++u) {
+        if (t[u] < 0) return ctx->fail(TELMO_ERR_ARGUMENT, "granite_encode: negative row count");
+        int f = t[u];
+        for (int k = 0; k < c.n_subsample; ++k) f /= 2;
+        if (f == 0) {
+            char buf[160];
+            snprintf(buf, sizeof buf, "The audio is too short (%d feature rows). The model needs at least %d.", t[u],
+                     1 << c.n_subsample);
+            return fail(TELMO_ERR_MODEL, buf);
+        }
+        total += t[u];
+    }
+    if (total > (1 << 30)) return ctx->fail(TELMO_ERR_ARGUMENT, "granite_encode: too many rows");
+    const int M0 = static_cast<int>(total);
+
+    // Task lists for every block: attention blocks, convolution spans, pooling sources.
+    struct Plan { int att_off, att_n, conv_off, conv_n, pool_off, pool_n, m, m_out; };
+    std::vector<Plan> plans(c.layers);
+    std::vector<int> host;  // packed task words
+    {
+        std::vector<int> len = t;
+        for (int i = 0; i < c.layers; ++i) {
+            const bool strided = blocks[i].strided;
+            Plan& p = plans[i];
+            int off = 0, off_out = 0;
+            p.att_off = static_cast<int>(host.size());
+            for (int u = 0; u < n_utt; ++u) {
+                for (int b0 = 0; b0 < len[u]; b0 += ctxn) {
+                    host.push_back(off + b0);
+                    host.push_back(std::min(ctxn, len[u] - b0));
+                }
+                off += len[u];
+            }
+            p.m = off;
+            p.att_n = (static_cast<int>(host.size()) - p.att_off) / 2;
+            p.conv_off = static_cast<int>(host.size());
+            off = 0;
+            for (int u = 0; u < n_utt; ++u) {
+                const int n_out = strided ? len[u] / 2 : len[u];
+                for (int r = 0; r < n_out; r += 32) {
+                    host.insert(host.end(), {off, len[u], off_out, r, std::min(32, n_out - r), strided ? 2 : 1});
+                }
+                off += len[u];
+                off_out += n_out;
+            }
+            p.conv_n = (static_cast<int>(host.size()) - p.conv_off) / 6;
+            p.m_out = off_out;
+            p.pool_off = static_cast<int>(host.size());
+            p.pool_n = 0;
+            if (strided) {
+                off = 0;
+                for (int u = 0; u < n_utt; ++u) {
+                    for (int r = 0; r < len[u] / 2; ++r) host.push_back(off + 2 * r);
+                    off += len[u];
+                }
+                p.pool_n = static_cast<int>(host.size()) - p.pool_off;
+            }
+            for (int u = 0; u < n_utt; ++u)
+                if (strided) len[u] /= 2;
+            if (i == tap)
+                for (int u = 0; u < n_utt; ++u) frames_out[u] = len[u];
+        }
+        if (tap < 0 || tap >= c.layers)
+            for (int u = 0; u < n_utt; ++u) frames_out[u] = len[u];
+    }
+    const int words = static_cast<int>(host.size());
+    if (int rc = ensure(M0, (words + 7) / 8 + 1)) return rc;
+    if (int rc = ctx->cuda(cudaMemcpyAsync(tasks_dev, host.data(), sizeof(int) * words, cudaMemcpyHostToDevice, s),
+                           "granite tasks"))
+        return rc;
+    // The upload reads `host` asynchronously for pageable memory only after the copy is staged;
+    // wait so the vector may go out of scope.
+    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "granite tasks")) return rc;
+
+    // Input projection (src/granite.rs:724-733).
+    const int kin = 4 * c.n_mels;
+    if (int rc = ctx->cuda(quantize_x2(feats, kin, M0, kin, q, s), "quant")) return rc;
+    ++launches;
+    if (int rc = gemm(q, M0, input, x, d, kActNone, 1.0f, 0, s)) return rc;
+
+    const float scale = static_cast<float>(std::pow(static_cast<double>(c.head_dim), -0.5));
+    const int sc_layer = c.layers / 2 - 1;
+    float* cur = x;
+    float* other = y;
+    for (int i = 0; i < c.layers; ++i) {
+        const Block& b = blocks[i];
+        const Plan& p = plans[i];
+        const int m = p.m;
+        if (int rc = feed_forward(b.ff1, cur, m, s)) return rc;
+        // Attention (src/granite.rs:820-851).
+        if (int rc = ctx->cuda(ln_chain(cur, m, d, b.norm_att.g.p, b.norm_att.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
+            return rc;
+        ++launches;
+        if (int rc = gemm_w(q, m, b.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s)) return rc;
+        if (int rc = ctx->cuda(granite_attention(big, c.heads, c.head_dim, ctxn,
+                                                 reinterpret_cast<const AttnTask*>(tasks_dev + p.att_off), p.att_n,
+                                                 b.rel.values, b.rel.ld, b.rel.scales, scale, att, s),
+                               "attention"))
+            return rc;
+        ++launches;
+        if (int rc = ctx->cuda(quantize_x2(att, d, m, d, q, s), "quant")) return rc;
+        ++launches;
+        if (int rc = gemm(q, m, b.out, cur, d, kActNone, 1.0f, 1, s)) return rc;
+        // Convolution module (src/granite.rs:853-944).
+        if (int rc = ctx->cuda(ln_chain(cur, m, d, b.norm_conv.g.p, b.norm_conv.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
+            return rc;
+        ++launches;
+        if (int rc = gemm(q, m, b.pw1, big, 2 * cc, kActNone, 1.0f, 0, s)) return rc;
+        if (int rc = ctx->cuda(glu_dwconv_silu(big, cc, c.conv_kernel, reinterpret_cast<const ConvTask*>(tasks_dev + p.conv_off),
+                                               p.conv_n, b.dw_w.p, b.dw_b.p, conv, s),
+                               "dwconv"))
+            return rc;
+        ++launches;
+        float* target = cur;
+        if (b.strided) {
+            if (int rc = ctx->cuda(pool_pairs(cur, d, tasks_dev + p.pool_off, p.pool_n, other, s), "pool")) return rc;
+            ++launches;
+            target = other;
+        }
+        const int n = p.m_out;
+        if (int rc = ctx->cuda(quantize_x2(conv, cc, n, cc, q, s), "quant")) return rc;
+        ++launches;
+        if (int rc = gemm(q, n, b.pw2, target, d, kActNone, 1.0f, 1, s)) return rc;
+        if (int rc = feed_forward(b.ff2, target, n, s)) return rc;
+        if (int rc = ctx->cuda(ln_chain(target, n, d, b.norm_out.g.p, b.norm_out.b.p, target, nullptr, nullptr, nullptr, s),
+                               "ln"))
+            return rc;
+        ++launches;
+        if (b.strided) std::swap(cur, other);
+        if (i == sc_layer) {
+            // Self-conditioning (src/granite.rs:1040-1069): x += mid(softmax(head(x))).
+            if (int rc = ctx->cuda(quantize_x2(cur, d, n, d, q, s), "quant")) return rc;
+            ++launches;
+            if (int rc = gemm(q, n, head, big, vocab_ld, kActNone, 1.0f, 0, s)) return rc;
+            if (int rc = ctx->cuda(softmax_quant(big, n, c.vocab, vocab_ld, q, s), "softmax")) return rc;
+            ++launches;
+            if (int rc = gemm(q, n, mid, cur, d, kActNone, 1.0f, 1, s)) return rc;
+        }
+        if (i == tap) {
+            return ctx->cuda(cudaMemcpyAsync(out, cur, sizeof(float) * n * d, cudaMemcpyDeviceToDevice, s), "copy");
+        }
+    }
+    return ctx->cuda(cudaMemcpyAsync(out, cur, sizeof(float) * plans.back().m_out * d, cudaMemcpyDeviceToDevice, s),
+                     "copy");
+}
+
+int Granite::logits(const float* encoded, int frames, float* out, int64_t ld, cudaStream_t s) {
+    const int d = c.d_model;
+    if (int rc = ensure(frames, 1)) return rc;
+    if (int rc = ctx->cuda(quantize_x2(encoded, d, frames, d, q, s), "quant")) return rc;
+    ++launches;
+    return gemm(q, frames, head, out, ld, kActNone, 1.0f, 0, s);
+}
+
+int Granite::frame_ids(const float* encoded, int frames, uint32_t* ids, float* margin, cudaStream_t s) {
+    // frame_scores + argmax (src/granite.rs:690-716, :1139-1147).
+    if (frames <= 0) return TELMO_OK;
+    if (int rc = ensure(frames, 1)) return rc;
+    if (int rc = logits(encoded, frames, big, vocab_ld, s)) return rc;
+    ++launches;
+    return ctx->cuda(argmax_rows(big, frames, c.vocab, vocab_ld, ids, margin, s), "argmax");
+}
+
+}  // namespace telmo
+
+using namespace telmo;
+
+static Granite* as_granite(telmo_granite* g) { return reinterpret_cast<Granite*>(g); }
+
+extern "C" int telmo_granite_create(telmo_ctx* cp, const telmo_granite_config* config, telmo_granite** out) {
+    Ctx* ctx = as_ctx(cp);
+    if (!ctx || !config || !out) return TELMO_ERR_ARGUMENT;
+    *out = nullptr;
+    std::string why;
+    if (int rc = Granite::validate(*config, why))
+        return ctx->fail(rc, "config doesn't describe a supported Granite Speech CTC model. %s", why.c_str());
+    if (int rc = ctx->use_device()) return rc;
+    auto* g = new Granite();
+    g->ctx = ctx;
+    g->c = *config;
+    g->blocks.resize(config->layers);
+    for (int i = 0; i < config->layers; ++i)
+        for (int k = 0; k < config->n_subsample; ++k)
+            if (config->subsample_layers[k] == i) g->blocks[i].strided = true;
+    *out = reinterpret_cast<telmo_granite*>(g);
+    return TELMO_OK;
+}
+
+extern "C" void telmo_granite_free(telmo_granite* g) { delete as_granite(g); }
+
+extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int precision, size_t n, size_t k,
+                                        const void* panel_values, const float* scales) {
+    Granite* g = as_granite(gp);
+    if (!g || !name) return TELMO_ERR_ARGUMENT;
+    Granite::Entry e = g->find(name);
+    if (!e.mat) return g->ctx->fail(TELMO_ERR_MODEL, "granite: no matrix named %s", name);
+    if (static_cast<size_t>(e.n) != n || static_cast<size_t>(e.k) != k)
+        return g->ctx->fail(TELMO_ERR_MODEL, "granite: %s is [%zu, %zu], expected [%d, %d]", name, n, k, e.n, e.k);
+    if (int rc = g->ctx->use_device()) return rc;
+    free_weights(e.mat);
+    g->finalized = false;
+    return upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat);
+}
+
+extern "C" int telmo_granite_set_vector(telmo_granite* gp, const char* name, size_t len, const float* data) {
+    Granite* g = as_granite(gp);
+    if (!g || !name || !data) return TELMO_ERR_ARGUMENT;
+    Granite::Entry e = g->find(name);
+    if (!e.vec) return g->ctx->fail(TELMO_ERR_MODEL, "granite: no vector named %s", name);
+    if (static_cast<size_t>(e.len) != len)
+        return g->ctx->fail(TELMO_ERR_MODEL, "granite: %s has %zu values, expected %d", name, len, e.len);
+    if (int rc = g->ctx->use_device()) return rc;
+    if (e.vec->p) cudaFree(e.vec->p);
+    e.vec->p = nullptr;
+    if (int rc = g->ctx->cuda(cudaMalloc(&e.vec->p, sizeof(float) * len), "granite vector")) return rc;
+    g->finalized = false;
+    return g->ctx->cuda(cudaMemcpy(e.vec->p, data, sizeof(float) * len, cudaMemcpyHostToDevice), "granite vector");
+}
+
+extern "C" int telmo_granite_finalize(telmo_granite* gp) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    const std::string m = g->missing();
+    if (!m.empty()) return g->ctx->fail(TELMO_ERR_MODEL, "granite: the pack has no entry %s", m.c_str());
+    g->finalized = true;
+    return TELMO_OK;
+}
+
+extern "C" size_t telmo_granite_frames_for(const telmo_granite* gp, size_t rows) {
+    const Granite* g = reinterpret_cast<const Granite*>(gp);
+    if (!g) return 0;
+    for (int k = 0; k < g->c.n_subsample; ++k) rows /= 2;
+    return rows;
+}
+
+extern "C" int telmo_granite_encode(telmo_granite* gp, const float* features, const int* rows, int n_utt, float* out,
+                                    int* frames, int tap_layer, void* stream) {
+    Granite* g = as_granite(gp);
+    if (!g || !frames) return TELMO_ERR_ARGUMENT;
+    if (int rc = g->ctx->use_device()) return rc;
+    return g->encode(features, rows, n_utt, out, frames, tap_layer, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_granite_logits(telmo_granite* gp, const float* encoded, size_t frames, float* logits, size_t ld,
+                                    void* stream) {
+    Granite* g = as_granite(gp);
+    if (!g || !encoded || !logits) return TELMO_ERR_ARGUMENT;
+    if (ld < static_cast<size_t>(g->c.vocab)) return g->ctx->fail(TELMO_ERR_ARGUMENT, "logits: ld below vocab");
+    if (frames == 0) return TELMO_OK;
+    if (int rc = g->ctx->use_device()) return rc;
+    return g->logits(encoded, static_cast<int>(frames), logits, static_cast<int64_t>(ld),
+                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_granite_frame_ids(telmo_granite* gp, const float* encoded, size_t frames, uint32_t* ids,
+                                       float* margin, void* stream) {
+    Granite* g = as_granite(gp);
+    if (!g || !encoded || !ids) return TELMO_ERR_ARGUMENT;
+    if (int rc = g->ctx->use_device()) return rc;
+    return g->frame_ids(encoded, static_cast<int>(frames), ids, margin, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_ctc_tokens(telmo_ctx* cp, const uint32_t* ids, const int* first, const int* frames, int n_utt,
+                                uint32_t blank, uint32_t* tokens, int* counts, void* stream) {
+    Ctx* ctx = as_ctx(cp);
+    if (!ctx) return TELMO_ERR_ARGUMENT;
+    if (n_utt == 0) return TELMO_OK;
+    if (!ids || !first || !frames || !tokens || !counts || n_utt < 0)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_ctc_tokens: bad arguments");
+    if (int rc = ctx->use_device()) return rc;
+    return ctx->cuda(ctc_collapse(ids, first, frames, n_utt, blank, tokens, counts, static_cast<cudaStream_t>(stream)),
+                     "telmo_ctc_tokens");
+}

@@ -1,0 +1,398 @@
+// rowops.cu -- the memory-bound kernels of the conformer encoder: layer norm fused with the
+// split-int8 quantization of the next matrix product, softmax fused with the same, GLU +
+// depthwise convolution + SiLU, the stride-2 average pool, the CTC argmax and the CTC collapse.
+//
+// Arithmetic follows the reference's scalar kernels (src/kernels/scalar.rs): layer-norm
+// statistics in f64 and the output rounded to f32 before the affine step (:126-134), softmax
+// exponentials in f32 with an f64 sum (:136-147), GLU a / (1 + e^-b) (:149-153), the depthwise
+// sum starting from the bias and adding taps in order (:164-187). Explicit __fmul_rn/__fadd_rn
+// keep nvcc from contracting steps the reference rounds separately.
+#include "kernels.h"
+#include "rowops.h"
+
+#include <cfloat>
+
+namespace telmo {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+// The split-int8 rule (quantize_x2 in quant.cu) for one value.
+__device__ __forceinline__ void split(float x, float d, float id, float id_lo, signed char& h8,
+                                      signed char& l8) {
+    float h = roundf(__fmul_rn(x, id));
+    h = fminf(fmaxf(h, -127.0f), 127.0f);
+    const float e = __fmaf_rn(-h, d, x);
+    float l = roundf(__fmul_rn(e, id_lo));
+    l = fminf(fmaxf(l, -127.0f), 127.0f);
+    h8 = static_cast<signed char>(h);
+    l8 = static_cast<signed char>(l);
+}
+
+struct Scales {
+    float d, id, id_lo;
+};
+
+__device__ __forceinline__ Scales row_scales(float amax) {
+    Scales s;
+    s.d = __fdiv_rn(amax, 127.0f);
+    s.id = s.d != 0.0f ? __fdiv_rn(1.0f, s.d) : 0.0f;
+    s.id_lo = __fmul_rn(s.id, 254.0f);
+    return s;
+}
+
+// Layer norm of one row held as float4 chunks v[c] = elements (c * 32 + lane) * 4 .. + 3.
+template <int C>
+__device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, const float* __restrict__ gamma,
+                                                const float* __restrict__ beta, float eps, int lane) {
+    double s = 0.0;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        s += (static_cast<double>(v[c].x) + static_cast<double>(v[c].y)) +
+             (static_cast<double>(v[c].z) + static_cast<double>(v[c].w));
+    const double mean = warp_sum(s) / d;
+    double q = 0.0;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const double a = v[c].x - mean, b = v[c].y - mean, e = v[c].z - mean, f = v[c].w - mean;
+        q += (a * a + b * b) + (e * e + f * f);
+    }
+    const double var = warp_sum(q) / d;
+    const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int i = (c * 32 + lane) * 4;
+        const float4 g = *reinterpret_cast<const float4*>(gamma + i);
+        const float4 b = *reinterpret_cast<const float4*>(beta + i);
+        v[c].x = __fadd_rn(__fmul_rn(static_cast<float>((v[c].x - mean) * rstd), g.x), b.x);
+        v[c].y = __fadd_rn(__fmul_rn(static_cast<float>((v[c].y - mean) * rstd), g.y), b.y);
+        v[c].z = __fadd_rn(__fmul_rn(static_cast<float>((v[c].z - mean) * rstd), g.z), b.z);
+        v[c].w = __fadd_rn(__fmul_rn(static_cast<float>((v[c].w - mean) * rstd), g.w), b.w);
+    }
+}
+
+template <int C>
+__device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int lane, int8_t* hi, int8_t* lo,
+                                              float* scale_out) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
+    const Scales s = row_scales(warp_max(amax));
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int i = (c * 32 + lane) * 4;
+        char4 h, l;
+        split(v[c].x, s.d, s.id, s.id_lo, h.x, l.x);
+        split(v[c].y, s.d, s.id, s.id_lo, h.y, l.y);
+        split(v[c].z, s.d, s.id, s.id_lo, h.z, l.z);
+        split(v[c].w, s.d, s.id, s.id_lo, h.w, l.w);
+        *reinterpret_cast<char4*>(hi + i) = h;
+        *reinterpret_cast<char4*>(lo + i) = l;
+    }
+    if (lane == 0) *scale_out = s.d;
+}
+
+// y = LN_a(x) [written to y_out if given]; z = LN_b(y) if gamma_b given, else z = y;
+// z quantized into q if q.hi given. One warp per row of d = 128 * C values.
+template <int C>
+__global__ void ln_chain_kernel(const float* __restrict__ x, int m, int d, const float* __restrict__ ga,
+                                const float* __restrict__ ba, float* __restrict__ y_out,
+                                const float* __restrict__ gb, const float* __restrict__ bb, QuantAct q,
+                                float eps) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    const float* xr = x + static_cast<int64_t>(row) * d;
+    float4 v[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4);
+    if (ga) layer_norm_regs<C>(v, d, ga, ba, eps, lane);
+    if (y_out) {
+        float* yr = y_out + static_cast<int64_t>(row) * d;
+#pragma unroll
+        for (int c = 0; c < C; ++c) *reinterpret_cast<float4*>(yr + (c * 32 + lane) * 4) = v[c];
+    }
+    if (gb) layer_norm_regs<C>(v, d, gb, bb, eps, lane);
+    if (q.hi) quantize_regs<C>(v, lane, q.hi + static_cast<int64_t>(row) * q.ld, q.lo + static_cast<int64_t>(row) * q.ld,
+                               q.scale + row);
+}
+
+// Softmax of each row (n values, rows ld apart) in place, then its split-int8 quantization.
+// One warp per row; the exponentials are kept in the row.
+__global__ void softmax_quant_kernel(float* __restrict__ x, int m, int n, int64_t ld, QuantAct q) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    float* xr = x + row * ld;
+    float mx = -INFINITY;
+    for (int i = lane; i < n; i += 32) mx = fmaxf(mx, xr[i]);
+    mx = warp_max(mx);
+    double sum = 0.0;
+    for (int i = lane; i < n; i += 32) {
+        const float e = expf(__fsub_rn(xr[i], mx));
+        xr[i] = e;
+        sum += static_cast<double>(e);
+    }
+    sum = warp_sum(sum);
+    const float inv = static_cast<float>(1.0 / sum);
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+        const float p = __fmul_rn(xr[i], inv);
+        xr[i] = p;
+        amax = fmaxf(amax, p);
+    }
+    const Scales s = row_scales(warp_max(amax));
+    int8_t* hr = q.hi + static_cast<int64_t>(row) * q.ld;
+    int8_t* lr = q.lo + static_cast<int64_t>(row) * q.ld;
+    for (int i = lane; i < n; i += 32) {
+        signed char h, l;
+        split(xr[i], s.d, s.id, s.id_lo, h, l);
+        hr[i] = h;
+        lr[i] = l;
+    }
+    for (int i = n + lane; i < q.ld; i += 32) hr[i] = lr[i] = 0;
+    if (lane == 0) q.scale[row] = s.d;
+}
+
+__device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t row, int cc, int c) {
+    const float a = big[row * 2 * cc + c];
+    const float b = big[row * 2 * cc + cc + c];
+    return __fdiv_rn(a, __fadd_rn(1.0f, expf(-b)));
+}
+
+// GLU + depthwise convolution (taps in order from the bias, zero outside the utterance) + SiLU.
+// Task t covers output frames [out_first, out_first + count) of one utterance; threads cover
+// channels. A register window of K GLU values slides along the input frames.
+template <int K>
+__global__ void glu_dwconv_silu_kernel(const float* __restrict__ big, int cc, const ConvTask* __restrict__ tasks,
+                                       const float* __restrict__ w, const float* __restrict__ bias,
+                                       float* __restrict__ out) {
+    const ConvTask t = tasks[blockIdx.y];
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cc) return;
+    constexpr int half = K / 2;
+    float wk[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) wk[j] = __ldg(w + j * cc + c);
+    const float b = __ldg(bias + c);
+    // window[j] = GLU of local input frame (s * r + j - half) for the current output r.
+    float win[K];
+    const int r0 = t.out_first;
+    const int s = t.stride;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const int f = s * r0 + j - half;
+        win[j] = (f >= 0 && f < t.in_len) ? glu_at(big, t.in_row + f, cc, c) : 0.0f;
+    }
+    for (int r = r0; r < r0 + t.count; ++r) {
+        float acc = b;
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            const int f = s * r + j - half;
+            if (f >= 0 && f < t.in_len) acc = __fadd_rn(acc, __fmul_rn(wk[j], win[j]));
+        }
+        acc = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+        out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
+        // Slide by the stride.
+        if (s == 1) {
+#pragma unroll
+            for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+            const int f = r + 1 + K - 1 - half;
+            win[K - 1] = (f >= 0 && f < t.in_len) ? glu_at(big, t.in_row + f, cc, c) : 0.0f;
+        } else {
+#pragma unroll
+            for (int j = 0; j < K - 2; ++j) win[j] = win[j + 2];
+            const int f0 = 2 * (r + 1) + K - 2 - half, f1 = f0 + 1;
+            win[K - 2] = (f0 >= 0 && f0 < t.in_len) ? glu_at(big, t.in_row + f0, cc, c) : 0.0f;
+            win[K - 1] = (f1 >= 0 && f1 < t.in_len) ? glu_at(big, t.in_row + f1, cc, c) : 0.0f;
+        }
+    }
+}
+
+// The same without a window, for other kernel sizes.
+__global__ void glu_dwconv_silu_any_kernel(const float* __restrict__ big, int cc, int k,
+                                           const ConvTask* __restrict__ tasks, const float* __restrict__ w,
+                                           const float* __restrict__ bias, float* __restrict__ out) {
+    const ConvTask t = tasks[blockIdx.y];
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cc) return;
+    const int half = k / 2;
+    for (int r = t.out_first; r < t.out_first + t.count; ++r) {
+        float acc = __ldg(bias + c);
+        for (int j = 0; j < k; ++j) {
+            const int f = t.stride * r + j - half;
+            if (f >= 0 && f < t.in_len)
+                acc = __fadd_rn(acc, __fmul_rn(__ldg(w + j * cc + c), glu_at(big, t.in_row + f, cc, c)));
+        }
+        acc = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+        out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
+    }
+}
+
+// out[r] = (x[2r] + x[2r + 1]) / 2 over each utterance's pairs (src/granite.rs:919-930).
+__global__ void pool_pairs_kernel(const float* __restrict__ x, int d, const int* __restrict__ src_row,
+                                  int rows, float* __restrict__ out) {
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const float* a = x + static_cast<int64_t>(src_row[r]) * d;
+    const float* b = a + d;
+    float* o = out + static_cast<int64_t>(r) * d;
+    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+        const float4 p = *reinterpret_cast<const float4*>(a + i);
+        const float4 q = *reinterpret_cast<const float4*>(b + i);
+        float4 v;
+        v.x = __fdiv_rn(__fadd_rn(p.x, q.x), 2.0f);
+        v.y = __fdiv_rn(__fadd_rn(p.y, q.y), 2.0f);
+        v.z = __fdiv_rn(__fadd_rn(p.z, q.z), 2.0f);
+        v.w = __fdiv_rn(__fadd_rn(p.w, q.w), 2.0f);
+        *reinterpret_cast<float4*>(o + i) = v;
+    }
+}
+
+// The first largest value of each row and the gap to the runner-up (src/granite.rs:1139-1147).
+__global__ void argmax_kernel(const float* __restrict__ x, int m, int n, int64_t ld, uint32_t* __restrict__ ids,
+                              float* __restrict__ margin) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    const float* xr = x + row * ld;
+    float b1 = -INFINITY, b2 = -INFINITY;
+    int i1 = 0x7fffffff;
+    for (int i = lane; i < n; i += 32) {
+        const float v = xr[i];
+        if (v > b1) { b2 = b1; b1 = v; i1 = i; }
+        else if (v > b2) b2 = v;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ob1 = __shfl_xor_sync(kFull, b1, o), ob2 = __shfl_xor_sync(kFull, b2, o);
+        const int oi1 = __shfl_xor_sync(kFull, i1, o);
+        const bool other = ob1 > b1 || (ob1 == b1 && oi1 < i1);
+        const float lose = other ? b1 : ob1;
+        if (other) { b1 = ob1; i1 = oi1; }
+        b2 = fmaxf(fmaxf(b2, ob2), lose);
+    }
+    if (lane == 0) {
+        ids[row] = static_cast<uint32_t>(i1);
+        if (margin) margin[row] = __fsub_rn(b1, b2);
+    }
+}
+
+// ctc_tokens (src/granite.rs:1074-1094), one warp per utterance: a token starts where a
+// non-blank id differs from the previous frame's id; its duration is the run of equal ids.
+__global__ void ctc_collapse_kernel(const uint32_t* __restrict__ ids, const int* __restrict__ first,
+                                    const int* __restrict__ frames, int n_utt, uint32_t blank,
+                                    uint32_t* __restrict__ tokens, int* __restrict__ counts) {
+    const int u = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (u >= n_utt) return;
+    const uint32_t* id = ids + first[u];
+    uint32_t* out = tokens + 3 * static_cast<int64_t>(first[u]);
+    const int n = frames[u];
+    int count = 0;
+    for (int base = 0; base < n; base += 32) {
+        const int f = base + lane;
+        const bool valid = f < n;
+        const uint32_t v = valid ? id[f] : blank;
+        const bool start = valid && v != blank && (f == 0 || id[f - 1] != v);
+        const unsigned mask = __ballot_sync(kFull, start);
+        if (start) {
+            const int slot = count + __popc(mask & ((1u << lane) - 1));
+            int g = f + 1;
+            while (g < n && id[g] == v) ++g;
+            out[3 * slot] = v;
+            out[3 * slot + 1] = static_cast<uint32_t>(f);
+            out[3 * slot + 2] = static_cast<uint32_t>(g - f);
+        }
+        count += __popc(mask);
+    }
+    if (lane == 0) counts[u] = count;
+}
+
+}  // namespace
+
+cudaError_t ln_chain(const float* x, int m, int d, const float* ga, const float* ba, float* y_out,
+                     const float* gb, const float* bb, const QuantAct* q, cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    QuantAct qa = q ? *q : QuantAct();
+    constexpr int kWarps = 8;
+    const int grid = (m + kWarps - 1) / kWarps;
+    const float eps = 1e-5f;
+#define TELMO_LN_CASE(C)                                                                          \
+    case C:                                                                                       \
+        ln_chain_kernel<C><<<grid, kWarps * 32, 0, stream>>>(x, m, d, ga, ba, y_out, gb, bb, qa, eps); \
+        break;
+    switch (d / 128) {
+        TELMO_LN_CASE(1)
+        TELMO_LN_CASE(2)
+        TELMO_LN_CASE(4)
+        TELMO_LN_CASE(8)
+        TELMO_LN_CASE(12)
+        TELMO_LN_CASE(16)
+        default: return cudaErrorInvalidValue;
+    }
+#undef TELMO_LN_CASE
+    if (d % 128) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t softmax_quant(float* x, int m, int n, int64_t ld, const QuantAct& q, cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    constexpr int kWarps = 8;
+    softmax_quant_kernel<<<(m + kWarps - 1) / kWarps, kWarps * 32, 0, stream>>>(x, m, n, ld, q);
+    return cudaGetLastError();
+}
+
+cudaError_t glu_dwconv_silu(const float* big, int cc, int k, const ConvTask* tasks, int n_tasks, const float* w,
+                            const float* bias, float* out, cudaStream_t stream) {
+    if (n_tasks <= 0) return cudaSuccess;
+    const int threads = 128;
+    dim3 grid((cc + threads - 1) / threads, n_tasks);
+    switch (k) {
+        case 3: glu_dwconv_silu_kernel<3><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        case 5: glu_dwconv_silu_kernel<5><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        case 7: glu_dwconv_silu_kernel<7><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        case 9: glu_dwconv_silu_kernel<9><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        case 15: glu_dwconv_silu_kernel<15><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        default: glu_dwconv_silu_any_kernel<<<grid, threads, 0, stream>>>(big, cc, k, tasks, w, bias, out);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t pool_pairs(const float* x, int d, const int* src_row, int rows, float* out, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    pool_pairs_kernel<<<rows, 128, 0, stream>>>(x, d, src_row, rows, out);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_rows(const float* x, int m, int n, int64_t ld, uint32_t* ids, float* margin, cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    constexpr int kWarps = 8;
+    argmax_kernel<<<(m + kWarps - 1) / kWarps, kWarps * 32, 0, stream>>>(x, m, n, ld, ids, margin);
+    return cudaGetLastError();
+}
+
+cudaError_t ctc_collapse(const uint32_t* ids, const int* first, const int* frames, int n_utt, uint32_t blank,
+                         uint32_t* tokens, int* counts, cudaStream_t stream) {
+    if (n_utt <= 0) return cudaSuccess;
+    constexpr int kWarps = 4;
+    ctc_collapse_kernel<<<(n_utt + kWarps - 1) / kWarps, kWarps * 32, 0, stream>>>(ids, first, frames, n_utt, blank,
+                                                                                   tokens, counts);
+    return cudaGetLastError();
+}
+
+}  // namespace telmo

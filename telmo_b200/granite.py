@@ -1,0 +1,167 @@
+"""The Granite Speech CTC model on the GPU: the reference's Granite interface (src/granite.rs)
+over the C ABI.
+
+``Granite.from_entries`` plays the part of ``Granite::from_pack`` (named pack entries), and
+``encode`` / ``frame_ids`` / ``ctc_logits`` / ``ctc_tokens`` / ``transcribe`` mirror the
+reference's methods, extended to batches of utterances whose rows are packed one after another.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import TelmoError, check
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+@dataclass
+class Token:
+    """A CTC token: its id, the frame its run starts on and the run's length (src/parakeet.rs)."""
+    id: int
+    frame: int
+    duration: int
+
+
+def config_struct(config: dict) -> _lib.GraniteConfig:
+    cfg = _lib.GraniteConfig()
+    for key in ("d_model", "heads", "head_dim", "layers", "ff", "conv_kernel", "conv_channels",
+                "n_mels", "context", "max_relative", "vocab", "blank"):
+        setattr(cfg, key, int(config[key]))
+    subs = list(config["subsample_layers"])
+    if len(subs) > 8:
+        raise TelmoError(_lib.TELMO_ERR_MODEL, "too many subsample layers")
+    cfg.n_subsample = len(subs)
+    for i, s in enumerate(subs):
+        cfg.subsample_layers[i] = int(s)
+    return cfg
+
+
+class Granite:
+    """A loaded Granite Speech CTC model on one context (src/granite.rs:375-716)."""
+
+    def __init__(self, ctx, config: dict):
+        self.ctx = ctx
+        self.config = dict(config)
+        h = ctypes.c_void_p()
+        cfg = config_struct(config)
+        check(_lib.load().telmo_granite_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)),
+              ctx.handle)
+        self._h = h
+
+    @staticmethod
+    def from_entries(ctx, config: dict, entries: dict) -> "Granite":
+        """Builds the model from named pack entries: matrices as (values, scales, n, k) in the
+        panel layout, vectors as f32 arrays (Granite::from_pack, src/granite.rs:424-500)."""
+        g = Granite(ctx, config)
+        L = _lib.load()
+        for name, entry in entries.items():
+            if isinstance(entry, tuple):
+                values, scales, n, k = entry
+                values = np.ascontiguousarray(values, dtype=np.int8)
+                scales = np.ascontiguousarray(scales, dtype=np.float32)
+                rc = L.telmo_granite_set_matrix(g._h, name.encode(), 3, n, k, values.ctypes.data,
+                                                scales.ctypes.data)
+            else:
+                data = np.ascontiguousarray(entry, dtype=np.float32).reshape(-1)
+                rc = L.telmo_granite_set_vector(g._h, name.encode(), data.size, data.ctypes.data)
+            check(rc, ctx.handle)
+        check(L.telmo_granite_finalize(g._h), ctx.handle)
+        return g
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.load().telmo_granite_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def frames_for(self, rows: int) -> int:
+        """Config::frames_for (src/granite.rs:155-158)."""
+        return _lib.load().telmo_granite_frames_for(self._h, rows)
+
+    def encode(self, features, rows: Sequence[int], tap_layer: int = -1, stream=None):
+        """Granite::encode over a batch. ``features`` is a CUDA f32 tensor [sum(rows), 4 * n_mels];
+        returns (encoded CUDA tensor [sum(frames), d_model], frames per utterance)."""
+        import torch
+        rows_arr = np.ascontiguousarray(rows, dtype=np.int32)
+        n = rows_arr.size
+        total = sum(self.frames_for(int(r)) for r in rows_arr)
+        if tap_layer >= 0:
+            total = int(rows_arr.sum())
+        out = torch.empty((max(total, 1), self.config["d_model"]), dtype=torch.float32,
+                          device=features.device)
+        frames = np.zeros(n, np.int32)
+        check(_lib.load().telmo_granite_encode(self._h, features.data_ptr(), rows_arr.ctypes.data,
+                                               n, out.data_ptr(), frames.ctypes.data, tap_layer,
+                                               _stream(stream)), self.ctx.handle)
+        return out[:int(frames.sum())], frames
+
+    def ctc_logits(self, encoded, stream=None):
+        """Granite::ctc_logits (src/granite.rs:657-673): [frames, vocab]."""
+        import torch
+        frames = encoded.shape[0]
+        ld = (self.config["vocab"] + 3) // 4 * 4
+        out = torch.empty((max(frames, 1), ld), dtype=torch.float32, device=encoded.device)
+        check(_lib.load().telmo_granite_logits(self._h, encoded.data_ptr(), frames, out.data_ptr(),
+                                               ld, _stream(stream)), self.ctx.handle)
+        return out[:frames, :self.config["vocab"]]
+
+    def frame_ids(self, encoded, with_margin: bool = False, stream=None):
+        """Granite::frame_ids (src/granite.rs:677-716): each frame's first most likely token."""
+        import torch
+        frames = encoded.shape[0]
+        ids = torch.empty(max(frames, 1), dtype=torch.int32, device=encoded.device)
+        margin = torch.empty(max(frames, 1), dtype=torch.float32, device=encoded.device) \
+            if with_margin else None
+        check(_lib.load().telmo_granite_frame_ids(self._h, encoded.data_ptr(), frames,
+                                                  ids.data_ptr(),
+                                                  margin.data_ptr() if margin is not None else None,
+                                                  _stream(stream)), self.ctx.handle)
+        if with_margin:
+            return ids[:frames], margin[:frames]
+        return ids[:frames]
+
+    def ctc_tokens(self, ids, frames: Sequence[int], stream=None) -> List[List[Token]]:
+        """ctc_tokens (src/granite.rs:1074-1094) for every utterance of a batch, on the GPU."""
+        return ctc_tokens(self.ctx, ids, frames, self.config["blank"], stream)
+
+
+def ctc_tokens(ctx, ids, frames: Sequence[int], blank: int = 0, stream=None) -> List[List[Token]]:
+    import torch
+    frames_arr = np.ascontiguousarray(frames, dtype=np.int32)
+    first = np.concatenate([[0], np.cumsum(frames_arr)[:-1]]).astype(np.int32)
+    n = frames_arr.size
+    dev = ids.device
+    d_first = torch.from_numpy(first).to(dev)
+    d_frames = torch.from_numpy(frames_arr).to(dev)
+    tokens = torch.zeros((max(int(frames_arr.sum()), 1), 3), dtype=torch.int32, device=dev)
+    counts = torch.zeros(max(n, 1), dtype=torch.int32, device=dev)
+    check(_lib.load().telmo_ctc_tokens(ctx.handle, ids.data_ptr(), d_first.data_ptr(),
+                                       d_frames.data_ptr(), n, blank, tokens.data_ptr(),
+                                       counts.data_ptr(), _stream(stream)), ctx.handle)
+    tok = tokens.cpu().numpy()
+    cnt = counts.cpu().numpy()
+    out = []
+    for u in range(n):
+        t = tok[first[u]:first[u] + cnt[u]]
+        out.append([Token(int(a), int(b), int(c)) for a, b, c in t])
+    return out
