@@ -1,15 +1,21 @@
 """Benchmark of the B200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
-Workloads (seeded synthetic data, see telmo_b200/synthetic.py):
-  linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias,
-           f32 out. A step is one telmo_linear call (activation quantization + tensor-core GEMM).
+Workloads (seeded synthetic data, telmo_b200/synthetic.py):
+  granite  (default) config 5: 4096 utterances, lengths log-uniform in 1-30 s (about 34,900 s of
+           audio), through the config-2 Granite-shaped int8 CTC model: log-mel front end,
+           16-block encoder, CTC head, greedy argmax and collapse. Utterances are sharded across
+           ranks by longest-first greedy assignment (no collective; each rank keeps its tokens)
+           and processed in length-sorted batches of up to --batch-seconds of audio. A step is
+           one pass over the whole set. metric = RTFx (audio seconds / wall second), whole job.
+  linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias.
 
-`--impl reference` times the reference's CPU path for the same workload -- the oracle's C
-restatement of telmo's CPU kernels (the reference is Rust and cannot be built here), on all
-host cores -- and prints the same JSON line with "impl": "reference". Under torchrun only rank 0
-runs it.
+`--impl reference` times the reference's CPU path for the same workload: the oracle's C
+restatement of telmo's CPU path (the reference is Rust and cannot be built here) on all host
+cores, each step a bounded sample of the workload, and prints the same line with "impl":
+"reference". Under torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
@@ -29,17 +35,17 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
-FALLBACK_HBM_GBS = 6650.0
-FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SR = 16000
 
 
 def peaks():
     try:
         with open(PEAKS_FILE) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+        return {k: float(p[k]) for k in FALLBACK}, "measured (MEASURED_PEAKS.json)"
     except Exception:
-        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+        return dict(FALLBACK), "fallback (profiling recipe)"
 
 
 class Clocks:
@@ -50,9 +56,7 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
-        self.device = device
-        self.proc = None
-        self.lines = []
+        self.device, self.proc, self.lines = device, None, []
 
     def start(self):
         try:
@@ -78,7 +82,7 @@ class Clocks:
         except Exception:
             self.proc.kill()
         self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, power = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
@@ -87,198 +91,351 @@ class Clocks:
             try:
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
+                power.append(float(parts[3]))
             except ValueError:
                 continue
             for name, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
 
 
 # ---------------------------------------------------------------------------------------------
-# the config-1 linear workload
+# config 5: the Granite-shaped model over 4096 log-uniform utterances
+
+class GraniteWorkload:
+    name = "config5-granite-ctc"
+    metric = ("RTFx (audio-s per wall-s, whole job): Granite-shaped int8 CTC model, "
+              "16 kHz audio -> log-mel -> 16-block encoder -> CTC greedy tokens")
+    unit = "audio-s/s"
+    POOL = 64  # distinct 30 s base waveforms; utterance u is a slice of waveform u % 64
+
+    def __init__(self, rank, world, n_utt=4096, batch_seconds=2048.0):
+        from telmo_b200 import synthetic
+        self.synthetic = synthetic
+        self.n_utt = n_utt
+        secs = synthetic.lengths_log_uniform(n_utt, 1.0, 30.0, seed=0)
+        self.samples = np.maximum((secs * SR).astype(np.int64), 2 * 160)
+        self.total_seconds = float(self.samples.sum()) / SR
+        # Longest-first greedy assignment of utterances to ranks (cost linear in length).
+        order = np.argsort(-self.samples, kind="stable")
+        load = np.zeros(world)
+        owner = np.zeros(n_utt, np.int64)
+        for u in order:
+            r = int(np.argmin(load))
+            owner[u] = r
+            load[r] += self.samples[u]
+        mine = [int(u) for u in order if owner[u] == rank]
+        mine.sort(key=lambda u: self.samples[u])  # length buckets: similar lengths together
+        self.mine = mine
+        self.rank_seconds = float(self.samples[mine].sum()) / SR
+        self.batches = []
+        cur, acc = [], 0.0
+        for u in mine:
+            s = self.samples[u] / SR
+            if cur and acc + s > batch_seconds:
+                self.batches.append(cur)
+                cur, acc = [], 0.0
+            cur.append(u)
+            acc += s
+        if cur:
+            self.batches.append(cur)
+        self.batch_seconds = batch_seconds
+
+    def utterance(self, u, pool):
+        n = int(self.samples[u])
+        base = pool[u % self.POOL]
+        off = int(self.synthetic.rng(10_000 + u).integers(0, len(base) - n + 1))
+        return base[off:off + n]
+
+    def make_pool(self):
+        return [self.synthetic.audio(30.0, seed=1000 + i) for i in range(self.POOL)]
+
+    def config(self, world):
+        return {"workload": self.name, "utterances": self.n_utt,
+                "audio_seconds": round(self.total_seconds, 1),
+                "lengths": "log-uniform 1-30 s (seed 0)",
+                "model": "Granite-shaped: d 1024, 16 blocks, 8 heads x 128, ff 4096, conv 2048 x k15, "
+                         "context 128, vocab 2049, int8 weights (scales U(1e-3,1e-2))",
+                "global_batch": self.n_utt, "sharding": f"utterances over {world} GPU(s), "
+                                                        "longest-first greedy, no collective",
+                "per_rank_batches": len(self.batches), "batch_seconds_max": self.batch_seconds,
+                "activations": "split int8 (2 levels) x int8 weights -> i32, f32 elsewhere",
+                "l2": "inputs larger than L2 (2.2 GB of audio, ~1 GB of weights+activations "
+                      "per batch)"}
+
+    # -- GPU --------------------------------------------------------------------------------
+    def setup_gpu(self, ctx):
+        import torch
+        from telmo_b200.granite import Granite
+        cfg = self.synthetic.granite_config()
+        entries = self.synthetic.granite_entries(cfg, seed=1, scales="spec")
+        self.model = Granite.from_entries(ctx, cfg, entries)
+        del entries
+        pool = self.make_pool()
+        audio = [self.utterance(u, pool) for u in self.mine]
+        del pool
+        packed = np.concatenate(audio) if audio else np.zeros(1, np.float32)
+        self.host_audio = torch.from_numpy(packed).pin_memory()
+        self.dev_audio = self.host_audio.cuda()
+        self.offsets = []
+        at = 0
+        for b in self.batches:
+            n = int(self.samples[b].sum())
+            self.offsets.append((at, n))
+            at += n
+        frames = max((sum(self.model.frames_for_samples(int(self.samples[u])) for u in b)
+                      for b in self.batches), default=1)
+        self.dev_tokens = torch.empty(3 * frames + 3, dtype=torch.int32, device="cuda")
+        self.dev_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32,
+                                      device="cuda")
+        self.host_tokens = torch.empty(3 * frames + 3, dtype=torch.int32).pin_memory()
+        self.bi = int(packed.nbytes)
+        self.bo = 0
+
+    def step_gpu(self):
+        for b, (at, n) in zip(self.batches, self.offsets):
+            self.model.transcribe_device(self.dev_audio[at:at + n], self.samples[b],
+                                         self.dev_tokens, self.dev_counts)
+
+    def step_e2e(self):
+        bo = 0
+        for b, (at, n) in zip(self.batches, self.offsets):
+            toks = self.model.transcribe_packed(self.host_audio[at:at + n], self.samples[b],
+                                                tokens_buf=self.host_tokens)
+            bo += sum(3 * 4 * self.model.frames_for_samples(int(self.samples[u])) for u in b)
+            bo += 4 * len(b)
+        self.bo = bo
+        return toks
+
+    def units_per_step(self):
+        return self.rank_seconds
+
+    # -- CPU reference ------------------------------------------------------------------------
+    def cpu_sample_utts(self, target_s=24.0):
+        """A bounded sample of the workload for the CPU path: the first utterances of the set
+        (in input order) up to about target_s seconds."""
+        chosen, acc = [], 0.0
+        for u in range(self.n_utt):
+            s = self.samples[u] / SR
+            if acc + s > target_s and chosen:
+                break
+            chosen.append(u)
+            acc += s
+        return chosen, acc
+
+    def cpu_setup(self):
+        from oracle import oracle
+        cfg = self.synthetic.granite_config()
+        entries = self.synthetic.granite_entries(cfg, seed=1, scales="spec")
+        self.oracle = oracle
+        self.ref = oracle.Granite(cfg, entries)
+        del entries
+        pool = self.make_pool()
+        self.cpu_utts, self.cpu_seconds = self.cpu_sample_utts()
+        self.cpu_audio = [self.utterance(u, pool) for u in self.cpu_utts]
+
+    def cpu_step(self, threads):
+        for a in self.cpu_audio:
+            f = self.oracle.granite_features(a)
+            enc = self.ref.encode(f, threads=threads)
+            ids, _ = self.ref.frame_ids(enc, threads=threads)
+            self.oracle.ctc_tokens(ids)
+
+    def cpu_sample(self, threads):
+        self.cpu_setup()
+        t0 = time.perf_counter()
+        self.cpu_step(threads)
+        dt = time.perf_counter() - t0
+        return self.cpu_seconds / dt, (f"{len(self.cpu_utts)} utterances of the set "
+                                       f"({self.cpu_seconds:.1f} s of audio), features -> tokens")
+
+
+# ---------------------------------------------------------------------------------------------
+# config 1: one linear
 
 class LinearWorkload:
     name = "config1-linear"
     metric = "int8 linear TOPS (config 1: A f32 [1500,1024] x W int8 [4096,1024] + bias, f32 out)"
     unit = "TOPS"
 
-    def __init__(self):
+    def __init__(self, rank, world):
         from telmo_b200 import synthetic
         self.a, (self.values, self.scales, self.n, self.k), self.bias = synthetic.config1()
         self.m = self.a.shape[0]
         self.ops = 2.0 * self.m * self.n * self.k
 
-    def config(self):
+    def config(self, world):
         return {"workload": self.name, "m": self.m, "k": self.k, "n": self.n,
                 "activations": "split int8 (2 levels), i32 accumulate", "l2": "flushed"}
 
-    # -- GPU ------------------------------------------------------------------------------
     def setup_gpu(self, ctx):
         import torch
         from telmo_b200 import Kernels, PackedWeights, Precision
-        self.torch = torch
         self.kern = Kernels(ctx)
         self.w = PackedWeights(self.n, self.k, Precision.INT8, self.values, self.scales).upload(ctx)
         self.da = torch.from_numpy(self.a).cuda()
         self.dbias = torch.from_numpy(self.bias).cuda()
         self.dc = torch.empty((self.m, self.n), dtype=torch.float32, device="cuda")
-        ldq = (self.k + 15) // 16 * 16
-        self.ldq = ldq
-        self.hi = torch.empty((self.m, ldq), dtype=torch.int8, device="cuda")
-        self.lo = torch.empty_like(self.hi)
-        self.rs = torch.empty(self.m, dtype=torch.float32, device="cuda")
         self.ha = torch.from_numpy(self.a).pin_memory()
         self.hc = torch.empty((self.m, self.n), dtype=torch.float32).pin_memory()
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+        self.bi, self.bo = self.a.nbytes, self.m * self.n * 4
 
-    def step_gpu(self, ev=None):
-        """One step; ev = (e_before_gemm, e_after_gemm) to time the dominant kernel."""
+    def step_gpu(self):
         from telmo_b200 import Epilogue
-        self.kern.quantize_x2(self.da, self.k, self.m, self.k, self.hi, self.lo, self.ldq, self.rs)
-        if ev:
-            ev[0].record()
-        self.kern.linear_q(self.hi, self.lo, self.ldq, self.rs, self.m, self.w, self.dc, self.n,
-                           Epilogue(bias=self.dbias))
-        if ev:
-            ev[1].record()
-
-    launches_per_step = 2
+        self.kern.linear(self.da, self.m, self.w, self.dc, Epilogue(bias=self.dbias))
 
     def step_e2e(self):
-        """Through the public call with host buffers: H2D of A, telmo_linear, D2H of C."""
         from telmo_b200 import Epilogue
         self.da.copy_(self.ha, non_blocking=True)
         self.kern.linear(self.da, self.m, self.w, self.dc, Epilogue(bias=self.dbias))
         self.hc.copy_(self.dc, non_blocking=True)
 
-    def e2e_bytes(self):
-        return self.a.nbytes, self.m * self.n * 4
+    def between_steps(self):
+        self.flush.zero_()
 
     def units_per_step(self):
-        return self.ops / 1e12  # tera-ops
+        return self.ops / 1e12
 
-    def kernel_roofline(self, hbm_gbs, bf16_tflops, peak_kind):
-        # The GEMM's algorithmic HBM bytes: both int8 levels of A, W, the f32 output, scales.
-        traffic = 2 * self.m * self.k + self.n * self.k + 4 * self.m * self.n + 4 * (self.m + 2 * self.n)
-        return {"bound": "hbm", "bytes": traffic, "peak": hbm_gbs, "unit": "GB/s",
-                "peak_kind": peak_kind}
-
-    # -- CPU reference -------------------------------------------------------------------------
-    def cpu_step(self, threads, rows):
+    def cpu_step(self, threads):
         from oracle import oracle
-        oracle.linear_int8(self.a[:rows], self.values, self.scales, self.n, self.k, self.bias,
+        oracle.linear_int8(self.a, self.values, self.scales, self.n, self.k, self.bias,
                            threads=threads)
 
     def cpu_sample(self, threads):
-        """Times the reference's CPU path (oracle port) on a bounded sample: the full config-1
-        product, best of 5 (benches/matmul.rs:59-60)."""
-        rows = self.m
         best = float("inf")
-        t_end = time.time() + 20
         for _ in range(5):
             t0 = time.perf_counter()
-            self.cpu_step(threads, rows)
+            self.cpu_step(threads)
             best = min(best, time.perf_counter() - t0)
-            if time.time() > t_end:
-                break
-        ops = 2.0 * rows * self.n * self.k
-        return ops / best / 1e12, f"config-1 product ({rows}x{self.k}x{self.n}), best of 5"
+        return self.ops / best / 1e12, "config-1 product, best of 5"
 
 
-WORKLOADS = {"linear": LinearWorkload}
-
-
-def flush_l2(buf):
-    buf.zero_()
+WORKLOADS = {"granite": GraniteWorkload, "linear": LinearWorkload}
 
 
 def run_ours(args, rank, world, local_rank):
     import torch
     import telmo_b200
+    from telmo_b200 import _lib
     torch.cuda.set_device(local_rank)
     dist = None
     if world > 1:
-        import torch.distributed as dist_mod
         import datetime
-        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        import torch.distributed as dist_mod
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", local_rank))
         dist = dist_mod
     ctx = telmo_b200.Context(local_rank)
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](rank, world)
     wl.setup_gpu(ctx)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    for _ in range(args.warmup):
-        wl.step_gpu()
-        flush_l2(flush)
-    ctx.check()
+    granite = args.workload == "granite"
 
     def barrier():
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
 
+    for _ in range(args.warmup):
+        wl.step_gpu()
+        if hasattr(wl, "between_steps"):
+            wl.between_steps()
+    ctx.check()
+    if granite:
+        L = _lib.load()
+        L.telmo_granite_profile(wl.model.handle, 1)
+        L.telmo_granite_profile_read(wl.model.handle, None, None, None, None)
+        launches0 = wl.model.launches()
     clocks = Clocks(local_rank)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
     barrier()
     clocks.start()
     time.sleep(0.3)
     for i in range(args.steps):
-        flush_l2(flush)
+        if hasattr(wl, "between_steps"):
+            wl.between_steps()
         starts[i].record()
-        wl.step_gpu(kev[i])
+        wl.step_gpu()
         ends[i].record()
     barrier()
     ctx.check()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    prof = None
+    if granite:
+        import ctypes
+        ms = (ctypes.c_double * 4)()
+        cnt = (ctypes.c_long * 4)()
+        ops, byt = ctypes.c_double(), ctypes.c_double()
+        L.telmo_granite_profile_read(wl.model.handle, ms, cnt, ctypes.byref(ops),
+                                     ctypes.byref(byt))
+        L.telmo_granite_profile(wl.model.handle, 0)
+        launches = wl.model.launches() - launches0
+        prof = {"gemm_ms": ms[0], "gemm_n": cnt[0], "attn_ms": ms[1], "attn_n": cnt[1],
+                "fe_ms": ms[3], "ops": ops.value, "bytes": byt.value}
+    else:
+        launches = 2 * args.steps
     # e2e through the public call with host buffers.
     e_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
-        flush_l2(flush)
+        if hasattr(wl, "between_steps"):
+            wl.between_steps()
         e_start[i].record()
         wl.step_e2e()
         e_end[i].record()
     barrier()
     clk = clocks.stop()
     ctx.check()
-    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    kern_ms = [a.elapsed_time(b) for a, b in kev]
     e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_start, e_end))
     t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    units = torch.tensor([wl.units_per_step()], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(units, op=dist.ReduceOp.SUM)
     step_ms, e2e_ms = t.tolist()
+    total_units = units.item()
     if rank == 0:
-        hbm, bf16, kind = peaks()
-        units = wl.units_per_step() * args.steps * world
-        value = units / (step_ms / 1e3)
-        rl = wl.kernel_roofline(hbm, bf16, kind)
-        avg_kernel_s = statistics.mean(kern_ms) / 1e3
-        if rl["bound"] == "hbm":
-            achieved = rl["bytes"] / avg_kernel_s / 1e9
+        pk, pk_src = peaks()
+        value = total_units * args.steps / (step_ms / 1e3)
+        e2e_value = total_units * args.steps / (e2e_ms / 1e3)
+        if granite:
+            avg = prof["gemm_ms"] / max(prof["gemm_n"], 1) / 1e3
+            ops_launch = prof["ops"] / max(prof["gemm_n"], 1)
+            achieved = ops_launch / avg / 1e12
+            peak = pk["bf16_tflops_sustained"]
+            roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                        "kernel": "gemm_i8x2_kernel (split-int8 tcgen05 linear)",
+                        "ops_per_launch": ops_launch, "avg_launch_us": round(avg * 1e6, 2),
+                        "peak_source": pk_src + ": bf16_tflops_sustained; the split-int8 "
+                        "product issues two int8 MMAs per multiply-add, so its tensor ceiling "
+                        "is the bf16 one",
+                        "time_share": {"gemm": round(prof["gemm_ms"] / step_ms, 3),
+                                       "attention": round(prof["attn_ms"] / step_ms, 3),
+                                       "front_end": round(prof["fe_ms"] / step_ms, 3)}}
         else:
-            achieved = rl["flops"] / avg_kernel_s / 1e12
+            roofline = {"bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": None, "traffic": None, "peak_source": pk_src}
         cpu_value, cpu_sample = wl.cpu_sample(os.cpu_count() or 1)
-        bi, bo = wl.e2e_bytes()
         line = {
-            "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
+            "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(step_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32 (2 levels)",
-            "data": "synthetic (seeded, telmo_b200/synthetic.py)", "config": wl.config(),
-            "e2e": {"value": round(wl.units_per_step() * args.steps * world / (e2e_ms / 1e3), 3),
-                    "unit": wl.unit, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo},
-            "roofline": {"bound": rl["bound"], "achieved": round(achieved, 1), "peak": rl["peak"],
-                         "unit": rl["unit"], "frac": round(achieved / rl["peak"], 4),
-                         "traffic": None, "peak_source": rl["peak_kind"],
-                         "kernel_us": round(avg_kernel_s * 1e6, 2)},
-            "cpu_baseline": {"value": round(cpu_value, 4), "unit": wl.unit,
+            "ms_per_step": round(step_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong" if granite else "weak", "vs_baseline": None,
+            "dtype": "int8 x int8 -> i32 (split-int8 activations), f32/f64 elsewhere",
+            "data": "synthetic (seeded; telmo_b200/synthetic.py), random-init weights",
+            "config": wl.config(world),
+            "e2e": {"value": round(e2e_value, 2), "unit": wl.unit,
+                    "h2d_bytes_per_step": int(wl.bi), "d2h_bytes_per_step": int(wl.bo)},
+            "roofline": roofline,
+            "cpu_baseline": {"value": round(cpu_value, 3), "unit": wl.unit,
                              "cores": os.cpu_count(), "kind": "port", "sample": cpu_sample},
             "clocks": clk,
-            "gpu_launches": wl.launches_per_step * args.steps,
+            "gpu_launches": int(launches),
         }
         print(json.dumps(line), flush=True)
     if dist:
@@ -290,28 +447,36 @@ def run_ours(args, rank, world, local_rank):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
+    wl = WORKLOADS[args.workload](0, 1)
+    if hasattr(wl, "cpu_setup"):
+        wl.cpu_setup()
+        per_step = wl.cpu_seconds
+        sample = (f"the oracle's C restatement of telmo's CPU path (reference Rust not "
+                  f"buildable here): {len(wl.cpu_utts)} utterances of the set "
+                  f"({wl.cpu_seconds:.1f} s of audio) per step, features -> tokens")
+    else:
+        per_step = wl.units_per_step()
+        sample = "the oracle's C restatement, full config-1 product per step"
     for _ in range(args.warmup):
-        wl.cpu_step(threads, wl.m)
-    times = []
+        wl.cpu_step(threads)
+    total = 0.0
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        wl.cpu_step(threads, wl.m)
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = wl.units_per_step() * args.steps / total
+        wl.cpu_step(threads)
+        total += time.perf_counter() - t0
+    value = per_step * args.steps / total
     line = {
-        "impl": "reference", "metric": wl.metric, "value": round(value, 4), "unit": wl.unit,
+        "impl": "reference", "metric": wl.metric, "value": round(value, 3), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights widened)",
-        "data": "synthetic (seeded, telmo_b200/synthetic.py)", "config": wl.config(),
-        "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads,
-                         "kind": "port",
-                         "sample": "the oracle's C restatement of telmo's AVX-512 path "
-                                   "(reference Rust not buildable here), full config-1 product"},
-        "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0,
+        "ms_per_step": round(total / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "granite" else "weak", "vs_baseline": None,
+        "dtype": "f32 (int8 weights widened), f64 statistics",
+        "data": "synthetic (seeded; telmo_b200/synthetic.py), random-init weights",
+        "config": wl.config(world),
+        "cpu_baseline": {"value": round(value, 3), "unit": wl.unit, "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": wl.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -320,14 +485,14 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="linear")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="granite")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -105,6 +105,24 @@ int telmo_linear_q(telmo_ctx *ctx, const int8_t *hi, const int8_t *lo, size_t ld
                    int act, float scale, int accumulate, void *c, int c_dtype, size_t ldc,
                    void *stream);
 
+/* ---- log-mel front ends ---------------------------------------------------------------------- */
+
+#define TELMO_FRONTEND_GRANITE 0  /* GraniteFrontEnd (src/granite_features.rs): 320-wide rows */
+#define TELMO_FRONTEND_PARAKEET 1 /* FrontEnd with FrontEndConfig::parakeet (src/features.rs) */
+
+/* Rows of features for an utterance of `samples` samples at 16 kHz: Granite's rows_for
+ * (src/granite_features.rs:66-69), Parakeet's frames_for (src/features.rs:94-98); 0 when the
+ * audio is too short. */
+size_t telmo_logmel_rows(int kind, int64_t samples);
+
+/* GraniteFrontEnd::compute (src/granite_features.rs:161-186) or FrontEnd::compute
+ * (src/features.rs:101-117) for a batch: samples holds every utterance's 16 kHz samples one
+ * after another (device f32), lengths (host) their counts; features (device f32) receives every
+ * utterance's rows one after another ([rows, 320] for Granite, [rows, 128] for Parakeet), rows
+ * (host) their counts. Too-short audio is TELMO_ERR_MODEL, as in the reference. */
+int telmo_logmel(telmo_ctx *ctx, int kind, const float *samples, const int64_t *lengths, int n_utt,
+                 float *features, int *rows, void *stream);
+
 /* ---- the Granite Speech CTC encoder --------------------------------------------------------- */
 
 /* The architecture, as Granite's Config (src/granite.rs:37-164): config.json's sizes. */
@@ -152,6 +170,36 @@ int telmo_granite_logits(telmo_granite *g, const float *encoded, size_t frames, 
  * gap between the best and the second-best logit. */
 int telmo_granite_frame_ids(telmo_granite *g, const float *encoded, size_t frames, uint32_t *ids,
                             float *margin, void *stream);
+
+/* Encoder frames for an utterance of `samples` 16 kHz samples (front end rows, then
+ * frames_for). */
+size_t telmo_granite_frames_for_samples(const telmo_granite *g, int64_t samples);
+
+/* Model::transcribe / Granite::transcribe (src/model.rs:154-159, src/granite.rs:553-582) for a
+ * batch, up to the token ids (no biasing, no detokenising): front end, encoder, CTC head argmax
+ * and collapse. samples: every utterance's 16 kHz samples one after another, HOST memory
+ * (pinned memory copies fastest); lengths (host) their counts. frames (host, n_utt) receives
+ * each utterance's encoder frame count F[u]; tokens (host) receives utterance u's tokens as
+ * (id, frame, duration) triples starting at element 3 * (F[0] + ... + F[u-1]) -- size it for
+ * 3 * sum of telmo_granite_frames_for_samples(lengths[u]) -- and counts (host, n_utt) their
+ * numbers. */
+int telmo_granite_transcribe(telmo_granite *g, const float *samples, const int64_t *lengths,
+                             int n_utt, uint32_t *tokens, int *counts, int *frames, void *stream);
+/* The same with samples, tokens and counts in device memory (lengths and frames on the host). */
+int telmo_granite_transcribe_device(telmo_granite *g, const float *samples,
+                                    const int64_t *lengths, int n_utt, uint32_t *tokens,
+                                    int *counts, int *frames, void *stream);
+/* CUDA kernels this model has launched so far (front end included). */
+long telmo_granite_launches(const telmo_granite *g);
+
+/* Per-kernel timing, the reference's Timings (src/parakeet.rs:151-200) for the GPU: while
+ * enabled, every matrix product, attention launch and front-end pass is bracketed by CUDA events
+ * on its stream. telmo_granite_profile_read waits for them and returns, per class (0 matrix
+ * products, 1 attention, 2 row kernels, 3 front end), the summed milliseconds and launch counts,
+ * and the matrix products' algorithmic operations (2 m n k) and bytes; then it starts over. */
+int telmo_granite_profile(telmo_granite *g, int enable);
+int telmo_granite_profile_read(telmo_granite *g, double *ms, long *launches, double *gemm_ops,
+                               double *gemm_bytes);
 
 /* ctc_tokens (src/granite.rs:1074-1094) on the device for n_utt utterances: utterance u's ids
  * are ids[first[u] .. first[u] + frames[u]) (first, frames: device int arrays); its tokens go to

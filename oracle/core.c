@@ -165,69 +165,106 @@ static void tile_generic(size_t kc, const float *a, size_t lda, size_t rows, con
 }
 
 #if defined(__x86_64__)
+/* R x 16 register tiles, the AVX-512 shape (8 rows, src/kernels/avx512.rs:15, :43-106) and the
+ * AVX2 shape (6 rows, src/kernels/mod.rs:31), one function per row count so the accumulators
+ * stay in registers; every row sums in the same fused order as tile_generic. */
+#define TELMO_TILE512(R)                                                                        \
+    __attribute__((target("avx512f,fma"))) static void tile512_##R(                             \
+        size_t kc, const float *a, size_t lda, const float *b, size_t k_stride, float *out,     \
+        int load)                                                                               \
+    {                                                                                           \
+        __m512 c[R];                                                                            \
+        for (int r = 0; r < R; r++)                                                             \
+            c[r] = load ? _mm512_loadu_ps(out + r * PANEL) : _mm512_setzero_ps();               \
+        for (size_t i = 0; i < kc; i++) {                                                       \
+            __m512 bv = _mm512_loadu_ps(b + i * k_stride);                                      \
+            for (int r = 0; r < R; r++)                                                         \
+                c[r] = _mm512_fmadd_ps(_mm512_set1_ps(a[r * lda + i]), bv, c[r]);               \
+        }                                                                                       \
+        for (int r = 0; r < R; r++) _mm512_storeu_ps(out + r * PANEL, c[r]);                    \
+    }
+TELMO_TILE512(1) TELMO_TILE512(2) TELMO_TILE512(3) TELMO_TILE512(4)
+TELMO_TILE512(5) TELMO_TILE512(6) TELMO_TILE512(7) TELMO_TILE512(8)
+
 __attribute__((target("avx512f,fma"))) static void
 tile_avx512(size_t kc, const float *a, size_t lda, size_t rows, const float *b, size_t k_stride,
             float *out, int load)
 {
-    /* 8 x 16 register tile, the AVX-512 shape (src/kernels/avx512.rs:15, :43-106). */
-    if (rows != 8) {
-        tile_generic(kc, a, lda, rows, b, k_stride, out, load);
-        return;
+    switch (rows) {
+    case 1: tile512_1(kc, a, lda, b, k_stride, out, load); break;
+    case 2: tile512_2(kc, a, lda, b, k_stride, out, load); break;
+    case 3: tile512_3(kc, a, lda, b, k_stride, out, load); break;
+    case 4: tile512_4(kc, a, lda, b, k_stride, out, load); break;
+    case 5: tile512_5(kc, a, lda, b, k_stride, out, load); break;
+    case 6: tile512_6(kc, a, lda, b, k_stride, out, load); break;
+    case 7: tile512_7(kc, a, lda, b, k_stride, out, load); break;
+    default: tile512_8(kc, a, lda, b, k_stride, out, load); break;
     }
-    __m512 c0, c1, c2, c3, c4, c5, c6, c7;
-    if (load) {
-        c0 = _mm512_loadu_ps(out + 0 * PANEL); c1 = _mm512_loadu_ps(out + 1 * PANEL);
-        c2 = _mm512_loadu_ps(out + 2 * PANEL); c3 = _mm512_loadu_ps(out + 3 * PANEL);
-        c4 = _mm512_loadu_ps(out + 4 * PANEL); c5 = _mm512_loadu_ps(out + 5 * PANEL);
-        c6 = _mm512_loadu_ps(out + 6 * PANEL); c7 = _mm512_loadu_ps(out + 7 * PANEL);
-    } else {
-        c0 = c1 = c2 = c3 = c4 = c5 = c6 = c7 = _mm512_setzero_ps();
-    }
-    for (size_t i = 0; i < kc; i++) {
-        __m512 bv = _mm512_loadu_ps(b + i * k_stride);
-        c0 = _mm512_fmadd_ps(_mm512_set1_ps(a[0 * lda + i]), bv, c0);
-        c1 = _mm512_fmadd_ps(_mm512_set1_ps(a[1 * lda + i]), bv, c1);
-        c2 = _mm512_fmadd_ps(_mm512_set1_ps(a[2 * lda + i]), bv, c2);
-        c3 = _mm512_fmadd_ps(_mm512_set1_ps(a[3 * lda + i]), bv, c3);
-        c4 = _mm512_fmadd_ps(_mm512_set1_ps(a[4 * lda + i]), bv, c4);
-        c5 = _mm512_fmadd_ps(_mm512_set1_ps(a[5 * lda + i]), bv, c5);
-        c6 = _mm512_fmadd_ps(_mm512_set1_ps(a[6 * lda + i]), bv, c6);
-        c7 = _mm512_fmadd_ps(_mm512_set1_ps(a[7 * lda + i]), bv, c7);
-    }
-    _mm512_storeu_ps(out + 0 * PANEL, c0); _mm512_storeu_ps(out + 1 * PANEL, c1);
-    _mm512_storeu_ps(out + 2 * PANEL, c2); _mm512_storeu_ps(out + 3 * PANEL, c3);
-    _mm512_storeu_ps(out + 4 * PANEL, c4); _mm512_storeu_ps(out + 5 * PANEL, c5);
-    _mm512_storeu_ps(out + 6 * PANEL, c6); _mm512_storeu_ps(out + 7 * PANEL, c7);
 }
+
+#define TELMO_TILE256(R)                                                                        \
+    __attribute__((target("avx2,fma"))) static void tile256_##R(                                \
+        size_t kc, const float *a, size_t lda, const float *b, size_t k_stride, float *out,     \
+        int load)                                                                               \
+    {                                                                                           \
+        __m256 c[2 * R];                                                                        \
+        for (int r = 0; r < R; r++) {                                                           \
+            c[2 * r] = load ? _mm256_loadu_ps(out + r * PANEL) : _mm256_setzero_ps();           \
+            c[2 * r + 1] = load ? _mm256_loadu_ps(out + r * PANEL + 8) : _mm256_setzero_ps();   \
+        }                                                                                       \
+        for (size_t i = 0; i < kc; i++) {                                                       \
+            __m256 b0 = _mm256_loadu_ps(b + i * k_stride);                                      \
+            __m256 b1 = _mm256_loadu_ps(b + i * k_stride + 8);                                  \
+            for (int r = 0; r < R; r++) {                                                       \
+                __m256 av = _mm256_set1_ps(a[r * lda + i]);                                     \
+                c[2 * r] = _mm256_fmadd_ps(av, b0, c[2 * r]);                                   \
+                c[2 * r + 1] = _mm256_fmadd_ps(av, b1, c[2 * r + 1]);                           \
+            }                                                                                   \
+        }                                                                                       \
+        for (int r = 0; r < R; r++) {                                                           \
+            _mm256_storeu_ps(out + r * PANEL, c[2 * r]);                                        \
+            _mm256_storeu_ps(out + r * PANEL + 8, c[2 * r + 1]);                                \
+        }                                                                                       \
+    }
+TELMO_TILE256(1) TELMO_TILE256(2) TELMO_TILE256(3) TELMO_TILE256(4) TELMO_TILE256(5)
+TELMO_TILE256(6)
 
 __attribute__((target("avx2,fma"))) static void
 tile_avx2(size_t kc, const float *a, size_t lda, size_t rows, const float *b, size_t k_stride,
           float *out, int load)
 {
-    /* 6 x 16 register tile, the AVX2 shape (src/kernels/mod.rs:31, avx2.rs). */
-    if (rows != 6) {
-        tile_generic(kc, a, lda, rows, b, k_stride, out, load);
-        return;
+    switch (rows) {
+    case 1: tile256_1(kc, a, lda, b, k_stride, out, load); break;
+    case 2: tile256_2(kc, a, lda, b, k_stride, out, load); break;
+    case 3: tile256_3(kc, a, lda, b, k_stride, out, load); break;
+    case 4: tile256_4(kc, a, lda, b, k_stride, out, load); break;
+    case 5: tile256_5(kc, a, lda, b, k_stride, out, load); break;
+    default: tile256_6(kc, a, lda, b, k_stride, out, load); break;
     }
-    __m256 c[12];
-    for (int r = 0; r < 6; r++) {
-        c[2 * r] = load ? _mm256_loadu_ps(out + r * PANEL) : _mm256_setzero_ps();
-        c[2 * r + 1] = load ? _mm256_loadu_ps(out + r * PANEL + 8) : _mm256_setzero_ps();
-    }
+}
+
+/* widen (src/kernels/avx512.rs:221): 16 int8 values to f32, times the panel's scales. */
+__attribute__((target("avx512f"))) static void
+widen_avx512(size_t kc, const int8_t *src, const float *scales, float *out)
+{
+    __m512 s = _mm512_loadu_ps(scales);
     for (size_t i = 0; i < kc; i++) {
-        __m256 b0 = _mm256_loadu_ps(b + i * k_stride), b1 = _mm256_loadu_ps(b + i * k_stride + 8);
-        for (int r = 0; r < 6; r++) {
-            __m256 av = _mm256_set1_ps(a[r * lda + i]);
-            c[2 * r] = _mm256_fmadd_ps(av, b0, c[2 * r]);
-            c[2 * r + 1] = _mm256_fmadd_ps(av, b1, c[2 * r + 1]);
-        }
-    }
-    for (int r = 0; r < 6; r++) {
-        _mm256_storeu_ps(out + r * PANEL, c[2 * r]);
-        _mm256_storeu_ps(out + r * PANEL + 8, c[2 * r + 1]);
+        __m128i q = _mm_loadu_si128((const __m128i *)(src + i * PANEL));
+        __m512 v = _mm512_cvtepi32_ps(_mm512_cvtepi8_epi32(q));
+        _mm512_storeu_ps(out + i * PANEL, _mm512_mul_ps(v, s));
     }
 }
 #endif
+
+static int have_avx512(void)
+{
+#if defined(__x86_64__)
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("fma");
+#else
+    return 0;
+#endif
+}
 
 typedef void (*tile_fn)(size_t, const float *, size_t, size_t, const float *, size_t, float *, int);
 
@@ -269,6 +306,8 @@ static void gemm_panels(const gemm_job *J, size_t p0, size_t p1)
 {
     size_t tile_rows;
     tile_fn tile = pick_tile(&tile_rows);
+    const int avx512 = have_avx512();
+    (void)avx512;
     size_t k = J->k;
     float *wide = (float *)malloc(KC * PANEL * sizeof(float));
     float *partial = (float *)malloc((J->m ? J->m : 1) * PANEL * sizeof(float));
@@ -283,9 +322,14 @@ static void gemm_panels(const gemm_job *J, size_t p0, size_t p1)
                 /* widen (src/kernels/scalar.rs:82-90): q as f32 * scale. */
                 const int8_t *src = J->values + (p * k + k0) * PANEL;
                 const float *s = J->scales + p * PANEL;
-                for (size_t i = 0; i < kc; i++)
-                    for (int j = 0; j < PANEL; j++)
-                        wide[i * PANEL + j] = (float)src[i * PANEL + j] * s[j];
+#if defined(__x86_64__)
+                if (avx512)
+                    widen_avx512(kc, src, s, wide);
+                else
+#endif
+                    for (size_t i = 0; i < kc; i++)
+                        for (int j = 0; j < PANEL; j++)
+                            wide[i * PANEL + j] = (float)src[i * PANEL + j] * s[j];
                 bp = wide;
                 k_stride = PANEL;
             } else {

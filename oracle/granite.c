@@ -227,11 +227,76 @@ static void linear(const float *a, size_t m, const lin *l, float *c, int act, fl
                        scale, accumulate, threads);
 }
 
+/* Row-wise work split into chunks of rows across threads, as for_rows does
+ * (src/kernels/mod.rs:770-789); rows are independent, so results do not depend on threads. */
+typedef struct {
+    void (*row)(void *ctx, size_t r);
+    void *ctx;
+    size_t rows, chunk;
+} rows_job;
+
+static void rows_task(void *p, size_t t)
+{
+    const rows_job *J = (const rows_job *)p;
+    size_t end = (t + 1) * J->chunk < J->rows ? (t + 1) * J->chunk : J->rows;
+    for (size_t r = t * J->chunk; r < end; r++) J->row(J->ctx, r);
+}
+
+static void for_rows(size_t rows, size_t chunk, int threads, void (*row)(void *, size_t),
+                     void *ctx)
+{
+    rows_job J = {row, ctx, rows, chunk};
+    oracle_parallel_for((rows + chunk - 1) / chunk, threads, rows_task, &J);
+}
+
+typedef struct {
+    const norm *nm;
+    const float *x;
+    float *out;
+    size_t d;
+} ln_ctx;
+
+static void ln_row(void *p, size_t r)
+{
+    const ln_ctx *C = (const ln_ctx *)p;
+    oracle_layer_norm(C->x + r * C->d, C->out + r * C->d, C->nm->g.p, C->nm->b.p, C->d, 1e-5f);
+}
+
+static int g_threads = 1; /* row-kernel threads of the current encode call */
+
 static void layer_norm_rows(const norm *nm, const float *x, float *out, size_t t, size_t d)
 {
     /* Granite::norm (src/granite.rs:735-749), eps 1e-5. */
-    for (size_t r = 0; r < t; r++)
-        oracle_layer_norm(x + r * d, out + r * d, nm->g.p, nm->b.p, d, 1e-5f);
+    ln_ctx C = {nm, x, out, d};
+    for_rows(t, 16, g_threads, ln_row, &C);
+}
+
+typedef struct {
+    const float *big;
+    float *glu, *dst;
+    size_t cc, m, stride, kernel;
+    const float *w, *bias;
+    size_t vocab;
+} conv_ctx;
+
+static void glu_row(void *p, size_t r)
+{
+    const conv_ctx *C = (const conv_ctx *)p;
+    oracle_glu(C->big + r * 2 * C->cc, C->big + r * 2 * C->cc + C->cc, C->glu + r * C->cc, C->cc);
+}
+
+static void dwconv_row(void *p, size_t r)
+{
+    const conv_ctx *C = (const conv_ctx *)p;
+    oracle_dwconv1d_frame(C->glu, C->cc, C->m, C->stride * r, C->w, C->kernel, C->bias,
+                          C->dst + r * C->cc);
+    oracle_silu(C->dst + r * C->cc, C->cc);
+}
+
+static void softmax_row(void *p, size_t r)
+{
+    const conv_ctx *C = (const conv_ctx *)p;
+    oracle_softmax(C->dst + r * C->vocab, C->vocab);
 }
 
 typedef struct {
@@ -310,13 +375,11 @@ static void block_span(const oracle_granite *g, const block *b, float *x, size_t
     size_t m = t, stride = b->strided ? 2 : 1, n = b->strided ? t / 2 : t;
     layer_norm_rows(&b->norm_conv, x, s->h, m, d);
     linear(s->h, m, &b->pw1, s->big, ORACLE_ACT_NONE, 1.0f, 0, threads);
-    for (size_t r = 0; r < m; r++)
-        oracle_glu(s->big + r * 2 * cc, s->big + r * 2 * cc + cc, s->glu + r * cc, cc);
-    for (size_t r = 0; r < n; r++) {
-        oracle_dwconv1d_frame(s->glu, cc, m, stride * r, b->dw_w.p, (size_t)c->conv_kernel,
-                              b->dw_b.p, s->big + r * cc);
-        oracle_silu(s->big + r * cc, cc);
-    }
+    conv_ctx C = {s->big, s->glu, s->big, cc, m, stride, (size_t)c->conv_kernel, b->dw_w.p,
+                  b->dw_b.p, 0};
+    for_rows(m, 16, threads, glu_row, &C);
+    /* Every output row reads only glu, and rows below n of big are free after the GLU. */
+    for_rows(n, 8, threads, dwconv_row, &C);
     for (size_t r = 0; r < n; r++) {
         float *row = out + r * d;
         if (b->strided) {
@@ -338,7 +401,8 @@ static void self_conditioning(const oracle_granite *g, const float *x, size_t t,
     size_t vocab = (size_t)g->c.vocab;
     float *logits = (float *)malloc((t ? t : 1) * vocab * sizeof(float));
     linear(x, t, &g->head, logits, ORACLE_ACT_NONE, 1.0f, 0, threads);
-    for (size_t r = 0; r < t; r++) oracle_softmax(logits + r * vocab, vocab);
+    conv_ctx C = {NULL, NULL, logits, 0, 0, 0, 0, NULL, NULL, vocab};
+    for_rows(t, 4, threads, softmax_row, &C);
     linear(logits, t, &g->mid, inj, ORACLE_ACT_NONE, 1.0f, 0, threads);
     free(logits);
 }
@@ -350,6 +414,7 @@ long oracle_granite_encode(const oracle_granite *g, const float *features, size_
     const oracle_granite_config *c = &g->c;
     if (oracle_granite_missing(g, NULL, 0)) return -1;
     if (oracle_granite_frames_for(g, rows) == 0) return -1;
+    g_threads = threads < 1 ? 1 : threads;
     size_t d = (size_t)c->d_model, cc = (size_t)c->conv_channels;
     size_t widest = (size_t)c->ff;
     if (3 * d > widest) widest = 3 * d;

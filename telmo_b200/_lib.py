@@ -50,7 +50,18 @@ SIGNATURES = {
     "telmo_granite_logits": (_int, [_vp, _vp, _sz, _vp, _sz, _vp]),
     "telmo_granite_frame_ids": (_int, [_vp, _vp, _sz, _vp, _vp, _vp]),
     "telmo_ctc_tokens": (_int, [_vp, _vp, _vp, _vp, _int, _c.c_uint32, _vp, _vp, _vp]),
+    "telmo_logmel_rows": (_sz, [_int, _c.c_int64]),
+    "telmo_logmel": (_int, [_vp, _int, _vp, _vp, _int, _vp, _vp, _vp]),
+    "telmo_granite_frames_for_samples": (_sz, [_vp, _c.c_int64]),
+    "telmo_granite_transcribe": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_granite_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_granite_launches": (_c.c_long, [_vp]),
+    "telmo_granite_profile": (_int, [_vp, _int]),
+    "telmo_granite_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),
 }
+
+FRONTEND_GRANITE = 0
+FRONTEND_PARAKEET = 1
 
 
 class GraniteConfig(ctypes.Structure):

@@ -1,6 +1,7 @@
 // api.cu -- the C ABI of libtelmo_b200: contexts, weights and the matrix product.
 #include "../../include/telmo_b200.h"
 #include "api_internal.h"
+#include "frontend.h"
 #include "kernels.h"
 
 #include <cmath>
@@ -95,6 +96,8 @@ extern "C" void telmo_ctx_destroy(telmo_ctx* c) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
+    delete ctx->granite_fe;
+    delete ctx->parakeet_fe;
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->error_word) cudaFree(ctx->error_word);
     delete ctx;

@@ -10,7 +10,11 @@ struct telmo_ctx;
 
 namespace telmo {
 
+struct FrontEnd;
+
 struct Ctx {
+    FrontEnd* granite_fe = nullptr;   // created on first use
+    FrontEnd* parakeet_fe = nullptr;
     int device = 0;
     int sms = 148;
     uint32_t* error_word = nullptr;  // device error word the kernels record into

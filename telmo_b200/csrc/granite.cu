@@ -7,6 +7,7 @@
 // edges) and the stride-2 pooling see utterance boundaries, through task lists built here.
 #include "../../include/telmo_b200.h"
 #include "api_internal.h"
+#include "frontend.h"
 #include "granite_internal.h"
 #include "kernels.h"
 #include "rowops.h"
@@ -43,6 +44,84 @@ Granite::~Granite() {
         free_vec(b.dw_w); free_vec(b.dw_b);
     }
     release_buffers();
+    release_e2e();
+    if (audio_dev) cudaFree(audio_dev);
+}
+
+void Granite::release_e2e() {
+    for (void* p : {static_cast<void*>(feats_dev), static_cast<void*>(enc_dev), static_cast<void*>(ids_dev),
+                    static_cast<void*>(tokens_dev), static_cast<void*>(counts_dev), static_cast<void*>(first_dev)})
+        if (p) cudaFree(p);
+    feats_dev = enc_dev = nullptr;
+    ids_dev = tokens_dev = nullptr;
+    counts_dev = first_dev = nullptr;
+    e2e_rows_cap = e2e_frames_cap = e2e_utt_cap = 0;
+}
+
+int Granite::ensure_e2e(int rows, int frames, int n_utt) {
+    if (rows <= e2e_rows_cap && frames <= e2e_frames_cap && n_utt <= e2e_utt_cap) return TELMO_OK;
+    cudaDeviceSynchronize();
+    const int R = std::max(rows, e2e_rows_cap), F = std::max(frames, e2e_frames_cap), U = std::max(n_utt, e2e_utt_cap);
+    release_e2e();
+    auto alloc = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes) == cudaSuccess; };
+    const bool ok = alloc(reinterpret_cast<void**>(&feats_dev), sizeof(float) * R * 4 * c.n_mels) &&
+                    alloc(reinterpret_cast<void**>(&enc_dev), sizeof(float) * static_cast<size_t>(F) * c.d_model) &&
+                    alloc(reinterpret_cast<void**>(&ids_dev), sizeof(uint32_t) * F) &&
+                    alloc(reinterpret_cast<void**>(&tokens_dev), sizeof(uint32_t) * 3 * F) &&
+                    alloc(reinterpret_cast<void**>(&counts_dev), sizeof(int) * U) &&
+                    alloc(reinterpret_cast<void**>(&first_dev), sizeof(int) * 2 * U);
+    if (!ok) {
+        release_e2e();
+        return ctx->fail(TELMO_ERR_CUDA, "granite: cannot allocate end-to-end buffers");
+    }
+    e2e_rows_cap = R;
+    e2e_frames_cap = F;
+    e2e_utt_cap = U;
+    return TELMO_OK;
+}
+
+int Granite::transcribe_device(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
+                               int* frames_out, cudaStream_t s) {
+    // Granite::transcribe (src/granite.rs:553-582) without biasing or detokenising: features,
+    // encoder, CTC head argmax, collapse.
+    if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "granite: the model is not finalized");
+    if (n_utt <= 0 || !samples || !lengths || !tokens || !counts || !frames_out)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "granite transcribe: bad arguments");
+    std::vector<int> rows(n_utt);
+    int64_t total_rows = 0, total_frames = 0;
+    for (int u = 0; u < n_utt; ++u) {
+        const size_t r = telmo_logmel_rows(TELMO_FRONTEND_GRANITE, lengths[u]);
+        rows[u] = static_cast<int>(r);
+        total_rows += static_cast<int64_t>(r);
+        size_t f = r;
+        for (int k = 0; k < c.n_subsample; ++k) f /= 2;
+        total_frames += static_cast<int64_t>(f);
+    }
+    if (total_rows > (1 << 30)) return ctx->fail(TELMO_ERR_ARGUMENT, "granite transcribe: batch too large");
+    if (int rc = ensure_e2e(static_cast<int>(total_rows) + 1, static_cast<int>(total_frames) + 1, n_utt)) return rc;
+    if (prof.on) prof.begin(kProfFrontEnd, s);
+    if (int rc = telmo_logmel(reinterpret_cast<telmo_ctx*>(ctx), TELMO_FRONTEND_GRANITE, samples, lengths, n_utt,
+                              feats_dev, rows.data(), s))
+        return rc;
+    if (prof.on) prof.end(kProfFrontEnd, s);
+    if (int rc = encode(feats_dev, rows.data(), n_utt, enc_dev, frames_out, -1, s)) return rc;
+    if (int rc = frame_ids(enc_dev, static_cast<int>(total_frames), ids_dev, nullptr, s)) return rc;
+    std::vector<int> first(2 * static_cast<size_t>(n_utt));
+    int at = 0;
+    for (int u = 0; u < n_utt; ++u) {
+        first[u] = at;
+        first[n_utt + u] = frames_out[u];
+        at += frames_out[u];
+    }
+    if (int rc = ctx->cuda(cudaMemcpyAsync(first_dev, first.data(), sizeof(int) * first.size(), cudaMemcpyHostToDevice, s),
+                           "transcribe"))
+        return rc;
+    ++launches;
+    if (int rc = ctx->cuda(ctc_collapse(ids_dev, first_dev, first_dev + n_utt, n_utt, static_cast<uint32_t>(c.blank),
+                                        tokens, counts, s),
+                           "ctc"))
+        return rc;
+    return ctx->cuda(cudaStreamSynchronize(s), "transcribe");
 }
 
 void Granite::release_buffers() {
@@ -201,7 +280,71 @@ int Granite::gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* 
     g.out_kind = kOutF32;
     g.error = ctx->error_word;
     ++launches;
-    return ctx->cuda(gemm_i8x2(g, s), "granite gemm");
+    if (prof.on) {
+        // Algorithmic work of this product: 2 m n k operations; bytes: both int8 levels of A,
+        // the int8 weights, the f32 output (read too when accumulating), scales and bias.
+        prof.gemm_ops += 2.0 * m * w.n * static_cast<double>(w.k);
+        prof.gemm_bytes += 2.0 * m * w.k + static_cast<double>(w.n) * w.k + (acc ? 8.0 : 4.0) * m * w.n +
+                           4.0 * m + 8.0 * w.n;
+        prof.begin(kProfGemm, s);
+    }
+    const int rc = ctx->cuda(gemm_i8x2(g, s), "granite gemm");
+    if (prof.on) prof.end(kProfGemm, s);
+    return rc;
+}
+
+cudaEvent_t Profiler::take() {
+    if (pool.empty()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        return e;
+    }
+    cudaEvent_t e = pool.back();
+    pool.pop_back();
+    return e;
+}
+
+void Profiler::begin(int kind, cudaStream_t s) {
+    cudaEvent_t e = take();
+    cudaEventRecord(e, s);
+    start[kind].push_back(e);
+}
+
+void Profiler::end(int kind, cudaStream_t s) {
+    cudaEvent_t e = take();
+    cudaEventRecord(e, s);
+    stop[kind].push_back(e);
+    ++count[kind];
+}
+
+void Profiler::read(double* ms, long* launches, double* ops, double* bytes) {
+    for (int k = 0; k < kProfKinds; ++k) {
+        double total = 0.0;
+        for (size_t i = 0; i < start[k].size() && i < stop[k].size(); ++i) {
+            cudaEventSynchronize(stop[k][i]);
+            float t = 0.0f;
+            cudaEventElapsedTime(&t, start[k][i], stop[k][i]);
+            total += t;
+        }
+        if (ms) ms[k] = total;
+        if (launches) launches[k] = count[k];
+        for (auto e : start[k]) pool.push_back(e);
+        for (auto e : stop[k]) pool.push_back(e);
+        start[k].clear();
+        stop[k].clear();
+        count[k] = 0;
+    }
+    if (ops) *ops = gemm_ops;
+    if (bytes) *bytes = gemm_bytes;
+    gemm_ops = gemm_bytes = 0.0;
+}
+
+Profiler::~Profiler() {
+    for (int k = 0; k < kProfKinds; ++k) {
+        for (auto e : start[k]) cudaEventDestroy(e);
+        for (auto e : stop[k]) cudaEventDestroy(e);
+    }
+    for (auto e : pool) cudaEventDestroy(e);
 }
 
 int Granite::feed_forward(const FF& f, float* xb, int m, cudaStream_t s) {
@@ -317,11 +460,13 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
             return rc;
         ++launches;
         if (int rc = gemm_w(q, m, b.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s)) return rc;
+        if (prof.on) prof.begin(kProfAttention, s);
         if (int rc = ctx->cuda(granite_attention(big, c.heads, c.head_dim, ctxn,
                                                  reinterpret_cast<const AttnTask*>(tasks_dev + p.att_off), p.att_n,
                                                  b.rel.values, b.rel.ld, b.rel.scales, scale, att, s),
                                "attention"))
             return rc;
+        if (prof.on) prof.end(kProfAttention, s);
         ++launches;
         if (int rc = ctx->cuda(quantize_x2(att, d, m, d, q, s), "quant")) return rc;
         ++launches;
@@ -483,6 +628,89 @@ extern "C" int telmo_granite_frame_ids(telmo_granite* gp, const float* encoded, 
     if (!g || !encoded || !ids) return TELMO_ERR_ARGUMENT;
     if (int rc = g->ctx->use_device()) return rc;
     return g->frame_ids(encoded, static_cast<int>(frames), ids, margin, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t telmo_granite_frames_for_samples(const telmo_granite* g, int64_t samples) {
+    return telmo_granite_frames_for(g, telmo_logmel_rows(TELMO_FRONTEND_GRANITE, samples));
+}
+
+extern "C" int telmo_granite_transcribe_device(telmo_granite* gp, const float* samples, const int64_t* lengths,
+                                               int n_utt, uint32_t* tokens, int* counts, int* frames, void* stream) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    if (int rc = g->ctx->use_device()) return rc;
+    return g->transcribe_device(samples, lengths, n_utt, tokens, counts, frames, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_granite_transcribe(telmo_granite* gp, const float* samples, const int64_t* lengths, int n_utt,
+                                        uint32_t* tokens, int* counts, int* frames, void* stream) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    if (n_utt <= 0 || !samples || !lengths || !tokens || !counts || !frames)
+        return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: bad arguments");
+    if (int rc = g->ctx->use_device()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int64_t total = 0;
+    for (int u = 0; u < n_utt; ++u) {
+        if (lengths[u] < 0) return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: negative length");
+        total += lengths[u];
+    }
+    if (static_cast<size_t>(total) > g->audio_cap) {
+        cudaStreamSynchronize(s);
+        if (g->audio_dev) cudaFree(g->audio_dev);
+        g->audio_dev = nullptr;
+        g->audio_cap = 0;
+        if (int rc = g->ctx->cuda(cudaMalloc(&g->audio_dev, sizeof(float) * (total + total / 8 + 1)), "transcribe"))
+            return rc;
+        g->audio_cap = static_cast<size_t>(total + total / 8 + 1);
+    }
+    // The device token buffers must exist before transcribe_device checks its arguments.
+    int64_t rows_total = 0, frames_total_est = 0;
+    for (int u = 0; u < n_utt; ++u) {
+        rows_total += static_cast<int64_t>(telmo_logmel_rows(TELMO_FRONTEND_GRANITE, lengths[u]));
+        frames_total_est += static_cast<int64_t>(telmo_granite_frames_for_samples(gp, lengths[u]));
+    }
+    if (rows_total > (1 << 30)) return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: batch too large");
+    if (int rc = g->ensure_e2e(static_cast<int>(rows_total) + 1, static_cast<int>(frames_total_est) + 1, n_utt))
+        return rc;
+    if (int rc = g->ctx->cuda(cudaMemcpyAsync(g->audio_dev, samples, sizeof(float) * total, cudaMemcpyHostToDevice, s),
+                              "transcribe"))
+        return rc;
+    if (int rc = g->transcribe_device(g->audio_dev, lengths, n_utt, g->tokens_dev, g->counts_dev, frames, s)) return rc;
+    int64_t frames_total = 0;
+    for (int u = 0; u < n_utt; ++u) frames_total += frames[u];
+    if (int rc = g->ctx->cuda(cudaMemcpyAsync(tokens, g->tokens_dev, sizeof(uint32_t) * 3 * frames_total,
+                                              cudaMemcpyDeviceToHost, s),
+                              "transcribe"))
+        return rc;
+    if (int rc = g->ctx->cuda(cudaMemcpyAsync(counts, g->counts_dev, sizeof(int) * n_utt, cudaMemcpyDeviceToHost, s),
+                              "transcribe"))
+        return rc;
+    return g->ctx->cuda(cudaStreamSynchronize(s), "transcribe");
+}
+
+extern "C" int telmo_granite_profile(telmo_granite* gp, int enable) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    g->prof.on = enable != 0;
+    return TELMO_OK;
+}
+
+extern "C" int telmo_granite_profile_read(telmo_granite* gp, double* ms, long* launches, double* gemm_ops,
+                                          double* gemm_bytes) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    if (int rc = g->ctx->use_device()) return rc;
+    g->prof.read(ms, launches, gemm_ops, gemm_bytes);
+    return TELMO_OK;
+}
+
+extern "C" long telmo_granite_launches(const telmo_granite* gp) {
+    const Granite* g = reinterpret_cast<const Granite*>(gp);
+    if (!g) return -1;
+    long n = g->launches;
+    if (g->ctx->granite_fe) n += g->ctx->granite_fe->launches;
+    return n;
 }
 
 extern "C" int telmo_ctc_tokens(telmo_ctx* cp, const uint32_t* ids, const int* first, const int* frames, int n_utt,

@@ -34,8 +34,27 @@ struct Block {
     DevVec dw_w, dw_b;
 };
 
+// Optional timing of every launch with CUDA events on the launching stream, by kernel class.
+enum ProfKind { kProfGemm = 0, kProfAttention, kProfRows, kProfFrontEnd, kProfKinds };
+
+struct Profiler {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;   // free events
+    std::vector<cudaEvent_t> start[kProfKinds], stop[kProfKinds];
+    double gemm_ops = 0.0, gemm_bytes = 0.0;
+    long count[kProfKinds] = {0, 0, 0, 0};
+
+    cudaEvent_t take();
+    void begin(int kind, cudaStream_t s);
+    void end(int kind, cudaStream_t s);
+    // Sums the recorded intervals (ms) per kind, then recycles the events.
+    void read(double* ms, long* launches, double* ops, double* bytes);
+    ~Profiler();
+};
+
 struct Granite {
     Ctx* ctx = nullptr;
+    Profiler prof;
     telmo_granite_config c{};
     Lin input, head, mid;
     std::vector<Block> blocks;
@@ -48,6 +67,17 @@ struct Granite {
     QuantAct q;
     int* tasks_dev = nullptr;
     int64_t big_ld = 0, vocab_ld = 0;
+
+    // End-to-end buffers (audio in, tokens out), grown on demand.
+    float* audio_dev = nullptr;
+    size_t audio_cap = 0;
+    float* feats_dev = nullptr;
+    float* enc_dev = nullptr;
+    uint32_t* ids_dev = nullptr;
+    uint32_t* tokens_dev = nullptr;
+    int* counts_dev = nullptr;
+    int* first_dev = nullptr;
+    int e2e_rows_cap = 0, e2e_frames_cap = 0, e2e_utt_cap = 0;
 
     struct Entry {
         DevWeights* mat = nullptr;
@@ -70,6 +100,12 @@ struct Granite {
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int logits(const float* encoded, int frames, float* out, int64_t ld, cudaStream_t s);
     int frame_ids(const float* encoded, int frames, uint32_t* ids, float* margin, cudaStream_t s);
+    // Audio (device) -> tokens and counts (device); frames_out (host) gets each utterance's
+    // encoder frames, whose prefix sums place its tokens.
+    int transcribe_device(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
+                          int* frames_out, cudaStream_t s);
+    int ensure_e2e(int rows, int frames, int n_utt);
+    void release_e2e();
 };
 
 }  // namespace telmo

@@ -144,6 +144,67 @@ class Granite:
         """ctc_tokens (src/granite.rs:1074-1094) for every utterance of a batch, on the GPU."""
         return ctc_tokens(self.ctx, ids, frames, self.config["blank"], stream)
 
+    def frames_for_samples(self, samples: int) -> int:
+        return _lib.load().telmo_granite_frames_for_samples(self._h, int(samples))
+
+    def transcribe(self, utterances: Sequence[np.ndarray], stream=None) -> List[List[Token]]:
+        """Granite::transcribe (src/granite.rs:553-582) up to the token ids, for a batch of 16 kHz
+        utterances in host memory."""
+        lengths = np.array([len(u) for u in utterances], np.int64)
+        samples = np.ascontiguousarray(np.concatenate(utterances), dtype=np.float32)
+        return self.transcribe_packed(samples, lengths, stream)
+
+    def transcribe_packed(self, samples: np.ndarray, lengths: np.ndarray, stream=None,
+                          tokens_buf: np.ndarray = None):
+        """As transcribe, with the utterances already packed one after another (host memory;
+        a pinned buffer copies fastest)."""
+        lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+        n = lengths.size
+        cap = sum(self.frames_for_samples(int(x)) for x in lengths)
+        tokens = tokens_buf if tokens_buf is not None else np.zeros(3 * max(cap, 1), np.uint32)
+        counts = np.zeros(n, np.int32)
+        frames = np.zeros(n, np.int32)
+        ptr = samples.data_ptr() if hasattr(samples, "data_ptr") else samples.ctypes.data
+        tptr = tokens.data_ptr() if hasattr(tokens, "data_ptr") else tokens.ctypes.data
+        check(_lib.load().telmo_granite_transcribe(self._h, ptr, lengths.ctypes.data, n, tptr,
+                                                   counts.ctypes.data, frames.ctypes.data,
+                                                   _stream(stream)), self.ctx.handle)
+        tok = tokens if isinstance(tokens, np.ndarray) else tokens.numpy()
+        out, at = [], 0
+        for u in range(n):
+            t = tok[3 * at:3 * at + 3 * counts[u]].reshape(-1, 3)
+            out.append([Token(int(a), int(b), int(c)) for a, b, c in t])
+            at += int(frames[u])
+        return out
+
+    def transcribe_device(self, samples, lengths, tokens, counts, stream=None):
+        """Device-resident variant: samples, tokens [3 * frames] (int32) and counts are CUDA
+        tensors; returns the host array of frames per utterance."""
+        lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+        frames = np.zeros(lengths.size, np.int32)
+        check(_lib.load().telmo_granite_transcribe_device(
+            self._h, samples.data_ptr(), lengths.ctypes.data, lengths.size, tokens.data_ptr(),
+            counts.data_ptr(), frames.ctypes.data, _stream(stream)), self.ctx.handle)
+        return frames
+
+    def launches(self) -> int:
+        return _lib.load().telmo_granite_launches(self._h)
+
+
+def logmel(ctx, kind: int, samples, lengths, stream=None):
+    """The batched front ends (telmo_logmel): samples a CUDA f32 tensor of every utterance's
+    samples one after another; returns (features CUDA tensor, rows per utterance)."""
+    import torch
+    lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+    L = _lib.load()
+    rows_total = sum(L.telmo_logmel_rows(kind, int(x)) for x in lengths)
+    width = 320 if kind == _lib.FRONTEND_GRANITE else 128
+    feats = torch.empty((max(rows_total, 1), width), dtype=torch.float32, device=samples.device)
+    rows = np.zeros(lengths.size, np.int32)
+    check(L.telmo_logmel(ctx.handle, kind, samples.data_ptr(), lengths.ctypes.data, lengths.size,
+                         feats.data_ptr(), rows.ctypes.data, _stream(stream)), ctx.handle)
+    return feats[:int(rows.sum())], rows
+
 
 def ctc_tokens(ctx, ids, frames: Sequence[int], blank: int = 0, stream=None) -> List[List[Token]]:
     import torch
