@@ -25,6 +25,7 @@
 
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cstring>
 #include <mutex>
 
@@ -301,6 +302,15 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                         float* sf = reinterpret_cast<float*>(sbuf);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) sf[j * 32 + lane] = v[j];
+                    } else if (p.out_kind == kOutF16Split) {
+                        __half* sh = reinterpret_cast<__half*>(sbuf);
+                        __half* sl = sh + 32 * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const __half h = __float2half_rn(v[j]);
+                            sh[j * 32 + lane] = h;
+                            sl[j * 32 + lane] = __float2half_rn(__fsub_rn(v[j], __half2float(h)));
+                        }
                     } else {
                         __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(sbuf);
 #pragma unroll
@@ -312,8 +322,21 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     if (lane == 0 && x0 < p.n) {
                         if (p.out_path == kTmaReduce) tma_reduce_add_2d(&map_out, sbuf, x0, mc);
                         else tma_store_2d(&map_out, sbuf, x0, mc);
+                        if (p.out_kind == kOutF16Split) tma_store_2d(&map_out, sbuf + 32 * 32 * 2, x0, mc + p.m);
                         bulk_commit();
                     }
+                } else if (p.out_kind == kOutF16Split) {
+                    float v[32];
+                    compute_chunk_any(p.act, hi, lo, my_rs, ws, bs, p.scale, v);
+                    __half* oh = static_cast<__half*>(p.out) + off;
+                    __half* ol = oh + static_cast<int64_t>(p.m) * p.ldc;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < rows_valid && n_ok) {
+                            const __half h = __float2half_rn(v[j]);
+                            oh[j * p.ldc] = h;
+                            ol[j * p.ldc] = __float2half_rn(__fsub_rn(v[j], __half2float(h)));
+                        }
                 } else if (p.out_kind == kOutF32) {
                     store_chunk_any(p.act, p.accumulate != 0, hi, lo, my_rs, ws, bs, p.scale,
                                     static_cast<float*>(p.out) + off, p.ldc, rows_valid, n_ok);
@@ -378,14 +401,18 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t ldc) {
     auto fn = encode_fn();
     if (!fn) return false;
-    const bool bf = kind == kOutBF16;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * (bf ? 2 : 4)};
+    const bool split = kind == kOutF16Split;
+    const bool two = kind == kOutBF16 || split;
+    // The split output's two planes form one tensor of 2m rows.
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(split ? 2 * m : m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * (two ? 2 : 4)};
     cuuint32_t box[2] = {32, 32};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType type = kind == kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : split          ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    CUresult r = fn(map, type, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -423,10 +450,11 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     CUtensorMap mo;
     memset(&mo, 0, sizeof mo);
     int path = kDirect;
-    const size_t esize = g.out_kind == kOutBF16 ? 2 : 4;
+    const size_t esize = (g.out_kind == kOutBF16 || g.out_kind == kOutF16Split) ? 2 : 4;
     const bool aligned = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldc * esize) % 16 == 0);
     if (aligned && g.out_kind == kOutF32) path = g.accumulate ? kTmaReduce : kTmaStore;
-    if (aligned && g.out_kind == kOutBF16 && !g.accumulate) path = kTmaStore;
+    if (aligned && (g.out_kind == kOutBF16 || g.out_kind == kOutF16Split) && !g.accumulate) path = kTmaStore;
+    if (g.out_kind == kOutF16Split && g.accumulate) return cudaErrorInvalidValue;
     if (path != kDirect && !make_out_map(&mo, g.out, g.out_kind, g.m, w.n, g.ldc)) path = kDirect;
     Params p{g.m, w.n, w.k, g.a.scale, w.scales, g.bias, g.act, g.scale, g.accumulate,
              g.out, g.ldc, g.out_kind, path, g.error};

@@ -40,6 +40,7 @@ Granite::~Granite() {
         lin(b.ff2.up); lin(b.ff2.down); nrm(b.ff2.norm);
         nrm(b.norm_att); nrm(b.norm_conv); nrm(b.norm_out);
         free_weights(&b.qkv); free_weights(&b.rel);
+        if (b.rel16) cudaFree(b.rel16);
         lin(b.out); lin(b.pw1); lin(b.pw2);
         free_vec(b.dw_w); free_vec(b.dw_b);
     }
@@ -265,8 +266,8 @@ int Granite::gemm(const QuantAct& a, int m, const Lin& l, float* out, int64_t ld
     return gemm_w(a, m, l.w, l.b.p, out, ldc, act, scale, acc, s);
 }
 
-int Granite::gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, float* out, int64_t ldc,
-                    int act, float scale, int acc, cudaStream_t s) {
+int Granite::gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc,
+                    int act, float scale, int acc, cudaStream_t s, int out_kind) {
     GemmArgs g;
     g.m = m;
     g.a = a;
@@ -277,7 +278,7 @@ int Granite::gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* 
     g.accumulate = acc;
     g.out = out;
     g.ldc = ldc;
-    g.out_kind = kOutF32;
+    g.out_kind = out_kind;
     g.error = ctx->error_word;
     ++launches;
     if (prof.on) {
@@ -459,13 +460,20 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
         if (int rc = ctx->cuda(ln_chain(cur, m, d, b.norm_att.g.p, b.norm_att.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
             return rc;
         ++launches;
-        if (int rc = gemm_w(q, m, b.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s)) return rc;
-        if (prof.on) prof.begin(kProfAttention, s);
-        if (int rc = ctx->cuda(granite_attention(big, c.heads, c.head_dim, ctxn,
-                                                 reinterpret_cast<const AttnTask*>(tasks_dev + p.att_off), p.att_n,
-                                                 b.rel.values, b.rel.ld, b.rel.scales, scale, att, s),
-                               "attention"))
+        // The tensor-core attention takes Q, K and V as fp16 high/low planes straight from the
+        // product's epilogue; the other path takes f32.
+        const bool mma = granite_attention_mma_supported(c.head_dim, ctxn) && b.rel16;
+        if (int rc = gemm_w(q, m, b.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s, mma ? kOutF16Split : kOutF32))
             return rc;
+        if (prof.on) prof.begin(kProfAttention, s);
+        const AttnTask* att_tasks = reinterpret_cast<const AttnTask*>(tasks_dev + p.att_off);
+        const cudaError_t ae =
+            mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(m) * 3 * d, c.heads,
+                                        c.head_dim, ctxn, att_tasks, p.att_n, static_cast<const __half*>(b.rel16),
+                                        b.rel.scales, scale, att, s)
+                : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, p.att_n, b.rel.values, b.rel.ld,
+                                    b.rel.scales, scale, att, s);
+        if (int rc = ctx->cuda(ae, "attention")) return rc;
         if (prof.on) prof.end(kProfAttention, s);
         ++launches;
         if (int rc = ctx->cuda(quantize_x2(att, d, m, d, q, s), "quant")) return rc;
@@ -569,7 +577,23 @@ extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int
     if (int rc = g->ctx->use_device()) return rc;
     free_weights(e.mat);
     g->finalized = false;
-    return upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat);
+    if (int rc = upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat)) return rc;
+    // The relative tables also get an fp16 copy for the tensor-core attention (int8 values are
+    // exact in fp16); the per-position scales stay in the weights' scale vector.
+    for (auto& b : g->blocks) {
+        if (e.mat != &b.rel) continue;
+        if (b.rel16) cudaFree(b.rel16);
+        b.rel16 = nullptr;
+        std::vector<__half> rel16(n * k);
+        const int8_t* v = static_cast<const int8_t*>(panel_values);
+        for (size_t o = 0; o < n; ++o)
+            for (size_t i = 0; i < k; ++i)
+                rel16[o * k + i] = __float2half(static_cast<float>(v[((o / 16) * k + i) * 16 + o % 16]));
+        if (int rc = g->ctx->cuda(cudaMalloc(&b.rel16, sizeof(__half) * n * k), "granite rel")) return rc;
+        return g->ctx->cuda(cudaMemcpy(b.rel16, rel16.data(), sizeof(__half) * n * k, cudaMemcpyHostToDevice),
+                            "granite rel");
+    }
+    return TELMO_OK;
 }
 
 extern "C" int telmo_granite_set_vector(telmo_granite* gp, const char* name, size_t len, const float* data) {

@@ -30,6 +30,7 @@ struct Block {
     FF ff1, ff2;
     Norm norm_att, norm_conv, norm_out;
     DevWeights qkv, rel;
+    void* rel16 = nullptr;  // the relative table as fp16 [2 * ctx - 1, head_dim] (exact)
     Lin out, pw1, pw2;
     DevVec dw_w, dw_b;
 };
@@ -94,8 +95,8 @@ struct Granite {
     void release_buffers();
     int gemm(const QuantAct& a, int m, const Lin& l, float* out, int64_t ldc, int act, float scale, int acc,
              cudaStream_t s);
-    int gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, float* out, int64_t ldc, int act,
-               float scale, int acc, cudaStream_t s);
+    int gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc, int act,
+               float scale, int acc, cudaStream_t s, int out_kind = kOutF32);
     int feed_forward(const FF& f, float* x, int m, cudaStream_t s);
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int logits(const float* encoded, int frames, float* out, int64_t ld, cudaStream_t s);

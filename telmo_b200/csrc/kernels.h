@@ -7,7 +7,9 @@
 
 namespace telmo {
 
-enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutI32Pair = 2 };
+// kOutF16Split writes each value v as two fp16 planes, hi = fp16(v) at rows 0..m-1 and
+// lo = fp16(v - hi) at rows m..2m-1 (ldc apart): the operands of the tensor-core attention.
+enum OutKind : int { kOutF32 = 0, kOutBF16 = 1, kOutI32Pair = 2, kOutF16Split = 3 };
 enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
 
 // Quantized activations for the split-int8 GEMM: two int8 levels and one scale per row, rows

@@ -3,6 +3,8 @@
 
 #include "kernels.h"
 
+#include <cuda_fp16.h>
+
 namespace telmo {
 
 // One span of a depthwise convolution: output frames [out_first, out_first + count) of one
@@ -47,5 +49,13 @@ cudaError_t ctc_collapse(const uint32_t* ids, const int* first, const int* frame
 cudaError_t granite_attention(const float* qkv, int heads, int hd, int ctx, const AttnTask* tasks, int n_tasks,
                               const int8_t* rel_w, int64_t ld_rel, const float* rel_scale, float scale,
                               float* att, cudaStream_t stream);
+
+// The same on the tensor cores (attention_mma.cu), for context 128 and head sizes 64 or 128:
+// qkv as fp16 high/low planes ([rows, 3 * heads * hd] each, the low one `plane` elements after
+// the high one), the relative table as fp16 [2 * ctx - 1, hd] with one f32 scale per row.
+bool granite_attention_mma_supported(int hd, int ctx);
+cudaError_t granite_attention_mma(const __half* qkv, int64_t plane, int heads, int hd, int ctx, const AttnTask* tasks,
+                                  int n_tasks, const __half* rel16, const float* rel_scale, float scale, float* att,
+                                  cudaStream_t stream);
 
 }  // namespace telmo
