@@ -317,6 +317,12 @@ class LinearWorkload:
 WORKLOADS = {"granite": GraniteWorkload, "linear": LinearWorkload}
 
 
+def make_workload(args, rank, world):
+    if args.workload == "granite":
+        return GraniteWorkload(rank, world, n_utt=args.utterances)
+    return WORKLOADS[args.workload](rank, world)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import telmo_b200
@@ -330,7 +336,7 @@ def run_ours(args, rank, world, local_rank):
                                     device_id=torch.device("cuda", local_rank))
         dist = dist_mod
     ctx = telmo_b200.Context(local_rank)
-    wl = WORKLOADS[args.workload](rank, world)
+    wl = make_workload(args, rank, world)
     wl.setup_gpu(ctx)
     granite = args.workload == "granite"
 
@@ -448,7 +454,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    wl = WORKLOADS[args.workload](0, 1)
+    wl = make_workload(args, 0, 1)
     if hasattr(wl, "cpu_setup"):
         wl.cpu_setup()
         per_step = wl.cpu_seconds
@@ -489,6 +495,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="granite")
+    ap.add_argument("--utterances", type=int, default=4096,
+                    help="granite: utterances in the set (4096 is config 5; fewer for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
