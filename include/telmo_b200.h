@@ -99,6 +99,24 @@ int telmo_linear(telmo_ctx *ctx, const float *a, size_t lda, size_t m, const tel
 int telmo_quantize_x2(telmo_ctx *ctx, const float *a, size_t lda, size_t m, size_t k, int8_t *hi,
                       int8_t *lo, size_t ldq, float *scale, void *stream);
 
+/* telmo_linear without any device allocation. It has no counterpart in the reference: telmo's
+ * CPU matmul never allocates device memory, but telmo_linear grows a workspace with cudaMalloc,
+ * which some callers cannot allow -- a service that gives all device memory to its own pool or
+ * fixed budget up front, or a latency-critical stream that cannot take the device-wide
+ * synchronisation that cudaMalloc and cudaFree imply. Here the quantized activations go to a
+ * fixed 8 MiB scratch array compiled into the library (every GPU that loads the library holds
+ * it until the process exits): both levels (m * round_up(k, 16) bytes each) and m f32 scales,
+ * each rounded up to 256 bytes, must fit -- up to 4088 rows at k = 1024, 1023 at k = 4096;
+ * larger products are TELMO_ERR_ARGUMENT (use telmo_linear). Arguments,
+ * results and errors are otherwise those of telmo_linear. The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture. All calls in the process share the one array: calls whose work may overlap
+ * on the GPU (different streams, or different host threads) race and must be serialised by the
+ * caller. */
+int telmo_linear_noalloc(telmo_ctx *ctx, const float *a, size_t lda, size_t m,
+                         const telmo_weights *w, const float *bias, int act, float scale,
+                         int accumulate, void *c, int c_dtype, size_t ldc, void *stream);
+
 /* telmo_linear on activations that telmo_quantize_x2 already split. */
 int telmo_linear_q(telmo_ctx *ctx, const int8_t *hi, const int8_t *lo, size_t ldq,
                    const float *row_scale, size_t m, const telmo_weights *w, const float *bias,

@@ -38,6 +38,8 @@ SIGNATURES = {
     "telmo_linear": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _int, _float, _int, _vp, _int, _sz,
                             _vp]),
     "telmo_quantize_x2": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
+    "telmo_linear_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _int, _float, _int, _vp, _int,
+                                    _sz, _vp]),
     "telmo_linear_q": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp, _vp, _int, _float, _int, _vp,
                               _int, _sz, _vp]),
     "telmo_granite_create": (_int, [_vp, _vp, _c.POINTER(_vp)]),
