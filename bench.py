@@ -113,35 +113,17 @@ class GraniteWorkload:
     POOL = 64  # distinct 30 s base waveforms; utterance u is a slice of waveform u % 64
 
     def __init__(self, rank, world, n_utt=4096, batch_seconds=2048.0):
-        from telmo_b200 import synthetic
+        from telmo_b200 import sharding, synthetic
         self.synthetic = synthetic
         self.n_utt = n_utt
         secs = synthetic.lengths_log_uniform(n_utt, 1.0, 30.0, seed=0)
         self.samples = np.maximum((secs * SR).astype(np.int64), 2 * 160)
         self.total_seconds = float(self.samples.sum()) / SR
-        # Longest-first greedy assignment of utterances to ranks (cost linear in length).
-        order = np.argsort(-self.samples, kind="stable")
-        load = np.zeros(world)
-        owner = np.zeros(n_utt, np.int64)
-        for u in order:
-            r = int(np.argmin(load))
-            owner[u] = r
-            load[r] += self.samples[u]
-        mine = [int(u) for u in order if owner[u] == rank]
-        mine.sort(key=lambda u: self.samples[u])  # length buckets: similar lengths together
-        self.mine = mine
-        self.rank_seconds = float(self.samples[mine].sum()) / SR
-        self.batches = []
-        cur, acc = [], 0.0
-        for u in mine:
-            s = self.samples[u] / SR
-            if cur and acc + s > batch_seconds:
-                self.batches.append(cur)
-                cur, acc = [], 0.0
-            cur.append(u)
-            acc += s
-        if cur:
-            self.batches.append(cur)
+        # Longest-first greedy assignment of utterances to ranks, then length-sorted batches.
+        mine = sharding.assign(self.samples, world)[rank]
+        self.batches = sharding.batches(mine, self.samples, batch_seconds)
+        self.mine = [u for b in self.batches for u in b]
+        self.rank_seconds = float(self.samples[self.mine].sum()) / SR
         self.batch_seconds = batch_seconds
 
     def utterance(self, u, pool):
