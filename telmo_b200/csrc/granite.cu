@@ -348,11 +348,15 @@ Profiler::~Profiler() {
     for (auto e : pool) cudaEventDestroy(e);
 }
 
-int Granite::feed_forward(const FF& f, float* xb, int m, cudaStream_t s) {
-    // Granite::feed_forward (src/granite.rs:752-793).
+int Granite::feed_forward(const FF& f, float* xb, int m, cudaStream_t s, bool normed) {
+    // Granite::feed_forward (src/granite.rs:752-793). With `normed`, q already holds the
+    // quantized LN(x) (the previous block's closing norm computed it).
     const int d = c.d_model;
-    if (int rc = ctx->cuda(ln_chain(xb, m, d, f.norm.g.p, f.norm.b.p, nullptr, nullptr, nullptr, &q, s), "ln")) return rc;
-    ++launches;
+    if (!normed) {
+        if (int rc = ctx->cuda(ln_chain(xb, m, d, f.norm.g.p, f.norm.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
+            return rc;
+        ++launches;
+    }
     if (int rc = gemm(q, m, f.up, big, big_ld, kActSilu, 1.0f, 0, s)) return rc;
     if (int rc = ctx->cuda(quantize_x2(big, big_ld, m, c.ff, q, s), "quant")) return rc;
     ++launches;
@@ -449,13 +453,15 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
 
     const float scale = static_cast<float>(std::pow(static_cast<double>(c.head_dim), -0.5));
     const int sc_layer = c.layers / 2 - 1;
+    bool normed = false;  // q holds the next block's quantized first norm
     float* cur = x;
     float* other = y;
     for (int i = 0; i < c.layers; ++i) {
         const Block& b = blocks[i];
         const Plan& p = plans[i];
         const int m = p.m;
-        if (int rc = feed_forward(b.ff1, cur, m, s)) return rc;
+        if (int rc = feed_forward(b.ff1, cur, m, s, normed)) return rc;
+        normed = false;
         // Attention (src/granite.rs:820-851).
         if (int rc = ctx->cuda(ln_chain(cur, m, d, b.norm_att.g.p, b.norm_att.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
             return rc;
@@ -500,9 +506,16 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
         ++launches;
         if (int rc = gemm(q, n, b.pw2, target, d, kActNone, 1.0f, 1, s)) return rc;
         if (int rc = feed_forward(b.ff2, target, n, s)) return rc;
-        if (int rc = ctx->cuda(ln_chain(target, n, d, b.norm_out.g.p, b.norm_out.b.p, target, nullptr, nullptr, nullptr, s),
+        // The closing norm; unless self-conditioning or a tap comes between, fused with the next
+        // block's first norm and its quantization (one pass over the residual stream).
+        const bool chain = i + 1 < c.layers && i != sc_layer && i != tap;
+        const FF* next_ff1 = chain ? &blocks[i + 1].ff1 : nullptr;
+        if (int rc = ctx->cuda(ln_chain(target, n, d, b.norm_out.g.p, b.norm_out.b.p, target,
+                                        chain ? next_ff1->norm.g.p : nullptr, chain ? next_ff1->norm.b.p : nullptr,
+                                        chain ? &q : nullptr, s),
                                "ln"))
             return rc;
+        normed = chain;
         ++launches;
         if (b.strided) std::swap(cur, other);
         if (i == sc_layer) {

@@ -97,7 +97,7 @@ struct Granite {
              cudaStream_t s);
     int gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc, int act,
                float scale, int acc, cudaStream_t s, int out_kind = kOutF32);
-    int feed_forward(const FF& f, float* x, int m, cudaStream_t s);
+    int feed_forward(const FF& f, float* x, int m, cudaStream_t s, bool normed = false);
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int logits(const float* encoded, int frames, float* out, int64_t ld, cudaStream_t s);
     int frame_ids(const float* encoded, int frames, uint32_t* ids, float* margin, cudaStream_t s);

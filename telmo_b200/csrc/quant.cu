@@ -69,6 +69,43 @@ __global__ void quantize_x2_kernel(const float* __restrict__ x, int64_t ldx, int
     if (lane == 0) scale[row] = d;
 }
 
+// The same for rows of k = 128 * C values (16-byte aligned): the row stays in registers, so it
+// is read from memory once.
+template <int C>
+__global__ void __launch_bounds__(256) quantize_x2_regs_kernel(const float* __restrict__ x, int64_t ldx, int m,
+                                                               int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                                                               int64_t ldq, float* __restrict__ scale) {
+    const int row = blockIdx.x * 8 + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    const float* xr = x + row * ldx;
+    float4 v[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4);
+    float amax = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
+    amax = warp_max(amax);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float id_lo = __fmul_rn(id, 254.0f);
+    int8_t* hr = hi + row * ldq;
+    int8_t* lr = lo + row * ldq;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        char4 h, l;
+        quant_one(v[c].x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
+        quant_one(v[c].y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
+        quant_one(v[c].z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
+        quant_one(v[c].w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
+        *reinterpret_cast<char4*>(hr + (c * 32 + lane) * 4) = h;
+        *reinterpret_cast<char4*>(lr + (c * 32 + lane) * 4) = l;
+    }
+    for (int i = C * 128 + lane; i < ldq; i += 32) hr[i] = lr[i] = 0;
+    if (lane == 0) scale[row] = d;
+}
+
 }  // namespace
 
 cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,
@@ -76,6 +113,18 @@ cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAc
     if (m <= 0) return cudaSuccess;
     constexpr int kWarps = 8;
     const int grid = (m + kWarps - 1) / kWarps;
+    const bool regs = k % 128 == 0 && ldx % 4 == 0 && q.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (regs) {
+        switch (k / 128) {
+            case 8: quantize_x2_regs_kernel<8><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+                return cudaGetLastError();
+            case 16: quantize_x2_regs_kernel<16><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+                return cudaGetLastError();
+            case 32: quantize_x2_regs_kernel<32><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+                return cudaGetLastError();
+            default: break;
+        }
+    }
     quantize_x2_kernel<<<grid, kWarps * 32, 0, stream>>>(x, ldx, m, k, q.hi, q.lo, q.ld, q.scale);
     return cudaGetLastError();
 }

@@ -174,52 +174,57 @@ __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t r
     return __fdiv_rn(a, __fadd_rn(1.0f, expf(-b)));
 }
 
-// GLU + depthwise convolution (taps in order from the bias, zero outside the utterance) + SiLU.
-// Task t covers output frames [out_first, out_first + count) of one utterance; threads cover
-// channels. A register window of K GLU values slides along the input frames.
+// GLU + depthwise convolution (taps in order from the bias, skipping frames outside the
+// utterance) + SiLU. Task t covers output frames [out_first, out_first + count <= 32) of one
+// utterance; each thread owns one channel. The GLU values of every input frame the task reads
+// are staged first -- eight frames' loads in flight at a time -- in a shared column per thread,
+// then each output frame sums its K taps from there.
+constexpr int kConvSpan = 32;  // output frames per task (set by the host's task list)
+
 template <int K>
-__global__ void glu_dwconv_silu_kernel(const float* __restrict__ big, int cc, const ConvTask* __restrict__ tasks,
-                                       const float* __restrict__ w, const float* __restrict__ bias,
-                                       float* __restrict__ out) {
-    const ConvTask t = tasks[blockIdx.y];
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= cc) return;
+__global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __restrict__ big, int cc,
+                                                              const ConvTask* __restrict__ tasks,
+                                                              const float* __restrict__ w,
+                                                              const float* __restrict__ bias,
+                                                              float* __restrict__ out) {
     constexpr int half = K / 2;
+    constexpr int kFrames = 2 * (kConvSpan - 1) + K;  // input frames of a stride-2 span
+    __shared__ float glu[kFrames][128];
+    const ConvTask t = tasks[blockIdx.y];
+    const int c = blockIdx.x * 128 + threadIdx.x;
+    const bool live = c < cc;
+    const int s = t.stride;
+    const int f_lo = s * t.out_first - half;
+    const int nf = s * (t.count - 1) + K;
+    const int64_t two_cc = 2 * static_cast<int64_t>(cc);
+    for (int i0 = 0; i0 < nf; i0 += 8) {
+        float a[8], b[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int f = f_lo + i0 + u;
+            const bool ok = live && i0 + u < nf && f >= 0 && f < t.in_len;
+            const int64_t row = static_cast<int64_t>(t.in_row + (ok ? f : 0));
+            a[u] = ok ? big[row * two_cc + c] : 0.0f;
+            b[u] = ok ? big[row * two_cc + cc + c] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (i0 + u < nf) glu[i0 + u][threadIdx.x] = __fdiv_rn(a[u], __fadd_rn(1.0f, expf(-b[u])));
+    }
+    if (!live) return;
     float wk[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) wk[j] = __ldg(w + j * cc + c);
-    const float b = __ldg(bias + c);
-    // window[j] = GLU of local input frame (s * r + j - half) for the current output r.
-    float win[K];
-    const int r0 = t.out_first;
-    const int s = t.stride;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-        const int f = s * r0 + j - half;
-        win[j] = (f >= 0 && f < t.in_len) ? glu_at(big, t.in_row + f, cc, c) : 0.0f;
-    }
-    for (int r = r0; r < r0 + t.count; ++r) {
-        float acc = b;
+    const float bc = __ldg(bias + c);
+    for (int r = t.out_first; r < t.out_first + t.count; ++r) {
+        float acc = bc;
 #pragma unroll
         for (int j = 0; j < K; ++j) {
             const int f = s * r + j - half;
-            if (f >= 0 && f < t.in_len) acc = __fadd_rn(acc, __fmul_rn(wk[j], win[j]));
+            if (f >= 0 && f < t.in_len) acc = __fadd_rn(acc, __fmul_rn(wk[j], glu[f - f_lo][threadIdx.x]));
         }
         acc = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
         out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
-        // Slide by the stride.
-        if (s == 1) {
-#pragma unroll
-            for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
-            const int f = r + 1 + K - 1 - half;
-            win[K - 1] = (f >= 0 && f < t.in_len) ? glu_at(big, t.in_row + f, cc, c) : 0.0f;
-        } else {
-#pragma unroll
-            for (int j = 0; j < K - 2; ++j) win[j] = win[j + 2];
-            const int f0 = 2 * (r + 1) + K - 2 - half, f1 = f0 + 1;
-            win[K - 2] = (f0 >= 0 && f0 < t.in_len) ? glu_at(big, t.in_row + f0, cc, c) : 0.0f;
-            win[K - 1] = (f1 >= 0 && f1 < t.in_len) ? glu_at(big, t.in_row + f1, cc, c) : 0.0f;
-        }
     }
 }
 
