@@ -132,6 +132,40 @@ void oracle_granite_frame_ids(const oracle_granite *g, const float *encoded, siz
 void oracle_granite_logits(const oracle_granite *g, const float *encoded, size_t frames,
                            float *logits, int threads);
 
+/* ---- parakeet.rs ----------------------------------------------------------------------------- */
+typedef struct oracle_parakeet oracle_parakeet;
+typedef struct {
+    int d_model, heads, layers, ff, conv_kernel, sub_channels, n_mels, pred_hidden, pred_layers,
+        vocab, blank, n_durations, durations[8], max_symbols;
+} oracle_parakeet_config;
+
+oracle_parakeet *oracle_parakeet_new(const oracle_parakeet_config *config);
+void oracle_parakeet_free(oracle_parakeet *p);
+/* Pack entries by name, as Parakeet::from_pack reads them (src/parakeet.rs:691-795). */
+int oracle_parakeet_set_matrix(oracle_parakeet *p, const char *name, size_t n, size_t k,
+                               const int8_t *values, const float *scales);
+int oracle_parakeet_set_vector(oracle_parakeet *p, const char *name, size_t len, const float *data);
+/* Encoder frames for a number of feature frames (three stride-2 convolutions). */
+size_t oracle_parakeet_frames_for(size_t feature_frames);
+/* positions (src/parakeet.rs:1618-1630): out [2t - 1, d]. */
+void oracle_parakeet_positions(size_t t, size_t d, float *out);
+/* Parakeet::encode (src/parakeet.rs:880-902): features [frames, n_mels] -> out [t, d].
+ * tap_layer >= 0 stops after that layer, -2 after the subsampling. Returns t, or -1. */
+long oracle_parakeet_encode(const oracle_parakeet *p, const float *features, size_t frames,
+                            float *out, int tap_layer, int threads);
+/* Greedy TDT decoding (src/parakeet.rs:1285-1296, :1412-1513): (id, frame, duration) triples,
+ * at most frames * max_symbols + frames of them; min_margin gets the smallest top-2 gap of any
+ * token or duration choice. Returns the token count. */
+size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, size_t frames,
+                              uint32_t *tokens, float *min_margin, int threads);
+/* One step of the greedy TDT loop after the joint (src/parakeet.rs:1482-1510): the first
+ * argmax over logits[0, vocab) is the token, durations[first argmax over the n_durations
+ * logits after them] the duration; a blank moves *t on by max(duration, 1); a token is written
+ * to token[0..2] as (id, *t, duration) and moves *t on by its duration, or for duration 0 after
+ * max_symbols tokens on the frame by 1. Returns 1 when a token was emitted. */
+int oracle_tdt_step(const float *logits, int vocab, int blank, const int *durations, int n_durations,
+                    int max_symbols, size_t *t, int *on_frame, uint32_t *token);
+
 /* ctc_tokens (src/granite.rs:1074-1094): writes (id, frame, duration) triples, returns count. */
 size_t oracle_ctc_tokens(const uint32_t *ids, size_t frames, uint32_t blank, uint32_t *out);
 

@@ -322,3 +322,120 @@ def ctc_tokens(ids, blank=0):
     out = np.zeros(3 * max(ids.size, 1), np.uint32)
     n = lib().oracle_ctc_tokens(ids, ids.size, blank, out)
     return [tuple(int(v) for v in out[3 * i:3 * i + 3]) for i in range(n)]
+
+
+# ---- the Parakeet TDT model ---------------------------------------------------------------------
+
+class ParakeetConfig(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int) for name in (
+        "d_model", "heads", "layers", "ff", "conv_kernel", "sub_channels", "n_mels",
+        "pred_hidden", "pred_layers", "vocab", "blank", "n_durations")] + [
+        ("durations", ctypes.c_int * 8), ("max_symbols", ctypes.c_int)]
+
+
+def _parakeet_lib():
+    L = lib()
+    if getattr(L, "_parakeet_declared", False):
+        return L
+    L.oracle_parakeet_new.restype = ctypes.c_void_p
+    L.oracle_parakeet_new.argtypes = [ctypes.POINTER(ParakeetConfig)]
+    L.oracle_parakeet_free.argtypes = [ctypes.c_void_p]
+    L.oracle_parakeet_set_matrix.restype = ctypes.c_int
+    L.oracle_parakeet_set_matrix.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _sz, _sz, _i8p,
+                                             _f32p]
+    L.oracle_parakeet_set_vector.restype = ctypes.c_int
+    L.oracle_parakeet_set_vector.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _sz, _f32p]
+    L.oracle_parakeet_frames_for.restype = _sz
+    L.oracle_parakeet_frames_for.argtypes = [_sz]
+    L.oracle_parakeet_positions.argtypes = [_sz, _sz, _f32p]
+    L.oracle_parakeet_encode.restype = ctypes.c_long
+    L.oracle_parakeet_encode.argtypes = [ctypes.c_void_p, _f32p, _sz, _f32p, ctypes.c_int,
+                                         ctypes.c_int]
+    L.oracle_parakeet_decode.restype = _sz
+    L.oracle_parakeet_decode.argtypes = [ctypes.c_void_p, _f32p, _sz, _u32p,
+                                         ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+    L.oracle_tdt_step.restype = ctypes.c_int
+    L.oracle_tdt_step.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                  ctypes.c_int, ctypes.c_int, ctypes.POINTER(_sz),
+                                  ctypes.POINTER(ctypes.c_int), _u32p]
+    L._parakeet_declared = True
+    return L
+
+
+def tdt_step(logits, vocab, blank, durations, max_symbols, t, on_frame):
+    """One greedy TDT step after the joint: (token (id, frame, duration) or None, t, on_frame)."""
+    lg = _c(logits, np.float32).reshape(-1)
+    durs = (ctypes.c_int * len(durations))(*[int(x) for x in durations])
+    tt = _sz(t)
+    on = ctypes.c_int(on_frame)
+    tok = np.zeros(3, np.uint32)
+    emitted = _parakeet_lib().oracle_tdt_step(lg, vocab, blank, durs, len(durations), max_symbols,
+                                              ctypes.byref(tt), ctypes.byref(on), tok)
+    return (tuple(int(v) for v in tok) if emitted else None), tt.value, on.value
+
+
+def parakeet_frames_for(feature_frames):
+    return _parakeet_lib().oracle_parakeet_frames_for(feature_frames)
+
+
+def parakeet_positions(t, d):
+    out = np.zeros((2 * t - 1, d), np.float32)
+    _parakeet_lib().oracle_parakeet_positions(t, d, out.reshape(-1))
+    return out
+
+
+class Parakeet:
+    """The oracle's Parakeet TDT model, filled from the same named entries as the CUDA model."""
+
+    def __init__(self, config: dict, entries: dict):
+        L = _parakeet_lib()
+        cfg = ParakeetConfig()
+        for key in ("d_model", "heads", "layers", "ff", "conv_kernel", "sub_channels", "n_mels",
+                    "pred_hidden", "pred_layers", "vocab", "blank", "max_symbols"):
+            setattr(cfg, key, int(config[key]))
+        cfg.n_durations = len(config["durations"])
+        for i, v in enumerate(config["durations"]):
+            cfg.durations[i] = int(v)
+        self.config = dict(config)
+        self._h = L.oracle_parakeet_new(ctypes.byref(cfg))
+        if not self._h:
+            raise ValueError("the Parakeet config does not fit together")
+        for name, entry in entries.items():
+            if isinstance(entry, tuple):
+                values, scales, n, k = entry
+                rc = L.oracle_parakeet_set_matrix(self._h, name.encode(), n, k,
+                                                  _c(values, np.int8), _c(scales, np.float32))
+            else:
+                data = _c(entry, np.float32).reshape(-1)
+                rc = L.oracle_parakeet_set_vector(self._h, name.encode(), data.size, data)
+            if rc != 0:
+                raise ValueError(f"bad entry {name}")
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None):
+                _parakeet_lib().oracle_parakeet_free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+    def encode(self, features, tap_layer=-1, threads=1):
+        f = _c(features, np.float32)
+        t = parakeet_frames_for(f.shape[0])
+        out = np.zeros((max(t, 1), self.config["d_model"]), np.float32)
+        got = _parakeet_lib().oracle_parakeet_encode(self._h, f.reshape(-1), f.shape[0],
+                                                     out.reshape(-1), tap_layer, threads)
+        if got < 0:
+            raise ValueError("no feature frames")
+        return out[:got]
+
+    def decode(self, encoded, threads=1):
+        """Greedy TDT: ([(id, frame, duration), ...], smallest top-2 logit gap)."""
+        e = _c(encoded, np.float32)
+        frames = e.shape[0]
+        cap = frames * (self.config["max_symbols"] + 1) + 1
+        out = np.zeros(3 * cap, np.uint32)
+        margin = ctypes.c_float()
+        n = _parakeet_lib().oracle_parakeet_decode(self._h, e.reshape(-1), frames, out,
+                                                   ctypes.byref(margin), threads)
+        return [tuple(int(v) for v in out[3 * i:3 * i + 3]) for i in range(n)], margin.value

@@ -129,6 +129,74 @@ def granite_entries(config: dict, seed: int = 1, scales: str = "spec") -> dict:
     return e
 
 
+PARAKEET = dict(d_model=1024, heads=8, layers=24, ff=4096, conv_kernel=9, sub_channels=256,
+                n_mels=128, pred_hidden=640, pred_layers=2, vocab=8193, blank=8192,
+                durations=[0, 1, 2, 3, 4], max_symbols=10)
+
+
+def parakeet_config(**overrides) -> dict:
+    c = dict(PARAKEET)
+    c.update(overrides)
+    return c
+
+
+def parakeet_entries(config: dict, seed: int = 3, scales: str = "spec") -> dict:
+    """Random-init weights of a Parakeet-TDT-shaped model, named as the reference's pack entries
+    (src/parakeet.rs:341-486): matrices as (values, scales, n, k), vectors as f32 arrays. The
+    subsampling convolutions draw N(0, 1/9) (weights [9, channels], tap first), layer norms
+    gamma 1 + N(0, 0.02) and beta N(0, 0.02), biases N(0, 0.02), depthwise weights
+    N(0, 1/kernel), bias_u and bias_v N(0, 0.02), the embedding N(0, 1)."""
+    g = rng(seed)
+    c = config
+    d, ch, h, k = c["d_model"], c["sub_channels"], c["pred_hidden"], c["conv_kernel"]
+    outputs = c["vocab"] + len(c["durations"])
+    e = {}
+
+    def int8m(n, kk):
+        return int8_matrix(g, n, kk, scales)
+
+    def f32(shape, std, mean=0.0):
+        return (mean + g.standard_normal(shape) * std).astype(np.float32)
+
+    for name in ("conv0", "dw1", "dw2"):
+        e[f"sub.{name}.w"] = f32((9, ch), 1.0 / 3.0)
+        e[f"sub.{name}.b"] = f32(ch, 0.02)
+    for name in ("pw1", "pw2"):
+        e[f"sub.{name}"] = int8m(ch, ch)
+        e[f"sub.{name}.b"] = f32(ch, 0.02)
+    e["sub.linear"] = int8m(d, ch * (c["n_mels"] // 8))
+    e["sub.linear.b"] = f32(d, 0.02)
+    for i in range(c["layers"]):
+        o = f"layers.{i}"
+        for nm in ("norm_ff1", "norm_att", "norm_conv", "norm_ff2", "norm_out"):
+            e[f"{o}.{nm}.w"] = f32(d, 0.02, 1.0)
+            e[f"{o}.{nm}.b"] = f32(d, 0.02)
+        e[f"{o}.ff1_in"] = int8m(c["ff"], d)
+        e[f"{o}.ff1_out"] = int8m(d, c["ff"])
+        e[f"{o}.qkv"] = int8m(3 * d, d)
+        e[f"{o}.pos"] = int8m(d, d)
+        e[f"{o}.bias_u"] = f32(d, 0.02)
+        e[f"{o}.bias_v"] = f32(d, 0.02)
+        e[f"{o}.out"] = int8m(d, d)
+        e[f"{o}.pw1"] = int8m(2 * d, d)
+        e[f"{o}.dw.w"] = f32((k, d), 1.0 / math.sqrt(k))
+        e[f"{o}.dw.b"] = f32(d, 0.02)
+        e[f"{o}.pw2"] = int8m(d, d)
+        e[f"{o}.ff2_in"] = int8m(c["ff"], d)
+        e[f"{o}.ff2_out"] = int8m(d, c["ff"])
+    for l in range(c["pred_layers"]):
+        e[f"dec.lstm.{l}"] = int8m(4 * h, 2 * h)
+        e[f"dec.lstm.{l}.b"] = f32(4 * h, 0.02)
+    e["dec.embedding"] = f32((c["vocab"], h), 1.0)
+    e["dec.pred_proj"] = int8m(h, h)
+    e["dec.pred_proj.b"] = f32(h, 0.02)
+    e["dec.enc_proj"] = int8m(h, d)
+    e["dec.enc_proj.b"] = f32(h, 0.02)
+    e["dec.joint"] = int8m(outputs, h)
+    e["dec.joint.b"] = f32(outputs, 0.02)
+    return e
+
+
 def audio(seconds: float, seed: int = 2) -> np.ndarray:
     """16 kHz f32 audio: 8 random sinusoids (50-4000 Hz) plus N(0, 0.05) noise."""
     g = rng(seed)

@@ -297,3 +297,131 @@ def test_tiny_granite_encodes_deterministically(oracle_lib):
     assert ids.shape == (11,) and np.all(margin >= 0)
     with pytest.raises(ValueError):
         g.encode(feats[:3])
+
+
+# ---- parakeet.rs --------------------------------------------------------------------------------
+
+@pytest.mark.skipif(not refdata.available(), reason="no copy of the reference's golden files")
+def test_parakeet_frames_for_matches_the_reference_goldens(oracle_lib):
+    for cid, _, tensors in refdata.clips("parakeet-tdt-0.6b-v3"):
+        feats = int(tensors["features_len"].reshape(-1)[0])
+        assert oracle_lib.parakeet_frames_for(feats) == int(tensors["encoded_len"][0]), cid
+        assert tensors["subsampling"].shape[0] in (int(tensors["encoded_len"][0]),
+                                                   int(tensors["encoded_len"][0]) + 1)
+
+
+@pytest.mark.skipif(not refdata.available(), reason="no copy of the reference's golden files")
+def test_tdt_loop_replays_the_reference_goldens(oracle_lib):
+    # The goldens trace the joint's logits of the first decoding steps with the frame each read;
+    # feeding them to the greedy TDT step must land on the same frames and emit the same
+    # (id, frame, duration) tokens as the reference (tests/goldens.rs:236-269).
+    vocab, blank, durations, max_symbols = 8193, 8192, [0, 1, 2, 3, 4], 10
+    checked = 0
+    for cid, _, tensors in refdata.clips("parakeet-tdt-0.6b-v3"):
+        joints, joint_frames = tensors["joint"], tensors["joint_frame"]
+        want = list(zip(tensors["tokens"].tolist(), tensors["token_frame"].tolist(),
+                        tensors["token_duration"].tolist()))
+        t, on, got = 0, 0, []
+        for s in range(joints.shape[0]):
+            assert t == int(joint_frames[s]), (cid, s)
+            tok, t, on = oracle_lib.tdt_step(joints[s], vocab, blank, durations, max_symbols, t,
+                                             on)
+            if tok is not None:
+                got.append(tok)
+        assert got and got == want[:len(got)], cid
+        checked += 1
+    assert checked >= 5
+
+
+def test_tdt_step_rules(oracle_lib):
+    vocab, blank, durs = 4, 3, [0, 1, 2]
+
+    def logits(token, dur):
+        v = np.zeros(vocab + len(durs), np.float32)
+        v[token] = 1.0
+        v[vocab + dur] = 1.0
+        return v
+
+    # A blank with duration 0 still moves on one frame; with 2, two.
+    assert oracle_lib.tdt_step(logits(3, 0), vocab, blank, durs, 2, 5, 1) == (None, 6, 0)
+    assert oracle_lib.tdt_step(logits(3, 2), vocab, blank, durs, 2, 5, 1) == (None, 7, 0)
+    # A token with duration 0 stays on the frame until max_symbols tokens came out there.
+    assert oracle_lib.tdt_step(logits(1, 0), vocab, blank, durs, 2, 5, 0) == ((1, 5, 0), 5, 1)
+    assert oracle_lib.tdt_step(logits(1, 0), vocab, blank, durs, 2, 5, 1) == ((1, 5, 0), 6, 0)
+    assert oracle_lib.tdt_step(logits(2, 2), vocab, blank, durs, 2, 5, 1) == ((2, 5, 2), 7, 0)
+    # Ties go to the first index (argmax, src/parakeet.rs:1683-1691).
+    tie = np.zeros(vocab + len(durs), np.float32)
+    assert oracle_lib.tdt_step(tie, vocab, blank, durs, 2, 0, 0) == ((0, 0, 0), 0, 1)
+
+
+def test_parakeet_positions_are_sinusoids_of_the_offset(oracle_lib):
+    # positions (src/parakeet.rs:1618-1630): row r is position t - 1 - r.
+    t, d = 7, 16
+    pos = oracle_lib.parakeet_positions(t, d)
+    assert pos.shape == (2 * t - 1, d)
+    p = (t - 1 - np.arange(2 * t - 1, dtype=np.float64))[:, None]
+    freq = np.exp(-np.arange(0, d, 2, dtype=np.float64) * (np.log(10000.0) / d))[None, :]
+    assert np.allclose(pos[:, 0::2], np.sin(p * freq), rtol=0, atol=1e-7)
+    assert np.allclose(pos[:, 1::2], np.cos(p * freq), rtol=0, atol=1e-7)
+    assert np.all(pos[t - 1, 0::2] == 0) and np.all(pos[t - 1, 1::2] == 1)
+    assert np.array_equal(pos[:t - 1, 0::2], -pos[t:, 0::2][::-1])
+
+
+def _np_conv3x3s2(x, w, b, depthwise):
+    """[t, f, ch] (depthwise) or [t, f] -> [t', f', ch], zero padding 1, taps dt * 3 + df."""
+    t, f = x.shape[:2]
+    to, fo = (t - 1) // 2 + 1, (f - 1) // 2 + 1
+    out = np.tile(b.astype(np.float64), (to, fo, 1))
+    xp = np.zeros((t + 2, f + 2) + x.shape[2:], np.float64)
+    xp[1:t + 1, 1:f + 1] = x
+    for dt in range(3):
+        for df in range(3):
+            src = xp[dt:dt + 2 * to:2, df:df + 2 * fo:2]
+            if not depthwise:
+                src = src[..., None]
+            out += src * w[dt * 3 + df].astype(np.float64)
+    return out
+
+
+def test_parakeet_subsampling_matches_a_direct_restatement(oracle_lib):
+    # Parakeet::subsample (src/parakeet.rs:904-993) in f64 numpy: conv0 + ReLU, depthwise,
+    # pointwise + ReLU twice, flatten channel-major (c * freqs + f), linear.
+    from telmo_b200 import synthetic
+    c = synthetic.parakeet_config(layers=1, d_model=128, heads=2, ff=256, sub_channels=16,
+                                  n_mels=32, pred_hidden=32, vocab=17, blank=16)
+    e = synthetic.parakeet_entries(c, seed=4, scales="conditioned")
+    model = oracle_lib.Parakeet(c, e)
+    feats = synthetic.rng(9).standard_normal((37, 32)).astype(np.float32)
+    got = model.encode(feats, tap_layer=-2)
+
+    def dense(name):
+        v, s, n, k = e[name]
+        return oracle_lib.decode_int8(v, s, n, k).astype(np.float64)
+
+    h = np.maximum(_np_conv3x3s2(feats, e["sub.conv0.w"], e["sub.conv0.b"], False), 0)
+    h = _np_conv3x3s2(h, e["sub.dw1.w"], e["sub.dw1.b"], True)
+    h = np.maximum(h @ dense("sub.pw1").T + e["sub.pw1.b"], 0)
+    h = _np_conv3x3s2(h, e["sub.dw2.w"], e["sub.dw2.b"], True)
+    h = np.maximum(h @ dense("sub.pw2").T + e["sub.pw2.b"], 0)
+    flat = h.transpose(0, 2, 1).reshape(h.shape[0], -1)
+    want = flat @ dense("sub.linear").T + e["sub.linear.b"]
+    assert got.shape == want.shape == (oracle_lib.parakeet_frames_for(37), 128)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+def test_tiny_parakeet_is_deterministic_and_decodes_in_order(oracle_lib):
+    from telmo_b200 import synthetic
+    c = synthetic.parakeet_config(layers=2, d_model=128, heads=2, ff=256, sub_channels=32,
+                                  pred_hidden=64, vocab=65, blank=64)
+    model = oracle_lib.Parakeet(c, synthetic.parakeet_entries(c, seed=5, scales="conditioned"))
+    feats = synthetic.rng(8).standard_normal((203, 128)).astype(np.float32)
+    out1 = model.encode(feats, threads=1)
+    out3 = model.encode(feats, threads=3)
+    assert out1.shape == (26, 128) and np.array_equal(out1, out3)
+    tokens, margin = model.decode(out1)
+    assert tokens == model.decode(out1, threads=3)[0]
+    frames = [f for _, f, _ in tokens]
+    assert frames == sorted(frames) and all(0 <= f < 26 for f in frames)
+    assert all(i != c["blank"] and i < c["vocab"] for i, _, _ in tokens)
+    assert all(d in c["durations"] for _, _, d in tokens)
+    assert np.isfinite(margin)
