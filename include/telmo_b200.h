@@ -225,6 +225,76 @@ int telmo_granite_profile_read(telmo_granite *g, double *ms, long *launches, dou
 int telmo_ctc_tokens(telmo_ctx *ctx, const uint32_t *ids, const int *first, const int *frames,
                      int n_utt, uint32_t blank, uint32_t *tokens, int *counts, void *stream);
 
+/* ---- Parakeet TDT (src/parakeet.rs) ------------------------------------------------------------ */
+
+/* Config (src/parakeet.rs:52-68): the encoder, the prediction network and the joint. */
+typedef struct {
+    int d_model, heads, layers, ff, conv_kernel;
+    int sub_channels;          /* channels of the subsampling convolutions */
+    int n_mels;                /* feature width (128 for the Parakeet front end) */
+    int pred_hidden, pred_layers;
+    int vocab, blank;          /* tokens plus the blank, which is the last */
+    int n_durations;           /* entries used in durations */
+    int durations[8];
+    int max_symbols;           /* tokens one frame may emit before decoding moves on */
+} telmo_parakeet_config;
+
+typedef struct telmo_parakeet telmo_parakeet;
+
+/* A model shell, checked as Config::from_json checks a config (src/parakeet.rs:70-145). */
+int telmo_parakeet_create(telmo_ctx *ctx, const telmo_parakeet_config *config,
+                          telmo_parakeet **out);
+void telmo_parakeet_free(telmo_parakeet *p);
+/* Pack entries by name as Parakeet::from_pack reads them (src/parakeet.rs:691-795): matrices
+ * "sub.pw1", "sub.pw2", "sub.linear" (whose columns read the last convolution channel-major,
+ * c * freqs + f, as the pack stores it), "layers.<i>.{ff1_in, ff1_out, qkv, pos, out, pw1, pw2,
+ * ff2_in, ff2_out}", "dec.lstm.<l>", "dec.pred_proj", "dec.enc_proj", "dec.joint"; vectors
+ * "sub.{conv0,dw1,dw2}.{w,b}" (weights [9, channels], tap first), "sub.{pw1,pw2,linear}.b",
+ * "layers.<i>.{norm_ff1,norm_att,norm_conv,norm_ff2,norm_out}.{w,b}", "layers.<i>.{bias_u,
+ * bias_v, dw.w, dw.b}", "dec.lstm.<l>.b", "dec.embedding", "dec.{pred_proj,enc_proj,joint}.b". */
+int telmo_parakeet_set_matrix(telmo_parakeet *p, const char *name, int precision, size_t n,
+                              size_t k, const void *panel_values, const float *scales);
+int telmo_parakeet_set_vector(telmo_parakeet *p, const char *name, size_t len, const float *data);
+int telmo_parakeet_finalize(telmo_parakeet *p);
+/* Encoder frames for `feature_frames` feature frames: three stride-2 convolutions,
+ * n -> (n - 1) / 2 + 1 (src/parakeet.rs:909-913). */
+size_t telmo_parakeet_frames_for(size_t feature_frames);
+/* The same for an utterance of `samples` 16 kHz samples (Parakeet front end frames first). */
+size_t telmo_parakeet_frames_for_samples(int64_t samples);
+
+/* Parakeet::encode (src/parakeet.rs:880-902) over a batch: features holds every utterance's
+ * feature frames [rows[u], n_mels] one after another (device f32); out receives every
+ * utterance's encoder frames [frames[u], d_model] one after another (device). rows is a host
+ * array; frames (host) receives the counts. tap_layer -2 returns the subsampling output, i >= 0
+ * layer i's output, -1 the encoder's output. */
+int telmo_parakeet_encode(telmo_parakeet *p, const float *features, const int *rows, int n_utt,
+                          float *out, int *frames, int tap_layer, void *stream);
+/* Parakeet::decode (src/parakeet.rs:1285-1296, greedy TDT decode_inner :1412-1513) for a batch
+ * of encoder outputs (device, packed as telmo_parakeet_encode writes them; frames a host array).
+ * tokens (device) receives (id, frame, duration) triples, utterance u's starting at element
+ * 3 * (counts[0] + ... + counts[u-1]); size it for 3 * max_symbols * (sum of frames). counts
+ * (device, n_utt) receives each utterance's number of tokens, *total (host) their sum. */
+int telmo_parakeet_decode(telmo_parakeet *p, const float *encoded, const int *frames, int n_utt,
+                          uint32_t *tokens, int *counts, long *total, void *stream);
+/* Parakeet::transcribe (src/parakeet.rs:842-867) without biasing or detokenising, for a batch:
+ * front end, encoder, greedy TDT decoding. samples, lengths and frames as
+ * telmo_granite_transcribe takes them; tokens (host) receives the triples packed as
+ * telmo_parakeet_decode packs them (size it for 3 * max_symbols * the sum of
+ * telmo_parakeet_frames_for_samples(lengths[u])), counts (host) their numbers. */
+int telmo_parakeet_transcribe(telmo_parakeet *p, const float *samples, const int64_t *lengths,
+                              int n_utt, uint32_t *tokens, int *counts, int *frames,
+                              void *stream);
+/* The same with samples, tokens and counts in device memory (lengths and frames on the host). */
+int telmo_parakeet_transcribe_device(telmo_parakeet *p, const float *samples,
+                                     const int64_t *lengths, int n_utt, uint32_t *tokens,
+                                     int *counts, int *frames, void *stream);
+/* CUDA kernels this model has launched so far (front end included). */
+long telmo_parakeet_launches(const telmo_parakeet *p);
+/* Per-class timing as telmo_granite_profile / telmo_granite_profile_read give it. */
+int telmo_parakeet_profile(telmo_parakeet *p, int enable);
+int telmo_parakeet_profile_read(telmo_parakeet *p, double *ms, long *launches, double *gemm_ops,
+                                double *gemm_bytes);
+
 #ifdef __cplusplus
 }
 #endif

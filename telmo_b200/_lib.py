@@ -60,6 +60,20 @@ SIGNATURES = {
     "telmo_granite_launches": (_c.c_long, [_vp]),
     "telmo_granite_profile": (_int, [_vp, _int]),
     "telmo_granite_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),
+    "telmo_parakeet_create": (_int, [_vp, _vp, _c.POINTER(_vp)]),
+    "telmo_parakeet_free": (None, [_vp]),
+    "telmo_parakeet_set_matrix": (_int, [_vp, _c.c_char_p, _int, _sz, _sz, _vp, _vp]),
+    "telmo_parakeet_set_vector": (_int, [_vp, _c.c_char_p, _sz, _vp]),
+    "telmo_parakeet_finalize": (_int, [_vp]),
+    "telmo_parakeet_frames_for": (_sz, [_sz]),
+    "telmo_parakeet_frames_for_samples": (_sz, [_c.c_int64]),
+    "telmo_parakeet_encode": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp]),
+    "telmo_parakeet_decode": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_parakeet_transcribe": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_parakeet_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_parakeet_launches": (_c.c_long, [_vp]),
+    "telmo_parakeet_profile": (_int, [_vp, _int]),
+    "telmo_parakeet_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),
 }
 
 FRONTEND_GRANITE = 0
@@ -72,6 +86,15 @@ class GraniteConfig(ctypes.Structure):
         "d_model", "heads", "head_dim", "layers", "ff", "conv_kernel", "conv_channels", "n_mels",
         "context", "max_relative", "n_subsample")] + [
         ("subsample_layers", ctypes.c_int * 8), ("vocab", ctypes.c_int), ("blank", ctypes.c_int)]
+
+
+class ParakeetConfig(ctypes.Structure):
+    """telmo_parakeet_config (include/telmo_b200.h)."""
+    _fields_ = [(name, ctypes.c_int) for name in (
+        "d_model", "heads", "layers", "ff", "conv_kernel", "sub_channels", "n_mels", "pred_hidden",
+        "pred_layers", "vocab", "blank", "n_durations")] + [
+        ("durations", ctypes.c_int * 8), ("max_symbols", ctypes.c_int)]
+
 
 _lib = None
 

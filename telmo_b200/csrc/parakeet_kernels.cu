@@ -1,0 +1,531 @@
+// parakeet_kernels.cu -- the Parakeet-specific kernels: the subsampling convolutions, the
+// relative position table, Transformer-XL attention over a whole utterance and the steps of
+// batched greedy TDT decoding.
+//
+// Arithmetic follows the reference: conv3x3s2_row (src/kernels/scalar.rs:194-232) starts from
+// the bias and adds taps dt-major with separate rounding; positions (src/parakeet.rs:1618-1630)
+// in f64; attention (src/parakeet.rs:1176-1282) sums every dot product over ascending d (or j)
+// with fused multiply-adds, adds the shifted position score before scaling, and takes the
+// softmax with f32 exponentials and an f64 sum; the LSTM (src/parakeet.rs:1524-1577) uses
+// sigmoid = 1 / (1 + e^-x) and tanh in f32.
+#include "parakeet_kernels.h"
+
+#include <cmath>
+
+namespace telmo {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float madd(float acc, float w, float v) { return __fadd_rn(acc, __fmul_rn(w, v)); }
+
+// conv0 (1 -> ch, 3x3, stride 2, zero padding 1) + ReLU at (t1, f1) for channel c, from the
+// staged feature rows (row t0 of the utterance at stage[(t0 - t0_base) * f0]).
+__device__ __forceinline__ float conv0_at(const float* stage, int t0_base, int t0_count, int f0, int t1, int f1,
+                                          const float* w0, const float* b0, int ch, int c) {
+    float o = b0[c];
+#pragma unroll
+    for (int dt = 0; dt < 3; ++dt) {
+        const int t0 = 2 * t1 + dt - 1;
+        if (t0 < 0 || t0 - t0_base >= t0_count) continue;
+#pragma unroll
+        for (int df = 0; df < 3; ++df) {
+            const int ff = 2 * f1 + df - 1;
+            if (ff < 0 || ff >= f0) continue;
+            o = madd(o, w0[(dt * 3 + df) * ch + c], stage[(t0 - t0_base) * f0 + ff]);
+        }
+    }
+    return fmaxf(o, 0.0f);
+}
+
+}  // namespace
+
+// Fused conv0 + ReLU + depthwise conv1 (Parakeet::subsample's first two convolutions,
+// src/parakeet.rs:937-941). One CTA per (span of output rows t2, block of 128 channels); the
+// conv0 values each depthwise output reads are recomputed (about 2.3x) instead of being stored.
+__global__ void __launch_bounds__(128) sub_front_kernel(const float* __restrict__ feats, int f0,
+                                                        const SubTask* __restrict__ tasks, int ch,
+                                                        const float* __restrict__ w0, const float* __restrict__ b0,
+                                                        const float* __restrict__ w1, const float* __restrict__ b1,
+                                                        float* __restrict__ out) {
+    extern __shared__ float stage[];
+    const SubTask t = tasks[blockIdx.x];
+    const int c = blockIdx.y * 128 + threadIdx.x;
+    const int f1n = (f0 - 1) / 2 + 1, f2n = (f1n - 1) / 2 + 1;
+    const int t1n = (t.t0 - 1) / 2 + 1;
+    // Feature rows the span reads: t1 in [2 t2_first - 1, 2 t2_last + 1], t0 = 2 t1 - 1 .. 2 t1 + 1.
+    const int t0_base = max(0, 4 * t.t2_first - 3);
+    const int t0_last = min(t.t0 - 1, 4 * (t.t2_first + t.t2_count - 1) + 3);
+    const int rows = t0_last - t0_base + 1;
+    for (int i = threadIdx.x; i < rows * f0; i += 128) stage[i] = feats[static_cast<int64_t>(t.feat_row + t0_base) * f0 + i];
+    __syncthreads();
+    if (c >= ch) return;
+    for (int t2 = t.t2_first; t2 < t.t2_first + t.t2_count; ++t2) {
+        for (int f2 = 0; f2 < f2n; ++f2) {
+            float acc = b1[c];
+#pragma unroll
+            for (int dt = 0; dt < 3; ++dt) {
+                const int t1 = 2 * t2 + dt - 1;
+                if (t1 < 0 || t1 >= t1n) continue;
+#pragma unroll
+                for (int df = 0; df < 3; ++df) {
+                    const int f1 = 2 * f2 + df - 1;
+                    if (f1 < 0 || f1 >= f1n) continue;
+                    const float h = conv0_at(stage, t0_base, rows, f0, t1, f1, w0, b0, ch, c);
+                    acc = madd(acc, w1[(dt * 3 + df) * ch + c], h);
+                }
+            }
+            out[(static_cast<int64_t>(t.out_row) + static_cast<int64_t>(t2 - t.t2_first) * f2n + f2) * ch + c] = acc;
+        }
+    }
+}
+
+// Depthwise 3x3 stride-2 convolution over [t_in, f_in, ch] rows of one utterance (conv3x3s2_row
+// with depthwise, src/kernels/scalar.rs:194-232). One CTA per (task, channel block).
+__global__ void __launch_bounds__(128) dw3x3s2_kernel(const float* __restrict__ in, int f_in, const SubTask* __restrict__ tasks,
+                                                      int ch, const float* __restrict__ w, const float* __restrict__ b,
+                                                      float* __restrict__ out) {
+    const SubTask t = tasks[blockIdx.x];
+    const int c = blockIdx.y * 128 + threadIdx.x;
+    if (c >= ch) return;
+    const int f_out = (f_in - 1) / 2 + 1;
+    const int t_in = t.t0;
+    for (int to = t.t2_first; to < t.t2_first + t.t2_count; ++to) {
+        for (int fo = 0; fo < f_out; ++fo) {
+            float acc = b[c];
+#pragma unroll
+            for (int dt = 0; dt < 3; ++dt) {
+                const int ti = 2 * to + dt - 1;
+                if (ti < 0 || ti >= t_in) continue;
+#pragma unroll
+                for (int df = 0; df < 3; ++df) {
+                    const int fi = 2 * fo + df - 1;
+                    if (fi < 0 || fi >= f_in) continue;
+                    acc = madd(acc, w[(dt * 3 + df) * ch + c],
+                               in[(static_cast<int64_t>(t.feat_row) + static_cast<int64_t>(ti) * f_in + fi) * ch + c]);
+                }
+            }
+            out[(static_cast<int64_t>(t.out_row) + static_cast<int64_t>(to - t.t2_first) * f_out + fo) * ch + c] = acc;
+        }
+    }
+}
+
+// positions (src/parakeet.rs:1618-1630): row r of [2t - 1, d] is position t - 1 - r, sine and
+// cosine interleaved. A row depends only on its position, so the table of a shorter utterance
+// of t' frames is rows t - t' .. t + t' - 2 of this one.
+__global__ void positions_kernel(int t, int d, float* __restrict__ out) {
+    const int r = blockIdx.x;
+    if (r >= 2 * t - 1) return;
+    const double p = static_cast<double>(t) - 1.0 - static_cast<double>(r);
+    float* row = out + static_cast<int64_t>(r) * d;
+    const double lg = log(10000.0) / static_cast<double>(d);
+    for (int i = threadIdx.x; i < d / 2; i += blockDim.x) {
+        const double freq = exp(-static_cast<double>(2 * i) * lg);
+        const double angle = p * freq;
+        row[2 * i] = static_cast<float>(sin(angle));
+        row[2 * i + 1] = static_cast<float>(cos(angle));
+    }
+}
+
+// Transformer-XL attention of one head over one utterance, for 32 query rows per CTA:
+//   S[i][j] = ((q_i + u) . k_j + (q_i + v) . p_{t-1-i+j}) * scale,  P = softmax_j(S),  O = P . V
+// with p the projected position rows of the utterance (2t - 1 of them). 256 threads; S lives in
+// shared memory ([32][t]); K, positions and V pass through in chunks of 32 rows.
+template <int HD>
+__global__ void __launch_bounds__(256) txl_attention_kernel(const float* __restrict__ qkv, const float* __restrict__ pp,
+                                                            const TxlTask* __restrict__ tasks, int heads,
+                                                            const float* __restrict__ bias_u,
+                                                            const float* __restrict__ bias_v, float scale,
+                                                            float* __restrict__ att) {
+    constexpr int R = 32, CH = 32;
+    extern __shared__ float sm[];
+    const TxlTask task = tasks[blockIdx.x];
+    const int h = blockIdx.y;
+    const int t = task.len, i0 = task.q_first;
+    const int rows = min(R, t - i0);
+    const int D = heads * HD;
+    const int64_t ld = 3 * static_cast<int64_t>(D);
+    const float* base = qkv + static_cast<int64_t>(task.row) * ld + h * HD;
+    const float* pbase = pp + static_cast<int64_t>(task.pos_row) * D + h * HD;
+    const int tp = (t + 3) / 4 * 4;  // pitch of S
+    float* qu = sm;                  // [R][HD + 1]
+    float* qv = qu + R * (HD + 1);   // [R][HD + 1]
+    float* chunk = qv + R * (HD + 1);  // [CH][HD + 1]
+    float* S = chunk + CH * (HD + 1);  // [R][tp]
+    const int tid = threadIdx.x;
+
+    for (int e = tid; e < R * HD; e += 256) {
+        const int r = e / HD, dd = e % HD;
+        float q = r < rows ? base[static_cast<int64_t>(i0 + r) * ld + dd] : 0.0f;
+        qu[r * (HD + 1) + dd] = __fadd_rn(q, bias_u[h * HD + dd]);
+        qv[r * (HD + 1) + dd] = __fadd_rn(q, bias_v[h * HD + dd]);
+    }
+    // Each thread computes 4 (row, column) pairs of a 32 x 32 output chunk.
+    const int cr = tid / 8;         // row 0..31
+    const int cc = (tid % 8) * 4;   // columns cc .. cc + 3
+
+    // ---- content scores against every key ----------------------------------------------------
+    for (int j0 = 0; j0 < t; j0 += CH) {
+        __syncthreads();
+        for (int e = tid; e < CH * HD; e += 256) {
+            const int j = e / HD, dd = e % HD;
+            chunk[j * (HD + 1) + dd] = j0 + j < t ? base[static_cast<int64_t>(j0 + j) * ld + D + dd] : 0.0f;
+        }
+        __syncthreads();
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        const float* q = qu + cr * (HD + 1);
+        for (int dd = 0; dd < HD; ++dd) {
+            const float qd = q[dd];
+            a0 = __fmaf_rn(qd, chunk[(cc + 0) * (HD + 1) + dd], a0);
+            a1 = __fmaf_rn(qd, chunk[(cc + 1) * (HD + 1) + dd], a1);
+            a2 = __fmaf_rn(qd, chunk[(cc + 2) * (HD + 1) + dd], a2);
+            a3 = __fmaf_rn(qd, chunk[(cc + 3) * (HD + 1) + dd], a3);
+        }
+        const float a[4] = {a0, a1, a2, a3};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (j0 + cc + e < t) S[cr * tp + j0 + cc + e] = a[e];
+    }
+    // ---- position scores: row i reads position index t - 1 - i + j ------------------------------
+    // The block's rows need indices from t - 1 - (i0 + rows - 1) to t - 1 - i0 + t - 1.
+    const int p_lo = t - 1 - (i0 + rows - 1), p_hi = 2 * t - 2 - i0;
+    for (int p0 = p_lo; p0 <= p_hi; p0 += CH) {
+        __syncthreads();
+        for (int e = tid; e < CH * HD; e += 256) {
+            const int j = e / HD, dd = e % HD;
+            chunk[j * (HD + 1) + dd] = p0 + j <= p_hi ? pbase[static_cast<int64_t>(p0 + j) * D + dd] : 0.0f;
+        }
+        __syncthreads();
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        const float* q = qv + cr * (HD + 1);
+        for (int dd = 0; dd < HD; ++dd) {
+            const float qd = q[dd];
+            a0 = __fmaf_rn(qd, chunk[(cc + 0) * (HD + 1) + dd], a0);
+            a1 = __fmaf_rn(qd, chunk[(cc + 1) * (HD + 1) + dd], a1);
+            a2 = __fmaf_rn(qd, chunk[(cc + 2) * (HD + 1) + dd], a2);
+            a3 = __fmaf_rn(qd, chunk[(cc + 3) * (HD + 1) + dd], a3);
+        }
+        const float a[4] = {a0, a1, a2, a3};
+        const int i = i0 + cr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int pidx = p0 + cc + e;
+            const int j = pidx - (t - 1 - i);
+            if (cr < rows && pidx <= p_hi && j >= 0 && j < t)
+                S[cr * tp + j] = __fmul_rn(__fadd_rn(S[cr * tp + j], a[e]), scale);
+        }
+    }
+    __syncthreads();
+    // ---- softmax per row (8 warps x 4 rows) ------------------------------------------------------
+    const int warp = tid / 32, lane = tid % 32;
+    for (int r = warp; r < R; r += 8) {
+        if (r >= rows) continue;
+        float* row = S + r * tp;
+        float mx = -INFINITY;
+        for (int j = lane; j < t; j += 32) mx = fmaxf(mx, row[j]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        double sum = 0.0;
+        for (int j = lane; j < t; j += 32) {
+            const float e = expf(__fsub_rn(row[j], mx));
+            row[j] = e;
+            sum += static_cast<double>(e);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
+        const float inv = static_cast<float>(1.0 / sum);
+        for (int j = lane; j < t; j += 32) row[j] = __fmul_rn(row[j], inv);
+    }
+    // ---- O = P . V over ascending keys: each thread owns (row cr, 4 columns per 32-column group) --
+    constexpr int G = HD / 32;
+    float o[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.0f;
+    for (int j0 = 0; j0 < t; j0 += CH) {
+        __syncthreads();
+        for (int e = tid; e < CH * HD; e += 256) {
+            const int j = e / HD, dd = e % HD;
+            chunk[j * (HD + 1) + dd] = j0 + j < t ? base[static_cast<int64_t>(j0 + j) * ld + 2 * D + dd] : 0.0f;
+        }
+        __syncthreads();
+        const int jn = min(CH, t - j0);
+        for (int j = 0; j < jn; ++j) {
+            const float pj = S[cr * tp + j0 + j];
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[g][e] = __fmaf_rn(pj, chunk[j * (HD + 1) + g * 32 + cc + e], o[g][e]);
+        }
+    }
+    if (cr < rows) {
+        float* orow = att + static_cast<int64_t>(task.row + i0 + cr) * D + h * HD;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) orow[g * 32 + cc + e] = o[g][e];
+    }
+}
+
+// ---- greedy TDT steps (decode_inner, src/parakeet.rs:1412-1513) --------------------------------
+
+// z[u] = relu(enc_proj[frame row of u] + pred[u]) for every utterance still decoding.
+__global__ void tdt_joint_input_kernel(const float* __restrict__ enc_proj, const TdtState* __restrict__ st, int n_utt,
+                                       int h, const float* __restrict__ pred, float* __restrict__ z) {
+    const int u = blockIdx.x;
+    if (u >= n_utt) return;
+    const TdtState s = st[u];
+    if (s.t >= s.frames) return;  // finished: its row of z is not read
+    const int64_t row = static_cast<int64_t>(s.enc_first) + s.t;
+    for (int j = threadIdx.x; j < h; j += blockDim.x)
+        z[static_cast<int64_t>(u) * h + j] =
+            fmaxf(__fadd_rn(enc_proj[row * h + j], pred[static_cast<int64_t>(u) * h + j]), 0.0f);
+}
+
+// The token and duration choices of one joint step and the state machine after them: blank ->
+// advance by max(duration, 1); a token -> emit it, predict next, advance by its duration or,
+// for duration 0, count symbols on this frame up to max_symbols. One warp per utterance.
+__global__ void tdt_decide_kernel(const float* __restrict__ logits, int64_t ld, int vocab, int blank,
+                                  const int* __restrict__ durations, int n_dur, int max_symbols,
+                                  TdtState* __restrict__ st, int n_utt, uint32_t* __restrict__ tokens,
+                                  int* __restrict__ predict_token, int* __restrict__ active) {
+    const int u = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (u >= n_utt) return;
+    TdtState s = st[u];
+    if (s.t >= s.frames) {
+        if (lane == 0) predict_token[u] = -1;
+        return;
+    }
+    const float* row = logits + static_cast<int64_t>(u) * ld;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = lane; i < vocab; i += 32) {
+        const float v = row[i];
+        if (v > best) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, best, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane != 0) return;
+    int di = 0;
+    for (int i = 1; i < n_dur; ++i)
+        if (row[vocab + i] > row[vocab + di]) di = i;
+    const int duration = durations[di];
+    int tok = -1;
+    if (bi == blank) {
+        s.t += duration > 1 ? duration : 1;
+        s.on_frame = 0;
+    } else {
+        uint32_t* out = tokens + 3 * static_cast<int64_t>(s.tok_first + s.count);
+        out[0] = static_cast<uint32_t>(bi);
+        out[1] = static_cast<uint32_t>(s.t);
+        out[2] = static_cast<uint32_t>(duration);
+        s.count += 1;
+        tok = bi;
+        if (duration > 0) {
+            s.t += duration;
+            s.on_frame = 0;
+        } else {
+            s.on_frame += 1;
+            if (s.on_frame >= max_symbols) {
+                s.t += 1;
+                s.on_frame = 0;
+            }
+        }
+    }
+    st[u] = s;
+    predict_token[u] = tok;
+    if (s.t < s.frames) atomicAdd(active, 1);
+}
+
+// The LSTM layer's input [x | h_l] for every utterance that predicts: x is the token's
+// embedding for layer 0, else the previous layer's new hidden state.
+__global__ void lstm_input_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layer, int layers,
+                                  const float* __restrict__ embedding, const float* __restrict__ state,
+                                  float* __restrict__ input) {
+    const int u = blockIdx.x;
+    if (u >= n_utt || predict_token[u] < 0) return;
+    const float* st = state + static_cast<int64_t>(u) * layers * 2 * h;
+    float* in = input + static_cast<int64_t>(u) * 2 * h;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) {
+        in[j] = layer == 0 ? embedding[static_cast<int64_t>(predict_token[u]) * h + j] : st[(layer - 1) * 2 * h + j];
+        in[h + j] = st[layer * 2 * h + j];
+    }
+}
+
+// c = f c + i g, h = o tanh(c) for the utterances that predict; other states stay.
+__global__ void lstm_cell_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layer, int layers,
+                                 const float* __restrict__ gates, float* __restrict__ state) {
+    const int u = blockIdx.x;
+    if (u >= n_utt || predict_token[u] < 0) return;
+    const float* g = gates + static_cast<int64_t>(u) * 4 * h;
+    float* hs = state + static_cast<int64_t>(u) * layers * 2 * h + layer * 2 * h;
+    float* cs = hs + h;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) {
+        const float i = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[j])));
+        const float f = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[h + j])));
+        const float gg = tanhf(g[2 * h + j]);
+        const float o = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[3 * h + j])));
+        const float c = __fadd_rn(__fmul_rn(f, cs[j]), __fmul_rn(i, gg));
+        cs[j] = c;
+        hs[j] = __fmul_rn(o, tanhf(c));
+    }
+}
+
+// The last layer's hidden states of the predicting utterances, gathered for pred_proj.
+__global__ void lstm_last_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layers,
+                                 const float* __restrict__ state, float* __restrict__ last) {
+    const int u = blockIdx.x;
+    if (u >= n_utt) return;
+    const float* hs = state + static_cast<int64_t>(u) * layers * 2 * h + (layers - 1) * 2 * h;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) last[static_cast<int64_t>(u) * h + j] = hs[j];
+}
+
+// The start of decoding (initial_decoder_state, src/parakeet.rs:1321-1336): every utterance
+// feeds the blank token to a zero LSTM state.
+__global__ void tdt_start_kernel(int n_utt, int blank, int* __restrict__ predict_token) {
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u < n_utt) predict_token[u] = blank;
+}
+
+// Moves each utterance's tokens from its worst-case slot (3 * tok_first words in) to the prefix
+// sum of the counts before it; counts[u] gets its count and *total the sum. One CTA: thread 0
+// forms the prefix sums in `offsets`, then every warp copies whole utterances.
+__global__ void __launch_bounds__(1024) tdt_compact_kernel(const uint32_t* __restrict__ raw,
+                                                           const TdtState* __restrict__ st, int n_utt,
+                                                           int* __restrict__ offsets, uint32_t* __restrict__ out,
+                                                           int* __restrict__ counts, int* __restrict__ total) {
+    if (threadIdx.x == 0) {
+        int at = 0;
+        for (int u = 0; u < n_utt; ++u) {
+            offsets[u] = at;
+            at += st[u].count;
+        }
+        *total = at;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    for (int u = warp; u < n_utt; u += blockDim.x / 32) {
+        const TdtState s = st[u];
+        const uint32_t* src = raw + 3 * static_cast<int64_t>(s.tok_first);
+        uint32_t* dst = out + 3 * static_cast<int64_t>(offsets[u]);
+        for (int i = lane; i < 3 * s.count; i += 32) dst[i] = src[i];
+        if (lane == 0) counts[u] = s.count;
+    }
+}
+
+// pred[u] = the new projection for utterances that predicted.
+__global__ void pred_commit_kernel(const int* __restrict__ predict_token, int n_utt, int h,
+                                   const float* __restrict__ fresh, float* __restrict__ pred) {
+    const int u = blockIdx.x;
+    if (u >= n_utt || predict_token[u] < 0) return;
+    for (int j = threadIdx.x; j < h; j += blockDim.x)
+        pred[static_cast<int64_t>(u) * h + j] = fresh[static_cast<int64_t>(u) * h + j];
+}
+
+// ---- launchers ---------------------------------------------------------------------------------
+
+cudaError_t sub_front(const float* feats, int f0, const SubTask* tasks, int n_tasks, int ch, const float* w0,
+                      const float* b0, const float* w1, const float* b1, float* out, int max_t2_span,
+                      cudaStream_t s) {
+    if (n_tasks <= 0) return cudaSuccess;
+    const int rows = 4 * max_t2_span + 3;
+    const size_t smem = sizeof(float) * rows * f0;
+    dim3 grid(n_tasks, (ch + 127) / 128);
+    sub_front_kernel<<<grid, 128, smem, s>>>(feats, f0, tasks, ch, w0, b0, w1, b1, out);
+    return cudaGetLastError();
+}
+
+cudaError_t dw3x3s2(const float* in, int f_in, const SubTask* tasks, int n_tasks, int ch, const float* w,
+                    const float* b, float* out, cudaStream_t s) {
+    if (n_tasks <= 0) return cudaSuccess;
+    dim3 grid(n_tasks, (ch + 127) / 128);
+    dw3x3s2_kernel<<<grid, 128, 0, s>>>(in, f_in, tasks, ch, w, b, out);
+    return cudaGetLastError();
+}
+
+cudaError_t positions(int t, int d, float* out, cudaStream_t s) {
+    if (t <= 0) return cudaSuccess;
+    positions_kernel<<<2 * t - 1, 128, 0, s>>>(t, d, out);
+    return cudaGetLastError();
+}
+
+size_t txl_attention_smem(int hd, int max_t) {
+    return sizeof(float) * (2 * 32 * (hd + 1) + 32 * (hd + 1) + 32 * ((max_t + 3) / 4 * 4));
+}
+
+cudaError_t txl_attention(const float* qkv, const float* pp, const TxlTask* tasks, int n_tasks, int heads, int hd,
+                          int max_t, const float* bias_u, const float* bias_v, float scale, float* att,
+                          cudaStream_t s) {
+    if (n_tasks <= 0) return cudaSuccess;
+    const size_t smem = txl_attention_smem(hd, max_t);
+    dim3 grid(n_tasks, heads);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    auto launch = [&](auto kernel) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        kernel<<<grid, 256, smem, s>>>(qkv, pp, tasks, heads, bias_u, bias_v, scale, att);
+        return cudaGetLastError();
+    };
+    switch (hd) {
+        case 32: return launch(txl_attention_kernel<32>);
+        case 64: return launch(txl_attention_kernel<64>);
+        case 128: return launch(txl_attention_kernel<128>);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t tdt_joint_input(const float* enc_proj, const TdtState* st, int n_utt, int h, const float* pred, float* z,
+                            cudaStream_t s) {
+    tdt_joint_input_kernel<<<n_utt, 128, 0, s>>>(enc_proj, st, n_utt, h, pred, z);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_decide(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
+                       int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
+                       cudaStream_t s) {
+    tdt_decide_kernel<<<(n_utt + 3) / 4, 128, 0, s>>>(logits, ld, vocab, blank, durations, n_dur, max_symbols, st, n_utt,
+                                                       tokens, predict_token, active);
+    return cudaGetLastError();
+}
+
+cudaError_t lstm_input(const int* predict_token, int n_utt, int h, int layer, int layers, const float* embedding,
+                       const float* state, float* input, cudaStream_t s) {
+    lstm_input_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layer, layers, embedding, state, input);
+    return cudaGetLastError();
+}
+
+cudaError_t lstm_cell(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
+                      float* state, cudaStream_t s) {
+    lstm_cell_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layer, layers, gates, state);
+    return cudaGetLastError();
+}
+
+cudaError_t lstm_last(const int* predict_token, int n_utt, int h, int layers, const float* state, float* last,
+                      cudaStream_t s) {
+    lstm_last_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layers, state, last);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_start(int n_utt, int blank, int* predict_token, cudaStream_t s) {
+    tdt_start_kernel<<<(n_utt + 255) / 256, 256, 0, s>>>(n_utt, blank, predict_token);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int* offsets, uint32_t* out, int* counts,
+                        int* total, cudaStream_t s) {
+    tdt_compact_kernel<<<1, 1024, 0, s>>>(raw, st, n_utt, offsets, out, counts, total);
+    return cudaGetLastError();
+}
+
+cudaError_t pred_commit(const int* predict_token, int n_utt, int h, const float* fresh, float* pred, cudaStream_t s) {
+    pred_commit_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, fresh, pred);
+    return cudaGetLastError();
+}
+
+}  // namespace telmo

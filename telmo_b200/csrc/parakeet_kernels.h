@@ -1,0 +1,81 @@
+// parakeet_kernels.h -- launchers of the Parakeet-specific kernels (internal to libtelmo_b200).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace telmo {
+
+// One span of a stride-2 3x3 convolution over one utterance: output rows (time steps)
+// [t2_first, t2_first + t2_count) of the utterance whose input starts at row feat_row and has
+// t0 time steps; output time step r goes to out_row + (r - t2_first) * out_freqs.
+struct SubTask {
+    int feat_row, t0, t2_first, t2_count, out_row;
+};
+
+// Query rows [q_first, q_first + 32) of one utterance of len frames whose rows start at row and
+// whose projected positions start at row pos_row of the position projection.
+struct TxlTask {
+    int row, len, q_first, pos_row;
+};
+
+// Greedy TDT decoding state of one utterance: encoder rows enc_first .. + frames - 1, the next
+// frame t, tokens emitted on t so far, where its tokens go and how many it has emitted.
+struct TdtState {
+    int enc_first, frames, t, on_frame, tok_first, count;
+};
+
+// Fused conv0 (1 -> ch, ReLU) + depthwise conv1 over features [rows, f0]; out [t2 * f2, ch]
+// per task. max_t2_span bounds every task's t2_count (it sizes the staged feature rows).
+cudaError_t sub_front(const float* feats, int f0, const SubTask* tasks, int n_tasks, int ch, const float* w0,
+                      const float* b0, const float* w1, const float* b1, float* out, int max_t2_span,
+                      cudaStream_t s);
+
+// Depthwise 3x3 stride-2 convolution: in [t0 * f_in, ch] per task (task.t0 input time steps)
+// -> out [count * f_out, ch].
+cudaError_t dw3x3s2(const float* in, int f_in, const SubTask* tasks, int n_tasks, int ch, const float* w,
+                    const float* b, float* out, cudaStream_t s);
+
+// The relative position table for t frames, out [2t - 1, d]; an utterance of t' <= t frames
+// uses its rows t - t' .. t + t' - 2.
+cudaError_t positions(int t, int d, float* out, cudaStream_t s);
+
+// Transformer-XL relative attention (src/parakeet.rs:1176-1282) of every task and head: qkv
+// [rows, 3 d] f32, pp the projected positions [*, d], att [rows, d]. hd is 32, 64 or 128.
+size_t txl_attention_smem(int hd, int max_t);
+cudaError_t txl_attention(const float* qkv, const float* pp, const TxlTask* tasks, int n_tasks, int heads, int hd,
+                          int max_t, const float* bias_u, const float* bias_v, float scale, float* att,
+                          cudaStream_t s);
+
+// z[u] = relu(enc_proj[u's current frame] + pred[u]), z [n_utt, h].
+cudaError_t tdt_joint_input(const float* enc_proj, const TdtState* st, int n_utt, int h, const float* pred, float* z,
+                            cudaStream_t s);
+
+// Token and duration choice from logits [n_utt, ld] and the state step after it; tokens are
+// (id, frame, duration) triples; predict_token[u] is the token to feed the prediction network
+// or -1; *active counts the utterances with frames left afterwards.
+cudaError_t tdt_decide(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
+                       int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
+                       cudaStream_t s);
+
+// LSTM layer input [x | h_layer] (x the token's embedding, or the layer below's new hidden state)
+// for the utterances with predict_token >= 0; state [n_utt, layers, 2, h] (hidden, cell).
+cudaError_t lstm_input(const int* predict_token, int n_utt, int h, int layer, int layers, const float* embedding,
+                       const float* state, float* input, cudaStream_t s);
+// The LSTM cell update from gates [n_utt, 4h] (i, f, g, o) for predicting utterances.
+cudaError_t lstm_cell(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
+                      float* state, cudaStream_t s);
+// last[u] = the top layer's hidden state.
+cudaError_t lstm_last(const int* predict_token, int n_utt, int h, int layers, const float* state, float* last,
+                      cudaStream_t s);
+// predict_token[u] = blank for every utterance (the start of decoding).
+cudaError_t tdt_start(int n_utt, int blank, int* predict_token, cudaStream_t s);
+// Tokens from each utterance's worst-case slot (3 * tok_first words into raw) to consecutive
+// places in out (prefix sums of the counts, kept in offsets [n_utt]); counts[u] and *total.
+cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int* offsets, uint32_t* out, int* counts,
+                        int* total, cudaStream_t s);
+// pred[u] = fresh[u] for predicting utterances.
+cudaError_t pred_commit(const int* predict_token, int n_utt, int h, const float* fresh, float* pred, cudaStream_t s);
+
+}  // namespace telmo

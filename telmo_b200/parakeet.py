@@ -1,0 +1,187 @@
+"""The Parakeet TDT model on the GPU: the reference's Parakeet interface (src/parakeet.rs) over
+the C ABI.
+
+``Parakeet.from_entries`` plays the part of ``Parakeet::from_pack`` (named pack entries), and
+``encode`` / ``decode`` / ``transcribe`` mirror the reference's methods, extended to batches of
+utterances whose rows are packed one after another.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import List, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import TelmoError, check
+from .granite import Token, _stream
+
+
+def config_struct(config: dict) -> _lib.ParakeetConfig:
+    cfg = _lib.ParakeetConfig()
+    for key in ("d_model", "heads", "layers", "ff", "conv_kernel", "sub_channels", "n_mels",
+                "pred_hidden", "pred_layers", "vocab", "blank", "max_symbols"):
+        setattr(cfg, key, int(config[key]))
+    durations = list(config["durations"])
+    if len(durations) > 8:
+        raise TelmoError(_lib.TELMO_ERR_UNSUPPORTED, "more than 8 durations")
+    cfg.n_durations = len(durations)
+    for i, x in enumerate(durations):
+        cfg.durations[i] = int(x)
+    return cfg
+
+
+def frames_for(feature_frames: int) -> int:
+    """Encoder frames for a number of feature frames (three stride-2 convolutions)."""
+    return _lib.load().telmo_parakeet_frames_for(int(feature_frames))
+
+
+def frames_for_samples(samples: int) -> int:
+    return _lib.load().telmo_parakeet_frames_for_samples(int(samples))
+
+
+class Parakeet:
+    """A loaded Parakeet TDT model on one context (src/parakeet.rs:315-327, :672-1596)."""
+
+    def __init__(self, ctx, config: dict):
+        self.ctx = ctx
+        self.config = dict(config)
+        h = ctypes.c_void_p()
+        cfg = config_struct(config)
+        check(_lib.load().telmo_parakeet_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)),
+              ctx.handle)
+        self._h = h
+
+    @staticmethod
+    def from_entries(ctx, config: dict, entries: dict) -> "Parakeet":
+        """Builds the model from named pack entries: matrices as (values, scales, n, k) in the
+        panel layout, vectors as f32 arrays (Parakeet::from_pack, src/parakeet.rs:691-795)."""
+        p = Parakeet(ctx, config)
+        L = _lib.load()
+        for name, entry in entries.items():
+            if isinstance(entry, tuple):
+                values, scales, n, k = entry
+                values = np.ascontiguousarray(values, dtype=np.int8)
+                scales = np.ascontiguousarray(scales, dtype=np.float32)
+                rc = L.telmo_parakeet_set_matrix(p._h, name.encode(), 3, n, k, values.ctypes.data,
+                                                 scales.ctypes.data)
+            else:
+                data = np.ascontiguousarray(entry, dtype=np.float32).reshape(-1)
+                rc = L.telmo_parakeet_set_vector(p._h, name.encode(), data.size, data.ctypes.data)
+            check(rc, ctx.handle)
+        check(L.telmo_parakeet_finalize(p._h), ctx.handle)
+        return p
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.load().telmo_parakeet_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, features, rows: Sequence[int], tap_layer: int = -1, stream=None):
+        """Parakeet::encode over a batch. ``features`` is a CUDA f32 tensor [sum(rows), n_mels];
+        tap_layer -2 stops after the subsampling, i >= 0 after layer i. Returns (encoded CUDA
+        tensor [sum(frames), d_model], frames per utterance)."""
+        import torch
+        rows_arr = np.ascontiguousarray(rows, dtype=np.int32)
+        n = rows_arr.size
+        total = sum(frames_for(int(r)) for r in rows_arr)
+        out = torch.empty((max(total, 1), self.config["d_model"]), dtype=torch.float32,
+                          device=features.device)
+        frames = np.zeros(n, np.int32)
+        check(_lib.load().telmo_parakeet_encode(self._h, features.data_ptr(), rows_arr.ctypes.data,
+                                                n, out.data_ptr(), frames.ctypes.data, tap_layer,
+                                                _stream(stream)), self.ctx.handle)
+        return out[:int(frames.sum())], frames
+
+    def decode_packed(self, encoded, frames: Sequence[int], stream=None):
+        """Greedy TDT decoding (Parakeet::decode, src/parakeet.rs:1285-1296) of a batch of
+        encoder outputs packed one after another; returns (tokens CUDA int32 [total, 3], counts
+        CUDA int32 [n], total)."""
+        import torch
+        frames_arr = np.ascontiguousarray(frames, dtype=np.int32)
+        n = frames_arr.size
+        cap = 3 * self.config["max_symbols"] * int(frames_arr.sum()) + 3
+        tokens = torch.zeros(cap, dtype=torch.int32, device=encoded.device)
+        counts = torch.zeros(max(n, 1), dtype=torch.int32, device=encoded.device)
+        total = ctypes.c_long(0)
+        check(_lib.load().telmo_parakeet_decode(self._h, encoded.data_ptr(), frames_arr.ctypes.data,
+                                                n, tokens.data_ptr(), counts.data_ptr(),
+                                                ctypes.byref(total), _stream(stream)),
+              self.ctx.handle)
+        return tokens[:3 * total.value].view(-1, 3), counts[:n], total.value
+
+    def decode(self, encoded, frames: Sequence[int], stream=None) -> List[List[Token]]:
+        """As decode_packed, split into each utterance's tokens."""
+        tokens, counts, _ = self.decode_packed(encoded, frames, stream)
+        return _split(tokens.cpu().numpy(), counts.cpu().numpy())
+
+    def transcribe(self, utterances: Sequence[np.ndarray], stream=None) -> List[List[Token]]:
+        """Parakeet::transcribe (src/parakeet.rs:842-867) up to the token ids, for a batch of
+        16 kHz utterances in host memory."""
+        lengths = np.array([len(u) for u in utterances], np.int64)
+        samples = np.ascontiguousarray(np.concatenate(utterances), dtype=np.float32)
+        return self.transcribe_packed(samples, lengths, stream)
+
+    def transcribe_packed(self, samples, lengths, stream=None, tokens_buf=None):
+        """As transcribe, with the utterances packed one after another in host memory (a pinned
+        buffer copies fastest)."""
+        lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+        n = lengths.size
+        cap = 3 * self.config["max_symbols"] * sum(frames_for_samples(int(x)) for x in lengths) + 3
+        tokens = tokens_buf if tokens_buf is not None else np.zeros(cap, np.uint32)
+        counts = np.zeros(n, np.int32)
+        frames = np.zeros(n, np.int32)
+        ptr = samples.data_ptr() if hasattr(samples, "data_ptr") else samples.ctypes.data
+        tptr = tokens.data_ptr() if hasattr(tokens, "data_ptr") else tokens.ctypes.data
+        check(_lib.load().telmo_parakeet_transcribe(self._h, ptr, lengths.ctypes.data, n, tptr,
+                                                    counts.ctypes.data, frames.ctypes.data,
+                                                    _stream(stream)), self.ctx.handle)
+        tok = tokens if isinstance(tokens, np.ndarray) else tokens.numpy()
+        return _split(tok.reshape(-1)[:3 * int(counts.sum())].reshape(-1, 3), counts)
+
+    def transcribe_device(self, samples, lengths, tokens, counts, stream=None):
+        """Device-resident variant: samples, tokens (int32, 3 * max_symbols * frames) and counts
+        are CUDA tensors; returns the host array of frames per utterance."""
+        lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+        frames = np.zeros(lengths.size, np.int32)
+        check(_lib.load().telmo_parakeet_transcribe_device(
+            self._h, samples.data_ptr(), lengths.ctypes.data, lengths.size, tokens.data_ptr(),
+            counts.data_ptr(), frames.ctypes.data, _stream(stream)), self.ctx.handle)
+        return frames
+
+    def launches(self) -> int:
+        return _lib.load().telmo_parakeet_launches(self._h)
+
+    def profile(self, enable: bool = True):
+        check(_lib.load().telmo_parakeet_profile(self._h, int(enable)), self.ctx.handle)
+
+    def profile_read(self):
+        """(ms[4], launches[4], gemm_ops, gemm_bytes) since the last read; classes as
+        telmo_granite_profile_read reports them."""
+        ms = (ctypes.c_double * 4)()
+        launches = (ctypes.c_long * 4)()
+        ops = ctypes.c_double(0.0)
+        byts = ctypes.c_double(0.0)
+        check(_lib.load().telmo_parakeet_profile_read(self._h, ms, launches, ctypes.byref(ops),
+                                                      ctypes.byref(byts)), self.ctx.handle)
+        return list(ms), list(launches), ops.value, byts.value
+
+
+def _split(tokens: np.ndarray, counts: np.ndarray) -> List[List[Token]]:
+    out, at = [], 0
+    for c in counts:
+        t = tokens[at:at + int(c)]
+        out.append([Token(int(a), int(b), int(d)) for a, b, d in t])
+        at += int(c)
+    return out
