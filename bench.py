@@ -10,6 +10,10 @@ Workloads (seeded synthetic data, telmo_b200/synthetic.py):
            ranks by longest-first greedy assignment (no collective; each rank keeps its tokens)
            and processed in length-sorted batches of up to --batch-seconds of audio. A step is
            one pass over the whole set. metric = RTFx (audio seconds / wall second), whole job.
+  parakeet config 4: 256 utterances, lengths uniform in 1-30 s (about 4,000 s of audio), through
+           the Parakeet-TDT-shaped int8 model: 128-bin log-mel, 8x convolutional subsampling,
+           24-layer FastConformer encoder, greedy TDT decoding (token and duration per step),
+           sharded and batched as granite.
   linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias.
 
 `--impl reference` times the reference's CPU path for the same workload: the oracle's C
@@ -195,6 +199,30 @@ class GraniteWorkload:
     def units_per_step(self):
         return self.rank_seconds
 
+    # -- per-kernel-class timing through the model's profiler -----------------------------------
+    def profile_start(self):
+        from telmo_b200 import _lib
+        L = _lib.load()
+        getattr(L, self.PROFILE)(self.model.handle, 1)
+        getattr(L, self.PROFILE + "_read")(self.model.handle, None, None, None, None)
+        self.launches0 = self.model.launches()
+
+    def profile_stop(self):
+        import ctypes
+        from telmo_b200 import _lib
+        L = _lib.load()
+        ms = (ctypes.c_double * 4)()
+        cnt = (ctypes.c_long * 4)()
+        ops, byt = ctypes.c_double(), ctypes.c_double()
+        getattr(L, self.PROFILE + "_read")(self.model.handle, ms, cnt, ctypes.byref(ops),
+                                           ctypes.byref(byt))
+        getattr(L, self.PROFILE)(self.model.handle, 0)
+        launches = self.model.launches() - self.launches0
+        return launches, {"gemm_ms": ms[0], "gemm_n": cnt[0], "attn_ms": ms[1], "attn_n": cnt[1],
+                          "rows_ms": ms[2], "fe_ms": ms[3], "ops": ops.value, "bytes": byt.value}
+
+    PROFILE = "telmo_granite_profile"
+
     # -- CPU reference ------------------------------------------------------------------------
     def cpu_sample_utts(self, target_s=24.0):
         """A bounded sample of the workload for the CPU path: the first utterances of the set
@@ -233,6 +261,94 @@ class GraniteWorkload:
         dt = time.perf_counter() - t0
         return self.cpu_seconds / dt, (f"{len(self.cpu_utts)} utterances of the set "
                                        f"({self.cpu_seconds:.1f} s of audio), features -> tokens")
+
+
+# ---------------------------------------------------------------------------------------------
+# config 4: the Parakeet-TDT-shaped model over 256 uniform utterances
+
+class ParakeetWorkload(GraniteWorkload):
+    name = "config4-parakeet-tdt"
+    metric = ("RTFx (audio-s per wall-s, whole job): Parakeet-TDT-shaped int8 model, "
+              "16 kHz audio -> log-mel -> 8x conv subsampling -> 24-layer FastConformer -> "
+              "greedy TDT tokens and durations")
+    PROFILE = "telmo_parakeet_profile"
+
+    # The whole set (about 4,240 s) fits one batch: every matrix product runs over all frames.
+    def __init__(self, rank, world, n_utt=256, batch_seconds=4500.0):
+        from telmo_b200 import sharding, synthetic
+        self.synthetic = synthetic
+        self.n_utt = n_utt
+        secs = synthetic.lengths_uniform(n_utt, 1.0, 30.0, seed=0)
+        self.samples = np.maximum((secs * SR).astype(np.int64), 2 * 160)
+        self.total_seconds = float(self.samples.sum()) / SR
+        mine = sharding.assign(self.samples, world)[rank]
+        self.batches = sharding.batches(mine, self.samples, batch_seconds)
+        self.mine = [u for b in self.batches for u in b]
+        self.rank_seconds = float(self.samples[self.mine].sum()) / SR
+        self.batch_seconds = batch_seconds
+        self.cfg = synthetic.parakeet_config()
+
+    def config(self, world):
+        c = dict(super().config(world))
+        c.update({"lengths": "uniform 1-30 s (seed 0)",
+                  "model": "Parakeet-TDT-shaped: 128 mels, 3 stride-2 convs x 256 ch, d 1024, "
+                           "24 layers, 8 heads x 128, ff 4096, conv k9, Transformer-XL positions; "
+                           "2-layer LSTM 640, joint 640 -> 8193 + 5 durations, max 10 symbols "
+                           "per frame; int8 weights (scales U(1e-3,1e-2))",
+                  "l2": "inputs larger than L2 (127 MB of audio, ~10 GB of activations per "
+                        "batch)"})
+        return c
+
+    def _entries(self):
+        return self.synthetic.parakeet_entries(self.cfg, seed=3, scales="spec")
+
+    def setup_gpu(self, ctx):
+        import torch
+        from telmo_b200.parakeet import Parakeet, frames_for_samples
+        self.model = Parakeet.from_entries(ctx, self.cfg, self._entries())
+        pool = self.make_pool()
+        audio = [self.utterance(u, pool) for u in self.mine]
+        del pool
+        packed = np.concatenate(audio) if audio else np.zeros(1, np.float32)
+        self.host_audio = torch.from_numpy(packed).pin_memory()
+        self.dev_audio = self.host_audio.cuda()
+        self.offsets = []
+        at = 0
+        for b in self.batches:
+            n = int(self.samples[b].sum())
+            self.offsets.append((at, n))
+            at += n
+        frames = max((sum(frames_for_samples(int(self.samples[u])) for u in b)
+                      for b in self.batches), default=1)
+        cap = 3 * self.cfg["max_symbols"] * frames + 3
+        self.dev_tokens = torch.empty(cap, dtype=torch.int32, device="cuda")
+        self.dev_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32,
+                                      device="cuda")
+        self.host_tokens = torch.empty(cap, dtype=torch.int32).pin_memory()
+        self.bi = int(packed.nbytes)
+        self.bo = 0
+
+    def step_e2e(self):
+        bo = 0
+        for b, (at, n) in zip(self.batches, self.offsets):
+            toks = self.model.transcribe_packed(self.host_audio[at:at + n], self.samples[b],
+                                                tokens_buf=self.host_tokens)
+            bo += 12 * sum(len(t) for t in toks) + 4 * len(b)
+        self.bo = bo
+        return toks
+
+    def cpu_setup(self):
+        from oracle import oracle
+        self.oracle = oracle
+        self.ref = oracle.Parakeet(self.cfg, self._entries())
+        pool = self.make_pool()
+        self.cpu_utts, self.cpu_seconds = self.cpu_sample_utts()
+        self.cpu_audio = [self.utterance(u, pool) for u in self.cpu_utts]
+
+    def cpu_step(self, threads):
+        for a in self.cpu_audio:
+            f = self.oracle.parakeet_features(a)
+            self.ref.decode(self.ref.encode(f, threads=threads), threads=threads)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -296,19 +412,21 @@ class LinearWorkload:
         return self.ops / best / 1e12, "config-1 product, best of 5"
 
 
-WORKLOADS = {"granite": GraniteWorkload, "linear": LinearWorkload}
+WORKLOADS = {"granite": GraniteWorkload, "parakeet": ParakeetWorkload, "linear": LinearWorkload}
+SPEECH = ("granite", "parakeet")
 
 
 def make_workload(args, rank, world):
     if args.workload == "granite":
-        return GraniteWorkload(rank, world, n_utt=args.utterances)
+        return GraniteWorkload(rank, world, n_utt=args.utterances or 4096)
+    if args.workload == "parakeet":
+        return ParakeetWorkload(rank, world, n_utt=args.utterances or 256)
     return WORKLOADS[args.workload](rank, world)
 
 
 def run_ours(args, rank, world, local_rank):
     import torch
     import telmo_b200
-    from telmo_b200 import _lib
     torch.cuda.set_device(local_rank)
     dist = None
     if world > 1:
@@ -320,7 +438,7 @@ def run_ours(args, rank, world, local_rank):
     ctx = telmo_b200.Context(local_rank)
     wl = make_workload(args, rank, world)
     wl.setup_gpu(ctx)
-    granite = args.workload == "granite"
+    speech = args.workload in SPEECH
 
     def barrier():
         if dist:
@@ -332,11 +450,8 @@ def run_ours(args, rank, world, local_rank):
         if hasattr(wl, "between_steps"):
             wl.between_steps()
     ctx.check()
-    if granite:
-        L = _lib.load()
-        L.telmo_granite_profile(wl.model.handle, 1)
-        L.telmo_granite_profile_read(wl.model.handle, None, None, None, None)
-        launches0 = wl.model.launches()
+    if speech:
+        wl.profile_start()
     clocks = Clocks(local_rank)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -353,17 +468,8 @@ def run_ours(args, rank, world, local_rank):
     ctx.check()
     step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     prof = None
-    if granite:
-        import ctypes
-        ms = (ctypes.c_double * 4)()
-        cnt = (ctypes.c_long * 4)()
-        ops, byt = ctypes.c_double(), ctypes.c_double()
-        L.telmo_granite_profile_read(wl.model.handle, ms, cnt, ctypes.byref(ops),
-                                     ctypes.byref(byt))
-        L.telmo_granite_profile(wl.model.handle, 0)
-        launches = wl.model.launches() - launches0
-        prof = {"gemm_ms": ms[0], "gemm_n": cnt[0], "attn_ms": ms[1], "attn_n": cnt[1],
-                "fe_ms": ms[3], "ops": ops.value, "bytes": byt.value}
+    if speech:
+        launches, prof = wl.profile_stop()
     else:
         launches = 2 * args.steps
     # e2e through the public call with host buffers.
@@ -390,7 +496,7 @@ def run_ours(args, rank, world, local_rank):
         pk, pk_src = peaks()
         value = total_units * args.steps / (step_ms / 1e3)
         e2e_value = total_units * args.steps / (e2e_ms / 1e3)
-        if granite:
+        if speech:
             avg = prof["gemm_ms"] / max(prof["gemm_n"], 1) / 1e3
             ops_launch = prof["ops"] / max(prof["gemm_n"], 1)
             achieved = ops_launch / avg / 1e12
@@ -404,6 +510,7 @@ def run_ours(args, rank, world, local_rank):
                         "is the bf16 one",
                         "time_share": {"gemm": round(prof["gemm_ms"] / step_ms, 3),
                                        "attention": round(prof["attn_ms"] / step_ms, 3),
+                                       "row_kernels_timed": round(prof["rows_ms"] / step_ms, 3),
                                        "front_end": round(prof["fe_ms"] / step_ms, 3)}}
         else:
             roofline = {"bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -413,7 +520,7 @@ def run_ours(args, rank, world, local_rank):
             "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(step_ms / args.steps, 3), "higher_is_better": True,
-            "scaling": "strong" if granite else "weak", "vs_baseline": None,
+            "scaling": "strong" if speech else "weak", "vs_baseline": None,
             "dtype": "int8 x int8 -> i32 (split-int8 activations), f32/f64 elsewhere",
             "data": "synthetic (seeded; telmo_b200/synthetic.py), random-init weights",
             "config": wl.config(world),
@@ -458,7 +565,7 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": wl.metric, "value": round(value, 3), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 2), "higher_is_better": True,
-        "scaling": "strong" if args.workload == "granite" else "weak", "vs_baseline": None,
+        "scaling": "strong" if args.workload in SPEECH else "weak", "vs_baseline": None,
         "dtype": "f32 (int8 weights widened), f64 statistics",
         "data": "synthetic (seeded; telmo_b200/synthetic.py), random-init weights",
         "config": wl.config(world),
@@ -477,8 +584,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="granite")
-    ap.add_argument("--utterances", type=int, default=4096,
-                    help="granite: utterances in the set (4096 is config 5; fewer for profiling)")
+    ap.add_argument("--utterances", type=int, default=0,
+                    help="utterances in the set (default: 4096 for granite, config 5; 256 for "
+                         "parakeet, config 4; fewer for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
