@@ -151,7 +151,7 @@ __device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
                  const __grid_constant__ CUtensorMap map_lo, const __grid_constant__ CUtensorMap map_out,
-                 const Params p) {
+                 const __grid_constant__ CUtensorMap map_out_lo, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + kStages * kStageBytes;
@@ -182,6 +182,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         prefetch_tensormap(&map_hi);
         prefetch_tensormap(&map_lo);
         if (p.out_path != kDirect) prefetch_tensormap(&map_out);
+        if (p.out_path != kDirect && p.out_kind == kOutF16Split) prefetch_tensormap(&map_out_lo);
     }
     if (warp == 1) {
         tmem_alloc(tmem_base_slot, kTmemCols);
@@ -322,7 +323,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     if (lane == 0 && x0 < p.n) {
                         if (p.out_path == kTmaReduce) tma_reduce_add_2d(&map_out, sbuf, x0, mc);
                         else tma_store_2d(&map_out, sbuf, x0, mc);
-                        if (p.out_kind == kOutF16Split) tma_store_2d(&map_out, sbuf + 32 * 32 * 2, x0, mc + p.m);
+                        if (p.out_kind == kOutF16Split) tma_store_2d(&map_out_lo, sbuf + 32 * 32 * 2, x0, mc);
                         bulk_commit();
                     }
                 } else if (p.out_kind == kOutF16Split) {
@@ -397,20 +398,20 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
     return r == CUDA_SUCCESS;
 }
 
-// The output tensor map: rows of n elements, ldc apart, 32 x 32 boxes without swizzle.
+// The output tensor map: m rows of n elements, ldc apart, 32 x 32 boxes without swizzle. Each
+// plane of the split output gets its own map, so TMA drops the rows of a partial chunk past m
+// instead of writing them into the other plane.
 bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t ldc) {
     auto fn = encode_fn();
     if (!fn) return false;
-    const bool split = kind == kOutF16Split;
-    const bool two = kind == kOutBF16 || split;
-    // The split output's two planes form one tensor of 2m rows.
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(split ? 2 * m : m)};
+    const bool two = kind == kOutBF16 || kind == kOutF16Split;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * (two ? 2 : 4)};
     cuuint32_t box[2] = {32, 32};
     cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapDataType type = kind == kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : split          ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const CUtensorMapDataType type = kind == kOutBF16        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : kind == kOutF16Split ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     CUresult r = fn(map, type, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -447,8 +448,9 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
         if (dev < 64) configured |= uint64_t(1) << dev;
     }
     // The output goes through TMA when its rows are 16-byte aligned.
-    CUtensorMap mo;
+    CUtensorMap mo, mo_lo;
     memset(&mo, 0, sizeof mo);
+    memset(&mo_lo, 0, sizeof mo_lo);
     int path = kDirect;
     const size_t esize = (g.out_kind == kOutBF16 || g.out_kind == kOutF16Split) ? 2 : 4;
     const bool aligned = (reinterpret_cast<uintptr_t>(g.out) % 16 == 0) && ((g.ldc * esize) % 16 == 0);
@@ -456,11 +458,15 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     if (aligned && (g.out_kind == kOutBF16 || g.out_kind == kOutF16Split) && !g.accumulate) path = kTmaStore;
     if (g.out_kind == kOutF16Split && g.accumulate) return cudaErrorInvalidValue;
     if (path != kDirect && !make_out_map(&mo, g.out, g.out_kind, g.m, w.n, g.ldc)) path = kDirect;
+    if (path != kDirect && g.out_kind == kOutF16Split &&
+        !make_out_map(&mo_lo, static_cast<__half*>(g.out) + static_cast<int64_t>(g.m) * g.ldc, g.out_kind, g.m, w.n,
+                      g.ldc))
+        path = kDirect;
     Params p{g.m, w.n, w.k, g.a.scale, w.scales, g.bias, g.act, g.scale, g.accumulate,
              g.out, g.ldc, g.out_kind, path, g.error};
     const int tiles = ((g.m + BM - 1) / BM) * ((w.n + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8x2_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mh, ml, mo, p);
+    gemm_i8x2_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, p);
     return cudaGetLastError();
 }
 

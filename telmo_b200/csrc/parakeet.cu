@@ -136,8 +136,8 @@ struct Parakeet {
     static int validate(const telmo_parakeet_config& c, std::string& why);
     Entry find(const std::string& name);
     std::string missing();
-    int gemm(const QuantAct& a, int m, const DevWeights& w, const float* bias, float* out, int64_t ldc, int act,
-             float scale, int acc, cudaStream_t s);
+    int gemm(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc, int act,
+             float scale, int acc, cudaStream_t s, int out_kind = kOutF32);
     int quant(const float* x, int64_t ldx, int m, int k, const QuantAct& q, cudaStream_t s);
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int decode(const float* encoded, const int* frames, int n_utt, uint32_t* tokens, int* counts, long* total,
@@ -269,8 +269,8 @@ std::string Parakeet::missing() {
     return "";
 }
 
-int Parakeet::gemm(const QuantAct& a, int m, const DevWeights& w, const float* bias, float* out, int64_t ldc, int act,
-                   float scale, int acc, cudaStream_t s) {
+int Parakeet::gemm(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc, int act,
+                   float scale, int acc, cudaStream_t s, int out_kind) {
     if (m <= 0) return TELMO_OK;
     GemmArgs g;
     g.m = m;
@@ -282,7 +282,7 @@ int Parakeet::gemm(const QuantAct& a, int m, const DevWeights& w, const float* b
     g.accumulate = acc;
     g.out = out;
     g.ldc = ldc;
-    g.out_kind = kOutF32;
+    g.out_kind = out_kind;
     g.error = ctx->error_word;
     ++launches;
     if (prof.on) {
@@ -335,12 +335,15 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     }
     if (r1 * std::max(ch, 1) > (int64_t(1) << 31) || feat_at * f0 > (int64_t(1) << 31))
         return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_encode: batch too large");
-    if (txl_attention_smem(hd, tmax) > 227 * 1024)
+    // The tensor-core attention takes 64 query rows per task, the other kernel 32.
+    const bool mma = txl_attention_mma_supported(hd);
+    const int q_rows = mma ? 64 : 32;
+    if (!mma && txl_attention_smem(hd, tmax) > 227 * 1024)
         return ctx->fail(TELMO_ERR_UNSUPPORTED, "parakeet_encode: an utterance of %d frames is too long", tmax);
     int at = 0;
     for (int u = 0; u < n_utt; ++u) {
         const int t = frames_out[u];
-        for (int q0 = 0; q0 < t; q0 += 32) att.push_back({at, t, q0, tmax - t});
+        for (int q0 = 0; q0 < t; q0 += q_rows) att.push_back({at, t, q0, tmax - t});
         for (int r = 0; r < t; r += 32) conv.push_back({at, t, at, r, std::min(32, t - r), 1});
         at += t;
     }
@@ -353,7 +356,8 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     const size_t bytes = 2 * piece<float>(static_cast<size_t>(r1) * ch) + quant_bytes(r1, ld_ch) +
                          quant_bytes(M, std::max(ld_lin, ld_main)) + 3 * piece<float>(static_cast<size_t>(M) * d) +
                          piece<float>(static_cast<size_t>(M) * big_ld) + 2 * piece<float>(static_cast<size_t>(P) * d) +
-                         quant_bytes(P, static_cast<int64_t>(round_up(d, 16))) + task_bytes;
+                         quant_bytes(P, static_cast<int64_t>(round_up(d, 16))) + piece<float>(static_cast<size_t>(P) * c.heads) +
+                         task_bytes;
     if (int rc = enc_arena.reserve(ctx, bytes)) return rc;
     Arena& A = enc_arena;
     float* sub_a = A.take<float>(static_cast<size_t>(r1) * ch);
@@ -370,6 +374,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     float* pos = A.take<float>(static_cast<size_t>(P) * d);
     float* pp = A.take<float>(static_cast<size_t>(P) * d);
     const QuantAct q_pos = quant_piece(A, P, static_cast<int64_t>(round_up(d, 16)));
+    float* cpos = A.take<float>(static_cast<size_t>(P) * c.heads);
     SubTask* front_dev = A.take<SubTask>(front.size());
     SubTask* dw2_dev = A.take<SubTask>(dw2t.size());
     TxlTask* att_dev = A.take<TxlTask>(att.size());
@@ -429,14 +434,28 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
         ++launches;
         if (int rc = ctx->cuda(ln_chain(x, M, d, L.norm_att.g.p, L.norm_att.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
             return rc;
-        if (int rc = gemm(q, M, L.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s)) return rc;
-        if (int rc = gemm(q_pos, P, L.pos, nullptr, pp, d, kActNone, 1.0f, 0, s)) return rc;
+        // The tensor-core attention reads Q, K, V and the projected positions as fp16 high/low
+        // planes straight from the products' epilogues; the other kernel reads f32.
+        const int kind = mma ? kOutF16Split : kOutF32;
+        if (int rc = gemm(q, M, L.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s, kind)) return rc;
+        if (int rc = gemm(q_pos, P, L.pos, nullptr, pp, d, kActNone, 1.0f, 0, s, kind)) return rc;
+        const __half* qkv16 = reinterpret_cast<const __half*>(big);
+        const __half* pp16 = reinterpret_cast<const __half*>(pp);
+        if (mma) {
+            ++launches;
+            if (int rc = ctx->cuda(txl_pos_bias(pp16, static_cast<int64_t>(P) * d, P, c.heads, hd, L.bias_u.p,
+                                                L.bias_v.p, cpos, s),
+                                   "parakeet position bias"))
+                return rc;
+        }
         if (prof.on) prof.begin(kProfAttention, s);
         ++launches;
-        if (int rc = ctx->cuda(txl_attention(big, pp, att_dev, static_cast<int>(att.size()), c.heads, hd, tmax,
-                                             L.bias_u.p, L.bias_v.p, scale, attn, s),
-                               "parakeet attention"))
-            return rc;
+        const cudaError_t ae =
+            mma ? txl_attention_mma(qkv16, static_cast<int64_t>(M) * 3 * d, pp16, static_cast<int64_t>(P) * d, cpos, P,
+                                    att_dev, static_cast<int>(att.size()), c.heads, hd, L.bias_u.p, scale, attn, s)
+                : txl_attention(big, pp, att_dev, static_cast<int>(att.size()), c.heads, hd, tmax, L.bias_u.p,
+                                L.bias_v.p, scale, attn, s);
+        if (int rc = ctx->cuda(ae, "parakeet attention")) return rc;
         if (prof.on) prof.end(kProfAttention, s);
         if (int rc = quant(attn, d, M, d, q, s)) return rc;
         if (int rc = gemm(q, M, L.out, nullptr, x, d, kActNone, 1.0f, 1, s)) return rc;

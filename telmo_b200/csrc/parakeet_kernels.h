@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace telmo {
@@ -47,6 +48,18 @@ size_t txl_attention_smem(int hd, int max_t);
 cudaError_t txl_attention(const float* qkv, const float* pp, const TxlTask* tasks, int n_tasks, int heads, int hd,
                           int max_t, const float* bias_u, const float* bias_v, float scale, float* att,
                           cudaStream_t s);
+
+// The same on the tensor cores (txl_attention_mma.cu), for head sizes 64 and 128, over tasks of
+// 64 query rows: qkv [rows, 3d] and the projected positions pos [npos, d] as fp16 high/low planes
+// (low plane `plane` / `pplane` elements after the high one), and cpos [heads, npos] from
+// txl_pos_bias.
+bool txl_attention_mma_supported(int hd);
+cudaError_t txl_attention_mma(const __half* qkv, int64_t plane, const __half* pos, int64_t pplane, const float* cpos,
+                              int npos, const TxlTask* tasks, int n_tasks, int heads, int hd, const float* bias_u,
+                              float scale, float* att, cudaStream_t s);
+// cpos[h][p] = (bias_v - bias_u) . pos[p] over head h's columns, pos as fp16 planes.
+cudaError_t txl_pos_bias(const __half* pos, int64_t pplane, int npos, int heads, int hd, const float* bias_u,
+                         const float* bias_v, float* cpos, cudaStream_t s);
 
 // z[u] = relu(enc_proj[u's current frame] + pred[u]), z [n_utt, h].
 cudaError_t tdt_joint_input(const float* enc_proj, const TdtState* st, int n_utt, int h, const float* pred, float* z,
