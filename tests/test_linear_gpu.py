@@ -4,7 +4,8 @@ Mirrors the reference's matrix-product tests (src/kernels/mod.rs:962-1128): shap
 edges, every epilogue, accumulate, and the config-1 shape. Three bars:
   * the quantized activations and the two int32 sums are bit-exact against the oracle;
   * the scaled output equals the oracle's step-for-step restatement of the CUDA epilogue bit for
-    bit (act none/relu) or within 2 ulp-scale (SiLU, whose exp differs between libm and CUDA);
+    bit (act none/relu) or within 1e-5 relative (SiLU, which the epilogue computes with the fast
+    exponential and division);
   * against the reference's own f32 path (int8 weights widened, f32 activations), each output
     matrix is within 1e-3 max-relative: max|got - ref| / max|ref| <= 1e-3.
 """
@@ -93,7 +94,7 @@ def test_linear_matches_the_oracle(ctx, oracle_lib, m, k, n, act, accumulate, wi
     got = c.cpu().numpy()
     exact = oracle_lib.linear_x2(a, values, scales, n, k, b, act, scale, c0, accumulate)
     if act == 2:
-        assert np.allclose(got, exact, rtol=2e-6, atol=1e-6)
+        assert np.allclose(got, exact, rtol=1e-5, atol=1e-6)
     else:
         assert np.array_equal(got.view(np.uint32), exact.view(np.uint32))
     ref = oracle_lib.linear_int8(a, values, scales, n, k, b, act, scale, c0, accumulate)
