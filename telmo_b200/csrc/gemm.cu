@@ -207,14 +207,16 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
     tc_fence_after();
     const uint32_t tmem_base = *tmem_base_slot;
 
-    // Tiles run feature-block-major: consecutive CTAs share a weight tile, which L2 then serves.
+    // Tiles run activation-block-major: the CTAs working at the same time share a block of
+    // activation rows (read from DRAM once, then served by L2) and sweep the features, whose
+    // weights (at most a few MB) stay in L2 for the whole product.
     if (warp == 0) {
         // ---- TMA producer ------------------------------------------------------------------
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-                const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
+                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) {
                         record_error(p.error, kErrWaitTimeout);
@@ -280,7 +282,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
             const int buf = it & 1;
             const uint32_t use = static_cast<uint32_t>(it >> 1);
-            const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
+            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
             const int n = n0 + quad * 32 + lane;
             const bool n_ok = n < p.n;
             const float ws = n_ok ? __ldg(p.w_scale + n) : 0.0f;
