@@ -37,7 +37,7 @@ namespace telmo {
 
 namespace {
 
-constexpr int kSubSpan = 8;     // output time steps of the first convolutions per task
+constexpr int kSubSpan = 8;     // output time steps of the second depthwise convolution per task
 constexpr int kPollSteps = 16;  // decoding passes between completion checks
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -320,8 +320,8 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
         const int t0 = rows[u];
         if (t0 < 1) return ctx->fail(TELMO_ERR_MODEL, "parakeet_encode: utterance %d has no feature frames", u);
         const int t1 = out_len(t0), t2 = out_len(t1), t3 = out_len(t2);
-        for (int a = 0; a < t2; a += kSubSpan)
-            front.push_back({static_cast<int>(feat_at), t0, a, std::min(kSubSpan, t2 - a),
+        for (int a = 0; a < t2; a += kSubRows)
+            front.push_back({static_cast<int>(feat_at), t0, a, std::min(kSubRows, t2 - a),
                              static_cast<int>(r1 + static_cast<int64_t>(a) * f2)});
         for (int a = 0; a < t3; a += kSubSpan)
             dw2t.push_back({static_cast<int>(r1), t2, a, std::min(kSubSpan, t3 - a),
@@ -391,7 +391,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     if (prof.on) prof.begin(kProfRows, s);
     ++launches;
     if (int rc = ctx->cuda(sub_front(feats, f0, front_dev, static_cast<int>(front.size()), ch, conv0_w.p, conv0_b.p,
-                                     dw1_w.p, dw1_b.p, sub_a, kSubSpan, s),
+                                     dw1_w.p, dw1_b.p, sub_a, s),
                            "parakeet conv0+dw1"))
         return rc;
     if (prof.on) prof.end(kProfRows, s);

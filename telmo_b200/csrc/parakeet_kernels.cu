@@ -20,93 +20,144 @@ constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ float madd(float acc, float w, float v) { return __fadd_rn(acc, __fmul_rn(w, v)); }
 
-// conv0 (1 -> ch, 3x3, stride 2, zero padding 1) + ReLU at (t1, f1) for channel c, from the
-// staged feature rows (row t0 of the utterance at stage[(t0 - t0_base) * f0]).
-__device__ __forceinline__ float conv0_at(const float* stage, int t0_base, int t0_count, int f0, int t1, int f1,
-                                          const float* w0, const float* b0, int ch, int c) {
-    float o = b0[c];
-#pragma unroll
-    for (int dt = 0; dt < 3; ++dt) {
-        const int t0 = 2 * t1 + dt - 1;
-        if (t0 < 0 || t0 - t0_base >= t0_count) continue;
-#pragma unroll
-        for (int df = 0; df < 3; ++df) {
-            const int ff = 2 * f1 + df - 1;
-            if (ff < 0 || ff >= f0) continue;
-            o = madd(o, w0[(dt * 3 + df) * ch + c], stage[(t0 - t0_base) * f0 + ff]);
-        }
-    }
-    return fmaxf(o, 0.0f);
-}
-
 }  // namespace
 
 // Fused conv0 + ReLU + depthwise conv1 (Parakeet::subsample's first two convolutions,
-// src/parakeet.rs:937-941). One CTA per (span of output rows t2, block of 128 channels); the
-// conv0 values each depthwise output reads are recomputed (about 2.3x) instead of being stored.
-__global__ void __launch_bounds__(128) sub_front_kernel(const float* __restrict__ feats, int f0,
+// src/parakeet.rs:937-941). One CTA per (span of kSubRows output time steps t2, block of kSubCh
+// channels): it stages the feature rows the span reads, computes conv0 + ReLU for the t1 rows the
+// span needs into shared memory (2 x kSubRows + 1 rows, so about 1/8 of conv0 is computed twice
+// across neighbouring spans), then the depthwise conv from there. Thread = (channel, group of
+// positions); each thread keeps its channel's 9 taps in registers.
+__global__ void __launch_bounds__(256) sub_front_kernel(const float* __restrict__ feats, int f0,
                                                         const SubTask* __restrict__ tasks, int ch,
                                                         const float* __restrict__ w0, const float* __restrict__ b0,
                                                         const float* __restrict__ w1, const float* __restrict__ b1,
                                                         float* __restrict__ out) {
-    extern __shared__ float stage[];
+    extern __shared__ float smf[];
     const SubTask t = tasks[blockIdx.x];
-    const int c = blockIdx.y * 128 + threadIdx.x;
+    const int c0 = blockIdx.y * kSubCh;
+    const int c = threadIdx.x % kSubCh, grp = threadIdx.x / kSubCh;
+    constexpr int kGroups = 256 / kSubCh;
     const int f1n = (f0 - 1) / 2 + 1, f2n = (f1n - 1) / 2 + 1;
     const int t1n = (t.t0 - 1) / 2 + 1;
-    // Feature rows the span reads: t1 in [2 t2_first - 1, 2 t2_last + 1], t0 = 2 t1 - 1 .. 2 t1 + 1.
-    const int t0_base = max(0, 4 * t.t2_first - 3);
-    const int t0_last = min(t.t0 - 1, 4 * (t.t2_first + t.t2_count - 1) + 3);
-    const int rows = t0_last - t0_base + 1;
-    for (int i = threadIdx.x; i < rows * f0; i += 128) stage[i] = feats[static_cast<int64_t>(t.feat_row + t0_base) * f0 + i];
+    const int t1_base = max(0, 2 * t.t2_first - 1);
+    const int t1_last = min(t1n - 1, 2 * (t.t2_first + t.t2_count - 1) + 1);
+    const int t1_rows = t1_last - t1_base + 1;
+    const int t0_base = max(0, 2 * t1_base - 1);
+    const int t0_last = min(t.t0 - 1, 2 * t1_last + 1);
+    const int t0_rows = t0_last - t0_base + 1;
+    float* stage = smf;                                  // [t0_rows][f0]
+    float* h1 = smf + (4 * kSubRows + 3) * f0;           // [t1_rows][f1n][kSubCh]
+    for (int i = threadIdx.x; i < t0_rows * f0; i += 256)
+        stage[i] = feats[static_cast<int64_t>(t.feat_row + t0_base) * f0 + i];
+    const bool live = c0 + c < ch;
+    float w[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[k] = live ? w0[k * ch + c0 + c] : 0.0f;
+    const float bias0 = live ? b0[c0 + c] : 0.0f;
     __syncthreads();
-    if (c >= ch) return;
-    for (int t2 = t.t2_first; t2 < t.t2_first + t.t2_count; ++t2) {
-        for (int f2 = 0; f2 < f2n; ++f2) {
-            float acc = b1[c];
+    // conv0 + ReLU: h1[t1][f1][c], row by row (no index division), frequencies strided by group.
+    for (int r = 0; r < t1_rows; ++r) {
+        const int t1 = t1_base + r;
+        const float* rows[3];
+        bool ok[3];
+#pragma unroll
+        for (int dt = 0; dt < 3; ++dt) {
+            const int t0 = 2 * t1 + dt - 1;
+            ok[dt] = t0 >= 0 && t0 < t.t0;
+            rows[dt] = stage + (ok[dt] ? t0 - t0_base : 0) * f0;
+        }
+        float* hrow = h1 + r * f1n * kSubCh + c;
+        for (int f1 = grp; f1 < f1n; f1 += kGroups) {
+            float o = bias0;
 #pragma unroll
             for (int dt = 0; dt < 3; ++dt) {
-                const int t1 = 2 * t2 + dt - 1;
-                if (t1 < 0 || t1 >= t1n) continue;
+                if (!ok[dt]) continue;
+#pragma unroll
+                for (int df = 0; df < 3; ++df) {
+                    const int ff = 2 * f1 + df - 1;
+                    if (ff < 0 || ff >= f0) continue;
+                    o = madd(o, w[dt * 3 + df], rows[dt][ff]);
+                }
+            }
+            hrow[f1 * kSubCh] = fmaxf(o, 0.0f);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[k] = live ? w1[k * ch + c0 + c] : 0.0f;
+    const float bias1 = live ? b1[c0 + c] : 0.0f;
+    __syncthreads();
+    // Depthwise conv1: out[t2][f2][c]
+    for (int r = 0; r < t.t2_count; ++r) {
+        const int t2 = t.t2_first + r;
+        const float* rows[3];
+        bool ok[3];
+#pragma unroll
+        for (int dt = 0; dt < 3; ++dt) {
+            const int t1 = 2 * t2 + dt - 1;
+            ok[dt] = t1 >= 0 && t1 < t1n;
+            rows[dt] = h1 + (ok[dt] ? t1 - t1_base : 0) * f1n * kSubCh + c;
+        }
+        float* orow = out + (static_cast<int64_t>(t.out_row) + static_cast<int64_t>(r) * f2n) * ch + c0 + c;
+        for (int f2 = grp; f2 < f2n; f2 += kGroups) {
+            float acc = bias1;
+#pragma unroll
+            for (int dt = 0; dt < 3; ++dt) {
+                if (!ok[dt]) continue;
 #pragma unroll
                 for (int df = 0; df < 3; ++df) {
                     const int f1 = 2 * f2 + df - 1;
                     if (f1 < 0 || f1 >= f1n) continue;
-                    const float h = conv0_at(stage, t0_base, rows, f0, t1, f1, w0, b0, ch, c);
-                    acc = madd(acc, w1[(dt * 3 + df) * ch + c], h);
+                    acc = madd(acc, w[dt * 3 + df], rows[dt][f1 * kSubCh]);
                 }
             }
-            out[(static_cast<int64_t>(t.out_row) + static_cast<int64_t>(t2 - t.t2_first) * f2n + f2) * ch + c] = acc;
+            if (live) orow[static_cast<int64_t>(f2) * ch] = acc;
         }
     }
 }
 
 // Depthwise 3x3 stride-2 convolution over [t_in, f_in, ch] rows of one utterance (conv3x3s2_row
-// with depthwise, src/kernels/scalar.rs:194-232). One CTA per (task, channel block).
-__global__ void __launch_bounds__(128) dw3x3s2_kernel(const float* __restrict__ in, int f_in, const SubTask* __restrict__ tasks,
+// with depthwise, src/kernels/scalar.rs:194-232). One CTA per (task, block of kSubCh channels);
+// thread = (channel, group of output positions) with the channel's 9 taps in registers, so each
+// warp reads 32 consecutive channels of one input position per tap.
+__global__ void __launch_bounds__(256) dw3x3s2_kernel(const float* __restrict__ in, int f_in, const SubTask* __restrict__ tasks,
                                                       int ch, const float* __restrict__ w, const float* __restrict__ b,
                                                       float* __restrict__ out) {
     const SubTask t = tasks[blockIdx.x];
-    const int c = blockIdx.y * 128 + threadIdx.x;
+    const int c = blockIdx.y * kSubCh + threadIdx.x % kSubCh, grp = threadIdx.x / kSubCh;
+    constexpr int kGroups = 256 / kSubCh;
     if (c >= ch) return;
     const int f_out = (f_in - 1) / 2 + 1;
     const int t_in = t.t0;
-    for (int to = t.t2_first; to < t.t2_first + t.t2_count; ++to) {
-        for (int fo = 0; fo < f_out; ++fo) {
-            float acc = b[c];
+    float wr[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) wr[k] = w[k * ch + c];
+    const float bias = b[c];
+    const float* src = in + static_cast<int64_t>(t.feat_row) * ch + c;
+    for (int r = 0; r < t.t2_count; ++r) {
+        const int to = t.t2_first + r;
+        const float* rows[3];
+        bool ok[3];
+#pragma unroll
+        for (int dt = 0; dt < 3; ++dt) {
+            const int ti = 2 * to + dt - 1;
+            ok[dt] = ti >= 0 && ti < t_in;
+            rows[dt] = src + static_cast<int64_t>(ok[dt] ? ti : 0) * f_in * ch;
+        }
+        float* orow = out + (static_cast<int64_t>(t.out_row) + static_cast<int64_t>(r) * f_out) * ch + c;
+        for (int fo = grp; fo < f_out; fo += kGroups) {
+            float acc = bias;
 #pragma unroll
             for (int dt = 0; dt < 3; ++dt) {
-                const int ti = 2 * to + dt - 1;
-                if (ti < 0 || ti >= t_in) continue;
+                if (!ok[dt]) continue;
 #pragma unroll
                 for (int df = 0; df < 3; ++df) {
                     const int fi = 2 * fo + df - 1;
                     if (fi < 0 || fi >= f_in) continue;
-                    acc = madd(acc, w[(dt * 3 + df) * ch + c],
-                               in[(static_cast<int64_t>(t.feat_row) + static_cast<int64_t>(ti) * f_in + fi) * ch + c]);
+                    acc = madd(acc, wr[dt * 3 + df], __ldg(rows[dt] + static_cast<int64_t>(fi) * ch));
                 }
             }
-            out[(static_cast<int64_t>(t.out_row) + static_cast<int64_t>(to - t.t2_first) * f_out + fo) * ch + c] = acc;
+            orow[static_cast<int64_t>(fo) * ch] = acc;
         }
     }
 }
@@ -429,22 +480,29 @@ __global__ void pred_commit_kernel(const int* __restrict__ predict_token, int n_
 
 // ---- launchers ---------------------------------------------------------------------------------
 
+size_t sub_front_smem(int f0) {
+    const int f1 = (f0 - 1) / 2 + 1;
+    return sizeof(float) * ((4 * kSubRows + 3) * f0 + (2 * kSubRows + 1) * f1 * kSubCh);
+}
+
 cudaError_t sub_front(const float* feats, int f0, const SubTask* tasks, int n_tasks, int ch, const float* w0,
-                      const float* b0, const float* w1, const float* b1, float* out, int max_t2_span,
-                      cudaStream_t s) {
+                      const float* b0, const float* w1, const float* b1, float* out, cudaStream_t s) {
     if (n_tasks <= 0) return cudaSuccess;
-    const int rows = 4 * max_t2_span + 3;
-    const size_t smem = sizeof(float) * rows * f0;
-    dim3 grid(n_tasks, (ch + 127) / 128);
-    sub_front_kernel<<<grid, 128, smem, s>>>(feats, f0, tasks, ch, w0, b0, w1, b1, out);
+    const size_t smem = sub_front_smem(f0);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    const cudaError_t e =
+        cudaFuncSetAttribute(sub_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    dim3 grid(n_tasks, (ch + kSubCh - 1) / kSubCh);
+    sub_front_kernel<<<grid, 256, smem, s>>>(feats, f0, tasks, ch, w0, b0, w1, b1, out);
     return cudaGetLastError();
 }
 
 cudaError_t dw3x3s2(const float* in, int f_in, const SubTask* tasks, int n_tasks, int ch, const float* w,
                     const float* b, float* out, cudaStream_t s) {
     if (n_tasks <= 0) return cudaSuccess;
-    dim3 grid(n_tasks, (ch + 127) / 128);
-    dw3x3s2_kernel<<<grid, 128, 0, s>>>(in, f_in, tasks, ch, w, b, out);
+    dim3 grid(n_tasks, (ch + kSubCh - 1) / kSubCh);
+    dw3x3s2_kernel<<<grid, 256, 0, s>>>(in, f_in, tasks, ch, w, b, out);
     return cudaGetLastError();
 }
 

@@ -15,8 +15,9 @@ struct SubTask {
     int feat_row, t0, t2_first, t2_count, out_row;
 };
 
-// Query rows [q_first, q_first + 32) of one utterance of len frames whose rows start at row and
-// whose projected positions start at row pos_row of the position projection.
+// Query rows [q_first, q_first + 32) (64 for the tensor-core kernel) of one utterance of len
+// frames whose rows start at row and whose projected positions start at row pos_row of the
+// position projection.
 struct TxlTask {
     int row, len, q_first, pos_row;
 };
@@ -27,11 +28,15 @@ struct TdtState {
     int enc_first, frames, t, on_frame, tok_first, count;
 };
 
+// Output time steps of the first convolutions per sub_front task, and channels per CTA.
+constexpr int kSubRows = 4;
+constexpr int kSubCh = 16;
+
 // Fused conv0 (1 -> ch, ReLU) + depthwise conv1 over features [rows, f0]; out [t2 * f2, ch]
-// per task. max_t2_span bounds every task's t2_count (it sizes the staged feature rows).
+// per task, every task spanning at most kSubRows output time steps.
+size_t sub_front_smem(int f0);
 cudaError_t sub_front(const float* feats, int f0, const SubTask* tasks, int n_tasks, int ch, const float* w0,
-                      const float* b0, const float* w1, const float* b1, float* out, int max_t2_span,
-                      cudaStream_t s);
+                      const float* b0, const float* w1, const float* b1, float* out, cudaStream_t s);
 
 // Depthwise 3x3 stride-2 convolution: in [t0 * f_in, ch] per task (task.t0 input time steps)
 // -> out [count * f_out, ch].
