@@ -16,8 +16,9 @@
 //    (a row depends only on its position), so the positions are built, quantized and projected
 //    once per layer for the whole batch.
 // Decoding advances every utterance by one joint step per pass, with the prediction network
-// run for the utterances that emitted a token; the host polls for completion every kPollSteps
-// passes (passes after an utterance finishes change nothing of it).
+// run for the utterances that emitted a token; the passes run as a replayed CUDA graph and the
+// host polls for completion every kPollSteps passes (passes after an utterance finishes change
+// nothing of it).
 #include "../../include/telmo_b200.h"
 #include "api_internal.h"
 #include "frontend.h"
@@ -95,6 +96,16 @@ QuantAct quant_piece(Arena& a, size_t rows, int64_t ld) {
 }
 size_t quant_bytes(size_t rows, int64_t ld) { return 2 * piece<int8_t>(rows * ld) + piece<float>(rows); }
 
+// An instantiated CUDA graph, destroyed with its scope.
+struct GraphExec {
+    cudaGraphExec_t exec = nullptr;
+    void reset() {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+    }
+    ~GraphExec() { reset(); }
+};
+
 }  // namespace
 
 // One conformer layer, as Parakeet's Layer (src/parakeet.rs:269-292).
@@ -123,6 +134,7 @@ struct Parakeet {
     long launches = 0;
 
     Arena enc_arena, dec_arena, e2e_arena;
+    cudaStream_t capture_stream = nullptr;  // records the decoding passes as a graph
     float* audio_dev = nullptr;
     size_t audio_cap = 0;
 
@@ -164,6 +176,7 @@ Parakeet::~Parakeet() {
     if (durations_dev) cudaFree(durations_dev);
     if (host_words) cudaFreeHost(host_words);
     if (audio_dev) cudaFree(audio_dev);
+    if (capture_stream) cudaStreamDestroy(capture_stream);
 }
 
 // Config::from_json's checks (src/parakeet.rs:131-140), plus the limits of these kernels.
@@ -552,42 +565,78 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
         return ctx->cuda(e, what);
     };
     // Parakeet::predict_rows (src/parakeet.rs:1523-1577) for the utterances with a token.
-    auto predict = [&]() -> int {
+    auto predict = [&](cudaStream_t st) -> int {
         for (int l = 0; l < L; ++l) {
-            if (int rc = rows_kernel(lstm_input(predict_token, U, h, l, L, embedding.p, state, input, s), "lstm input"))
+            if (int rc = rows_kernel(lstm_input(predict_token, U, h, l, L, embedding.p, state, input, st), "lstm input"))
                 return rc;
-            if (int rc = quant(input, 2 * h, U, 2 * h, qd, s)) return rc;
-            if (int rc = gemm(qd, U, lstm[l], lstm_b[l].p, gates, 4 * h, kActNone, 1.0f, 0, s)) return rc;
-            if (int rc = rows_kernel(lstm_cell(predict_token, U, h, l, L, gates, state, s), "lstm cell")) return rc;
+            if (int rc = quant(input, 2 * h, U, 2 * h, qd, st)) return rc;
+            if (int rc = gemm(qd, U, lstm[l], lstm_b[l].p, gates, 4 * h, kActNone, 1.0f, 0, st)) return rc;
+            if (int rc = rows_kernel(lstm_cell(predict_token, U, h, l, L, gates, state, st), "lstm cell")) return rc;
         }
-        if (int rc = rows_kernel(lstm_last(predict_token, U, h, L, state, last, s), "lstm last")) return rc;
-        if (int rc = quant(last, h, U, h, qd, s)) return rc;
-        if (int rc = gemm(qd, U, pred_proj, pred_proj_b.p, fresh, h, kActNone, 1.0f, 0, s)) return rc;
-        return rows_kernel(pred_commit(predict_token, U, h, fresh, pred, s), "pred commit");
+        if (int rc = rows_kernel(lstm_last(predict_token, U, h, L, state, last, st), "lstm last")) return rc;
+        if (int rc = quant(last, h, U, h, qd, st)) return rc;
+        if (int rc = gemm(qd, U, pred_proj, pred_proj_b.p, fresh, h, kActNone, 1.0f, 0, st)) return rc;
+        return rows_kernel(pred_commit(predict_token, U, h, fresh, pred, st), "pred commit");
     };
     // One joint step for every utterance (src/parakeet.rs:1455-1510).
-    auto step = [&]() -> int {
-        if (int rc = rows_kernel(tdt_joint_input(enc_proj_out, st_dev, U, h, pred, z, s), "joint input")) return rc;
-        if (int rc = quant(z, h, U, h, qd, s)) return rc;
-        if (int rc = gemm(qd, U, joint, joint_b.p, logits, ld_logits, kActNone, 1.0f, 0, s)) return rc;
-        if (int rc = ctx->cuda(cudaMemsetAsync(words, 0, sizeof(int), s), "tdt")) return rc;
+    auto step = [&](cudaStream_t st) -> int {
+        if (int rc = rows_kernel(tdt_joint_input(enc_proj_out, st_dev, U, h, pred, z, st), "joint input")) return rc;
+        if (int rc = quant(z, h, U, h, qd, st)) return rc;
+        if (int rc = gemm(qd, U, joint, joint_b.p, logits, ld_logits, kActNone, 1.0f, 0, st)) return rc;
+        if (int rc = ctx->cuda(cudaMemsetAsync(words, 0, sizeof(int), st), "tdt")) return rc;
         if (int rc = rows_kernel(tdt_decide(logits, ld_logits, c.vocab, c.blank, durations_dev, c.n_durations,
-                                            c.max_symbols, st_dev, U, raw, predict_token, words, s),
+                                            c.max_symbols, st_dev, U, raw, predict_token, words, st),
                                  "tdt decide"))
             return rc;
-        return predict();
+        return predict(st);
     };
     if (int rc = rows_kernel(tdt_start(U, c.blank, predict_token, s), "tdt start")) return rc;
-    if (int rc = predict()) return rc;
+    if (int rc = predict(s)) return rc;
     // Each pass advances every unfinished utterance by a frame or emits one of its at most
     // max_symbols tokens on a frame, so frames * (max_symbols + 1) passes bound the loop.
     int64_t max_frames = 0;
     for (int u = 0; u < U; ++u) max_frames = std::max<int64_t>(max_frames, frames[u]);
     const int64_t bound = max_frames * (c.max_symbols + 1) + 1;
+    // The kPollSteps passes between two completion checks are recorded once as a CUDA graph on a
+    // private stream and replayed on the caller's stream (one launch instead of about 17 per
+    // pass); if recording fails the passes are launched one by one.
+    GraphExec graph;
+    long graph_launches = 0;
+    if (max_frames > 0) {
+        if (!capture_stream && cudaStreamCreateWithFlags(&capture_stream, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            capture_stream = nullptr;
+        }
+        if (capture_stream) {
+            const long before = launches;
+            const bool prof_on = prof.on;
+            prof.on = false;  // no event records inside the graph
+            cudaGraph_t g = nullptr;
+            int rc = ctx->cuda(cudaStreamBeginCapture(capture_stream, cudaStreamCaptureModeThreadLocal), "tdt capture");
+            if (!rc) {
+                for (int i = 0; i < kPollSteps && !rc; ++i) rc = step(capture_stream);
+                const cudaError_t e = cudaStreamEndCapture(capture_stream, &g);
+                if (!rc && e == cudaSuccess && g) rc = ctx->cuda(cudaGraphInstantiate(&graph.exec, g, 0), "tdt graph");
+                if (g) cudaGraphDestroy(g);
+            }
+            prof.on = prof_on;
+            graph_launches = launches - before;
+            launches = before;
+            if (rc || !graph.exec) {
+                cudaGetLastError();
+                graph.reset();
+            }
+        }
+    }
     int64_t passes = 0;
     while (max_frames > 0) {
-        for (int i = 0; i < kPollSteps; ++i)
-            if (int rc = step()) return rc;
+        if (graph.exec) {
+            if (int rc = ctx->cuda(cudaGraphLaunch(graph.exec, s), "tdt graph")) return rc;
+            launches += graph_launches;
+        } else {
+            for (int i = 0; i < kPollSteps; ++i)
+                if (int rc = step(s)) return rc;
+        }
         passes += kPollSteps;
         if (int rc = ctx->cuda(cudaMemcpyAsync(host_words, words, sizeof(int), cudaMemcpyDeviceToHost, s), "tdt"))
             return rc;
