@@ -16,7 +16,8 @@
 // Structure: a persistent, warp-specialised kernel, one CTA per SM.
 //   warp 0      TMA producer: 128 x 128-byte boxes of W, A_hi and A_lo per stage (128B swizzle)
 //   warp 1      MMA issuer: 4 x tcgen05.mma kind::i8 per 128-byte K step
-//   warps 2-5   epilogue: tcgen05.ld, fused scale/bias/act/residual, coalesced global stores
+//   warps 2-9   epilogue: tcgen05.ld, fused scale/bias/act/residual, TMA stores (two warps per
+//               TMEM lane quarter, each on half of the tile's activation rows)
 // TMEM holds two tiles (2 x 256 columns), so the epilogue of one tile overlaps the main loop of
 // the next. Every mbarrier wait is bounded; on timeout the kernel records kErrWaitTimeout in the
 // error word and returns.
@@ -37,13 +38,14 @@ constexpr int BN = 128;  // output features per tile (MMA M)
 constexpr int BM = 128;  // activation rows per tile (MMA N = 2 * BM)
 constexpr int BK = 128;  // bytes = int8 elements per stage along K (one 128-byte swizzle row)
 constexpr int UMMA_K = 32;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each on half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStages = 4;
 constexpr int kTileBytes = 128 * BK;  // one 128-row operand box
 constexpr int kStageBytes = 3 * kTileBytes;
 constexpr int kTmemCols = 2 * 2 * BM;  // 2 buffers x (hi, lo) x BM columns
 constexpr int kStageOutBytes = 32 * 32 * 4;   // one 32 x 32 f32 output chunk
-constexpr int kOutStaging = 4 * 2 * kStageOutBytes;  // 4 epilogue warps x 2 buffers
+constexpr int kOutStaging = kEpiWarps * kStageOutBytes;  // one buffer per epilogue warp
 constexpr int kSmemBytes = kStages * kStageBytes + kOutStaging + 1024 + 256;
 
 // How the epilogue writes: TMA store of staged chunks, TMA reduce-add (accumulate), or direct
@@ -188,7 +190,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 4 * 32);
+            mbar_init(&tmem_empty[b], kEpiWarps * 32);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -273,11 +275,12 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
             __syncwarp();
         }
     } else {
-        // ---- epilogue (warps 2..5): thread = one output feature, 32 rows per TMEM load ----------
+        // ---- epilogue (warps 2..9): thread = one output feature, 32 rows per TMEM load; the two
+        // warps of a TMEM lane quarter take the tile's first and second 64 activation rows ----
         const int quad = warp & 3;  // TMEM lanes this warp may access: 32 * quad ..
+        const int part = (warp - 2) / 4;
         const bool has_bias = p.bias != nullptr;
-        uint8_t* my_staging = staging + quad * 2 * kStageOutBytes;
-        int chunk_count = 0;
+        uint8_t* sbuf = staging + (warp - 2) * kStageOutBytes;
         int it = 0;
         for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -296,7 +299,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(buf * 2 * BM);
 #pragma unroll 1
-            for (int c = 0; c < BM / 32; ++c) {
+            for (int c = part * (BM / 64); c < (part + 1) * (BM / 64); ++c) {
                 uint32_t hi[32], lo[32];
                 tmem_ld32(taddr + c * 32, hi);
                 tmem_ld32(taddr + BM + c * 32, lo);
@@ -308,12 +311,11 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                 const int64_t off = static_cast<int64_t>(mc) * p.ldc + n;
                 if (p.out_path != kDirect) {
                     // Stage the 32 x 32 chunk (row = activation row, column = feature) and let one
-                    // lane hand it to TMA; the buffer is reused two chunks later.
+                    // lane hand it to TMA; the previous chunk's store has read the buffer by the
+                    // time this chunk's values are computed, almost always.
                     float v[32];
                     compute_chunk_any(p.act, hi, lo, my_rs, ws, bs, p.scale, v);
-                    uint8_t* sbuf = my_staging + (chunk_count & 1) * kStageOutBytes;
-                    ++chunk_count;
-                    if (lane == 0) bulk_wait_read<1>();
+                    if (lane == 0) bulk_wait_read<0>();
                     __syncwarp();
                     if (p.out_kind == kOutF32) {
                         float* sf = reinterpret_cast<float*>(sbuf);
