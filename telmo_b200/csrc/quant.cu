@@ -70,30 +70,43 @@ __global__ void quantize_x2_kernel(const float* __restrict__ x, int64_t ldx, int
 }
 
 // The same for rows of k = 128 * C values (16-byte aligned): the row stays in registers, so it
-// is read from memory once.
-template <int C>
+// is read from memory once. W warps share a row (C / W float4 per lane each), exchanging their
+// maxima through shared memory, which keeps long rows at a register count that leaves room for
+// several blocks per SM.
+template <int C, int W>
 __global__ void __launch_bounds__(256) quantize_x2_regs_kernel(const float* __restrict__ x, int64_t ldx, int m,
                                                                int8_t* __restrict__ hi, int8_t* __restrict__ lo,
                                                                int64_t ldq, float* __restrict__ scale) {
-    const int row = blockIdx.x * 8 + threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
-    if (row >= m) return;
-    const float* xr = x + row * ldx;
-    float4 v[C];
+    constexpr int CW = C / W;  // float4 per lane
+    __shared__ float part[8];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int row = blockIdx.x * (8 / W) + warp / W;
+    const int piece = warp % W;
+    const bool live = row < m;
+    const float* xr = x + static_cast<int64_t>(live ? row : 0) * ldx + piece * CW * 128;
+    float4 v[CW];
 #pragma unroll
-    for (int c = 0; c < C; ++c) v[c] = *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4);
+    for (int c = 0; c < CW; ++c)
+        v[c] = live ? *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
     float amax = 0.0f;
 #pragma unroll
-    for (int c = 0; c < C; ++c)
+    for (int c = 0; c < CW; ++c)
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
     amax = warp_max(amax);
+    if (W > 1) {
+        if (lane == 0) part[warp] = amax;
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < W; ++i) amax = fmaxf(amax, part[(warp / W) * W + i]);
+    }
+    if (!live) return;
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     const float id_lo = __fmul_rn(id, 254.0f);
-    int8_t* hr = hi + row * ldq;
-    int8_t* lr = lo + row * ldq;
+    int8_t* hr = hi + static_cast<int64_t>(row) * ldq + piece * CW * 128;
+    int8_t* lr = lo + static_cast<int64_t>(row) * ldq + piece * CW * 128;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
+    for (int c = 0; c < CW; ++c) {
         char4 h, l;
         quant_one(v[c].x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
         quant_one(v[c].y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
@@ -102,8 +115,12 @@ __global__ void __launch_bounds__(256) quantize_x2_regs_kernel(const float* __re
         *reinterpret_cast<char4*>(hr + (c * 32 + lane) * 4) = h;
         *reinterpret_cast<char4*>(lr + (c * 32 + lane) * 4) = l;
     }
-    for (int i = C * 128 + lane; i < ldq; i += 32) hr[i] = lr[i] = 0;
-    if (lane == 0) scale[row] = d;
+    if (piece == W - 1) {
+        int8_t* hz = hi + static_cast<int64_t>(row) * ldq;
+        int8_t* lz = lo + static_cast<int64_t>(row) * ldq;
+        for (int i = C * 128 + lane; i < ldq; i += 32) hz[i] = lz[i] = 0;
+        if (lane == 0) scale[row] = d;
+    }
 }
 
 }  // namespace
@@ -116,11 +133,12 @@ cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAc
     const bool regs = k % 128 == 0 && ldx % 4 == 0 && q.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     if (regs) {
         switch (k / 128) {
-            case 8: quantize_x2_regs_kernel<8><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+            case 8: quantize_x2_regs_kernel<8, 1><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
                 return cudaGetLastError();
-            case 16: quantize_x2_regs_kernel<16><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+            case 16: quantize_x2_regs_kernel<16, 1><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
                 return cudaGetLastError();
-            case 32: quantize_x2_regs_kernel<32><<<grid, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
+            case 32:
+                quantize_x2_regs_kernel<32, 2><<<(m + 3) / 4, 256, 0, stream>>>(x, ldx, m, q.hi, q.lo, q.ld, q.scale);
                 return cudaGetLastError();
             default: break;
         }

@@ -175,7 +175,9 @@ __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t r
 }
 
 // GLU + depthwise convolution (taps in order from the bias, skipping frames outside the
-// utterance) + SiLU. Task t covers output frames [out_first, out_first + count <= 32) of one
+// utterance) + SiLU, the GLU gate and the SiLU with the fast exponential and division (a few
+// ulp from a / (1 + expf(-b)); the conversion unit would otherwise bound the kernel). Task t
+// covers output frames [out_first, out_first + count <= 32) of one
 // utterance; each thread owns one channel. The GLU values of every input frame the task reads
 // are staged first -- eight frames' loads in flight at a time -- in a shared column per thread,
 // then each output frame sums its K taps from there.
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-            if (i0 + u < nf) glu[i0 + u][threadIdx.x] = __fdiv_rn(a[u], __fadd_rn(1.0f, expf(-b[u])));
+            if (i0 + u < nf) glu[i0 + u][threadIdx.x] = __fdividef(a[u], __fadd_rn(1.0f, __expf(-b[u])));
     }
     if (!live) return;
     float wk[K];
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
             const int f = s * r + j - half;
             if (f >= 0 && f < t.in_len) acc = __fadd_rn(acc, __fmul_rn(wk[j], glu[f - f_lo][threadIdx.x]));
         }
-        acc = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+        acc = __fdividef(acc, __fadd_rn(1.0f, __expf(-acc)));
         out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
     }
 }
