@@ -490,7 +490,8 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
             return rc;
         ++launches;
         if (int rc = gemm(q, m, b.pw1, big, 2 * cc, kActNone, 1.0f, 0, s)) return rc;
-        if (int rc = ctx->cuda(glu_dwconv_silu(big, cc, c.conv_kernel, reinterpret_cast<const ConvTask*>(tasks_dev + p.conv_off),
+        if (int rc = ctx->cuda(glu_dwconv_silu(big, cc, c.conv_kernel, b.strided ? 2 : 1,
+                                               reinterpret_cast<const ConvTask*>(tasks_dev + p.conv_off),
                                                p.conv_n, b.dw_w.p, b.dw_b.p, conv, s),
                                "dwconv"))
             return rc;

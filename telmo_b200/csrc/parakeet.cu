@@ -480,7 +480,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
         if (int rc = gemm(q, M, L.pw1, nullptr, big, 2 * d, kActNone, 1.0f, 0, s)) return rc;
         if (prof.on) prof.begin(kProfRows, s);
         ++launches;
-        if (int rc = ctx->cuda(glu_dwconv_silu(big, d, c.conv_kernel, conv_dev, static_cast<int>(conv.size()), L.dw_w.p,
+        if (int rc = ctx->cuda(glu_dwconv_silu(big, d, c.conv_kernel, 1, conv_dev, static_cast<int>(conv.size()), L.dw_w.p,
                                                L.dw_b.p, convo, s),
                                "parakeet dwconv"))
             return rc;

@@ -54,27 +54,61 @@ __device__ __forceinline__ Scales row_scales(float amax) {
     return s;
 }
 
-// Layer norm of one row held as float4 chunks v[c] = elements (c * 32 + lane) * 4 .. + 3.
-template <int C>
-__device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, const float* __restrict__ gamma,
-                                                const float* __restrict__ beta, float eps, int lane) {
+// Sums and maxima over a row held by P warps: a warp reduction, then (P = 2) an exchange through
+// shared memory under a named barrier for the row's two warps. Every reduction of a row has its
+// own slot, so one barrier per reduction suffices; both warps add the two halves in the same
+// order and so agree on every result.
+template <int P>
+struct RowReduce {
+    double* xch;  // [kSlots][P] of this row's group
+    int part, bar, slot;
+    static constexpr int kSlots = 6;
+    __device__ __forceinline__ void sync() const {
+        if (P > 1) asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(32 * P) : "memory");
+    }
+    __device__ __forceinline__ double sum(double v, int lane) {
+        v = warp_sum(v);
+        if (P == 1) return v;
+        if (lane == 0) xch[slot * P + part] = v;
+        sync();
+        const double r = xch[slot * P] + xch[slot * P + 1];
+        ++slot;
+        return r;
+    }
+    __device__ __forceinline__ float max(float v, int lane) {
+        v = warp_max(v);
+        if (P == 1) return v;
+        if (lane == 0) xch[slot * P + part] = static_cast<double>(v);
+        sync();
+        const float r = fmaxf(static_cast<float>(xch[slot * P]), static_cast<float>(xch[slot * P + 1]));
+        ++slot;
+        return r;
+    }
+};
+
+// Layer norm of one row, this warp holding the float4 chunks v[c] = elements off + (c * 32 +
+// lane) * 4 .. + 3 of a row of d values.
+template <int C, int P>
+__device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, int off, const float* __restrict__ gamma,
+                                                const float* __restrict__ beta, float eps, int lane,
+                                                RowReduce<P>& red) {
     double s = 0.0;
 #pragma unroll
     for (int c = 0; c < C; ++c)
         s += (static_cast<double>(v[c].x) + static_cast<double>(v[c].y)) +
              (static_cast<double>(v[c].z) + static_cast<double>(v[c].w));
-    const double mean = warp_sum(s) / d;
+    const double mean = red.sum(s, lane) / d;
     double q = 0.0;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
         const double a = v[c].x - mean, b = v[c].y - mean, e = v[c].z - mean, f = v[c].w - mean;
         q += (a * a + b * b) + (e * e + f * f);
     }
-    const double var = warp_sum(q) / d;
+    const double var = red.sum(q, lane) / d;
     const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-        const int i = (c * 32 + lane) * 4;
+        const int i = off + (c * 32 + lane) * 4;
         const float4 g = *reinterpret_cast<const float4*>(gamma + i);
         const float4 b = *reinterpret_cast<const float4*>(beta + i);
         v[c].x = __fadd_rn(__fmul_rn(static_cast<float>((v[c].x - mean) * rstd), g.x), b.x);
@@ -84,17 +118,17 @@ __device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, const flo
     }
 }
 
-template <int C>
-__device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int lane, int8_t* hi, int8_t* lo,
-                                              float* scale_out) {
+template <int C, int P>
+__device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int off, int lane, int8_t* hi, int8_t* lo,
+                                              float* scale_out, bool write_scale, RowReduce<P>& red) {
     float amax = 0.0f;
 #pragma unroll
     for (int c = 0; c < C; ++c)
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c].x), fabsf(v[c].y)), fmaxf(fabsf(v[c].z), fabsf(v[c].w))));
-    const Scales s = row_scales(warp_max(amax));
+    const Scales s = row_scales(red.max(amax, lane));
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-        const int i = (c * 32 + lane) * 4;
+        const int i = off + (c * 32 + lane) * 4;
         char4 h, l;
         split(v[c].x, s.d, s.id, s.id_lo, h.x, l.x);
         split(v[c].y, s.d, s.id, s.id_lo, h.y, l.y);
@@ -103,32 +137,42 @@ __device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int lane, in
         *reinterpret_cast<char4*>(hi + i) = h;
         *reinterpret_cast<char4*>(lo + i) = l;
     }
-    if (lane == 0) *scale_out = s.d;
+    if (write_scale && lane == 0) *scale_out = s.d;
 }
 
 // y = LN_a(x) [written to y_out if given]; z = LN_b(y) if gamma_b given, else z = y;
-// z quantized into q if q.hi given. One warp per row of d = 128 * C values.
-template <int C>
-__global__ void ln_chain_kernel(const float* __restrict__ x, int m, int d, const float* __restrict__ ga,
-                                const float* __restrict__ ba, float* __restrict__ y_out,
-                                const float* __restrict__ gb, const float* __restrict__ bb, QuantAct q,
-                                float eps) {
-    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
+// z quantized into q if q.hi given. P warps per row of d = 128 * C values (each holding C / P
+// float4 per lane), 8 warps per block.
+template <int C, int P>
+__global__ void __launch_bounds__(256) ln_chain_kernel(const float* __restrict__ x, int m, int d,
+                                                       const float* __restrict__ ga, const float* __restrict__ ba,
+                                                       float* __restrict__ y_out, const float* __restrict__ gb,
+                                                       const float* __restrict__ bb, QuantAct q, float eps) {
+    constexpr int CW = C / P;
+    constexpr int kRows = 8 / P;
+    __shared__ double xch[kRows][RowReduce<P>::kSlots * P];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int grp = warp / P;
+    const int row = blockIdx.x * kRows + grp;
+    RowReduce<P> red{xch[grp], warp % P, 1 + grp, 0};
+    // A group past the last row still takes part in its own barriers: both of its warps skip
+    // together, so nothing waits on them.
     if (row >= m) return;
-    const float* xr = x + static_cast<int64_t>(row) * d;
-    float4 v[C];
+    const int off = (warp % P) * CW * 128;
+    const float* xr = x + static_cast<int64_t>(row) * d + off;
+    float4 v[CW];
 #pragma unroll
-    for (int c = 0; c < C; ++c) v[c] = *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4);
-    if (ga) layer_norm_regs<C>(v, d, ga, ba, eps, lane);
+    for (int c = 0; c < CW; ++c) v[c] = *reinterpret_cast<const float4*>(xr + (c * 32 + lane) * 4);
+    if (ga) layer_norm_regs<CW, P>(v, d, off, ga, ba, eps, lane, red);
     if (y_out) {
-        float* yr = y_out + static_cast<int64_t>(row) * d;
+        float* yr = y_out + static_cast<int64_t>(row) * d + off;
 #pragma unroll
-        for (int c = 0; c < C; ++c) *reinterpret_cast<float4*>(yr + (c * 32 + lane) * 4) = v[c];
+        for (int c = 0; c < CW; ++c) *reinterpret_cast<float4*>(yr + (c * 32 + lane) * 4) = v[c];
     }
-    if (gb) layer_norm_regs<C>(v, d, gb, bb, eps, lane);
-    if (q.hi) quantize_regs<C>(v, lane, q.hi + static_cast<int64_t>(row) * q.ld, q.lo + static_cast<int64_t>(row) * q.ld,
-                               q.scale + row);
+    if (gb) layer_norm_regs<CW, P>(v, d, off, gb, bb, eps, lane, red);
+    if (q.hi)
+        quantize_regs<CW, P>(v, off, lane, q.hi + static_cast<int64_t>(row) * q.ld,
+                             q.lo + static_cast<int64_t>(row) * q.ld, q.scale + row, warp % P == 0, red);
 }
 
 // Softmax of each row (n values, rows ld apart) in place, then its split-int8 quantization.
@@ -177,27 +221,27 @@ __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t r
 // GLU + depthwise convolution (taps in order from the bias, skipping frames outside the
 // utterance) + SiLU, the GLU gate and the SiLU with the fast exponential and division (a few
 // ulp from a / (1 + expf(-b)); the conversion unit would otherwise bound the kernel). Task t
-// covers output frames [out_first, out_first + count <= 32) of one
-// utterance; each thread owns one channel. The GLU values of every input frame the task reads
-// are staged first -- eight frames' loads in flight at a time -- in a shared column per thread,
-// then each output frame sums its K taps from there.
+// covers output frames [out_first, out_first + count <= 32) of one utterance; each thread owns
+// one channel. The GLU values of every input frame the task reads are staged first -- eight
+// frames' loads in flight at a time -- in a shared column per thread, frames outside the
+// utterance as zeros: adding w * 0 leaves the sum bit for bit as skipping the tap does (the
+// weights are finite), so the taps need no bounds checks. S is the stride of every task.
 constexpr int kConvSpan = 32;  // output frames per task (set by the host's task list)
 
-template <int K>
+template <int K, int S>
 __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __restrict__ big, int cc,
                                                               const ConvTask* __restrict__ tasks,
                                                               const float* __restrict__ w,
                                                               const float* __restrict__ bias,
                                                               float* __restrict__ out) {
     constexpr int half = K / 2;
-    constexpr int kFrames = 2 * (kConvSpan - 1) + K;  // input frames of a stride-2 span
+    constexpr int kFrames = S * (kConvSpan - 1) + K;  // input frames of a span
     __shared__ float glu[kFrames][128];
     const ConvTask t = tasks[blockIdx.y];
     const int c = blockIdx.x * 128 + threadIdx.x;
     const bool live = c < cc;
-    const int s = t.stride;
-    const int f_lo = s * t.out_first - half;
-    const int nf = s * (t.count - 1) + K;
+    const int f_lo = S * t.out_first - half;
+    const int nf = S * (t.count - 1) + K;
     const int64_t two_cc = 2 * static_cast<int64_t>(cc);
     for (int i0 = 0; i0 < nf; i0 += 8) {
         float a[8], b[8];
@@ -218,15 +262,14 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
 #pragma unroll
     for (int j = 0; j < K; ++j) wk[j] = __ldg(w + j * cc + c);
     const float bc = __ldg(bias + c);
-    for (int r = t.out_first; r < t.out_first + t.count; ++r) {
+    float* orow = out + static_cast<int64_t>(t.out_row + t.out_first) * cc + c;
+    for (int r = 0; r < t.count; ++r) {
+        const float* g = &glu[S * r][threadIdx.x];
         float acc = bc;
 #pragma unroll
-        for (int j = 0; j < K; ++j) {
-            const int f = s * r + j - half;
-            if (f >= 0 && f < t.in_len) acc = __fadd_rn(acc, __fmul_rn(wk[j], glu[f - f_lo][threadIdx.x]));
-        }
+        for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(wk[j], g[j * 128]));
         acc = __fdividef(acc, __fadd_rn(1.0f, __expf(-acc)));
-        out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
+        orow[static_cast<int64_t>(r) * cc] = acc;
     }
 }
 
@@ -336,20 +379,18 @@ cudaError_t ln_chain(const float* x, int m, int d, const float* ga, const float*
                      const float* gb, const float* bb, const QuantAct* q, cudaStream_t stream) {
     if (m <= 0) return cudaSuccess;
     QuantAct qa = q ? *q : QuantAct();
-    constexpr int kWarps = 8;
-    const int grid = (m + kWarps - 1) / kWarps;
     const float eps = 1e-5f;
-#define TELMO_LN_CASE(C)                                                                          \
-    case C:                                                                                       \
-        ln_chain_kernel<C><<<grid, kWarps * 32, 0, stream>>>(x, m, d, ga, ba, y_out, gb, bb, qa, eps); \
+#define TELMO_LN_CASE(C, P)                                                                               \
+    case C:                                                                                               \
+        ln_chain_kernel<C, P><<<(m + 8 / P - 1) / (8 / P), 256, 0, stream>>>(x, m, d, ga, ba, y_out, gb, bb, qa, eps); \
         break;
     switch (d / 128) {
-        TELMO_LN_CASE(1)
-        TELMO_LN_CASE(2)
-        TELMO_LN_CASE(4)
-        TELMO_LN_CASE(8)
-        TELMO_LN_CASE(12)
-        TELMO_LN_CASE(16)
+        TELMO_LN_CASE(1, 1)
+        TELMO_LN_CASE(2, 1)
+        TELMO_LN_CASE(4, 1)
+        TELMO_LN_CASE(8, 2)
+        TELMO_LN_CASE(12, 2)
+        TELMO_LN_CASE(16, 2)
         default: return cudaErrorInvalidValue;
     }
 #undef TELMO_LN_CASE
@@ -364,19 +405,26 @@ cudaError_t softmax_quant(float* x, int m, int n, int64_t ld, const QuantAct& q,
     return cudaGetLastError();
 }
 
-cudaError_t glu_dwconv_silu(const float* big, int cc, int k, const ConvTask* tasks, int n_tasks, const float* w,
-                            const float* bias, float* out, cudaStream_t stream) {
+cudaError_t glu_dwconv_silu(const float* big, int cc, int k, int stride, const ConvTask* tasks, int n_tasks,
+                            const float* w, const float* bias, float* out, cudaStream_t stream) {
     if (n_tasks <= 0) return cudaSuccess;
     const int threads = 128;
     dim3 grid((cc + threads - 1) / threads, n_tasks);
+#define TELMO_CONV_CASE(K)                                                                               \
+    case K:                                                                                              \
+        if (stride == 1) glu_dwconv_silu_kernel<K, 1><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); \
+        else glu_dwconv_silu_kernel<K, 2><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out);         \
+        break;
+    if (stride != 1 && stride != 2) return cudaErrorInvalidValue;
     switch (k) {
-        case 3: glu_dwconv_silu_kernel<3><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
-        case 5: glu_dwconv_silu_kernel<5><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
-        case 7: glu_dwconv_silu_kernel<7><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
-        case 9: glu_dwconv_silu_kernel<9><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
-        case 15: glu_dwconv_silu_kernel<15><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); break;
+        TELMO_CONV_CASE(3)
+        TELMO_CONV_CASE(5)
+        TELMO_CONV_CASE(7)
+        TELMO_CONV_CASE(9)
+        TELMO_CONV_CASE(15)
         default: glu_dwconv_silu_any_kernel<<<grid, threads, 0, stream>>>(big, cc, k, tasks, w, bias, out);
     }
+#undef TELMO_CONV_CASE
     return cudaGetLastError();
 }
 

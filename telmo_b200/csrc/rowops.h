@@ -27,8 +27,9 @@ cudaError_t ln_chain(const float* x, int m, int d, const float* ga, const float*
 // Row softmax of x [m, n] (rows ld apart) in place, then its split-int8 quantization into q.
 cudaError_t softmax_quant(float* x, int m, int n, int64_t ld, const QuantAct& q, cudaStream_t stream);
 
-// out[row, cc] = SiLU(dw_b + sum_j dw_w[j] * GLU(big)[frame]) for every task.
-cudaError_t glu_dwconv_silu(const float* big, int cc, int k, const ConvTask* tasks, int n_tasks,
+// out[row, cc] = SiLU(dw_b + sum_j dw_w[j] * GLU(big)[frame]) for every task; every task of a
+// launch has the given stride (1, or 2 for the blocks that halve the frame rate).
+cudaError_t glu_dwconv_silu(const float* big, int cc, int k, int stride, const ConvTask* tasks, int n_tasks,
                             const float* w, const float* bias, float* out, cudaStream_t stream);
 
 // out[r] = (x[src_row[r]] + x[src_row[r] + 1]) / 2.
