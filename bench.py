@@ -178,8 +178,14 @@ class GraniteWorkload:
         self.dev_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32,
                                       device="cuda")
         self.host_tokens = torch.empty(3 * frames + 3, dtype=torch.int32).pin_memory()
+        self.host_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32).pin_memory()
         self.bi = int(packed.nbytes)
         self.bo = 0
+        # End to end: two device audio buffers, so the next batch's host-to-device copy (on its
+        # own stream) runs while the current batch is transcribed.
+        biggest = max(n for _, n in self.offsets)
+        self.e2e_audio = [torch.empty(biggest, dtype=torch.float32, device="cuda") for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream()
 
     def step_gpu(self):
         for b, (at, n) in zip(self.batches, self.offsets):
@@ -187,14 +193,37 @@ class GraniteWorkload:
                                          self.dev_tokens, self.dev_counts)
 
     def step_e2e(self):
+        """Every batch through telmo_granite_transcribe_device with its audio copied from pinned
+        host memory and its tokens and counts copied back; batch i + 1's audio copy overlaps
+        batch i's transcription."""
+        import torch
+        main = torch.cuda.current_stream()
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+
+        def copy_in(i):
+            at, n = self.offsets[i]
+            with torch.cuda.stream(self.copy_stream):
+                if i >= 2:
+                    self.copy_stream.wait_event(free[i % 2])
+                self.e2e_audio[i % 2][:n].copy_(self.host_audio[at:at + n], non_blocking=True)
+                copied[i % 2].record(self.copy_stream)
+
         bo = 0
-        for b, (at, n) in zip(self.batches, self.offsets):
-            toks = self.model.transcribe_packed(self.host_audio[at:at + n], self.samples[b],
-                                                tokens_buf=self.host_tokens)
-            bo += sum(3 * 4 * self.model.frames_for_samples(int(self.samples[u])) for u in b)
-            bo += 4 * len(b)
+        copy_in(0)
+        for i, b in enumerate(self.batches):
+            n = self.offsets[i][1]
+            main.wait_event(copied[i % 2])
+            if i + 1 < len(self.batches):
+                copy_in(i + 1)
+            frames = self.model.transcribe_device(self.e2e_audio[i % 2][:n], self.samples[b],
+                                                  self.dev_tokens, self.dev_counts)
+            free[i % 2].record(main)
+            nt = 3 * int(frames.sum())
+            self.host_tokens[:nt].copy_(self.dev_tokens[:nt], non_blocking=True)
+            self.host_counts[:len(b)].copy_(self.dev_counts[:len(b)], non_blocking=True)
+            bo += 4 * nt + 4 * len(b)
         self.bo = bo
-        return toks
 
     def units_per_step(self):
         return self.rank_seconds
@@ -331,9 +360,9 @@ class ParakeetWorkload(GraniteWorkload):
     def step_e2e(self):
         bo = 0
         for b, (at, n) in zip(self.batches, self.offsets):
-            toks = self.model.transcribe_packed(self.host_audio[at:at + n], self.samples[b],
-                                                tokens_buf=self.host_tokens)
-            bo += 12 * sum(len(t) for t in toks) + 4 * len(b)
+            toks, counts, _ = self.model.transcribe_arrays(self.host_audio[at:at + n], self.samples[b],
+                                                           tokens_buf=self.host_tokens)
+            bo += 12 * int(counts.sum()) + 4 * len(b)
         self.bo = bo
         return toks
 

@@ -158,6 +158,18 @@ class Granite:
                           tokens_buf: np.ndarray = None):
         """As transcribe, with the utterances already packed one after another (host memory;
         a pinned buffer copies fastest)."""
+        tok, counts, frames = self.transcribe_arrays(samples, lengths, stream, tokens_buf)
+        out, at = [], 0
+        for u in range(len(counts)):
+            t = tok[3 * at:3 * at + 3 * counts[u]].reshape(-1, 3)
+            out.append([Token(int(a), int(b), int(c)) for a, b, c in t])
+            at += int(frames[u])
+        return out
+
+    def transcribe_arrays(self, samples, lengths, stream=None, tokens_buf=None):
+        """telmo_granite_transcribe as it is: (tokens, counts, frames) host arrays, utterance u's
+        counts[u] (id, frame, duration) triples at element 3 * (frames[0] + ... + frames[u-1])
+        of tokens."""
         lengths = np.ascontiguousarray(lengths, dtype=np.int64)
         n = lengths.size
         cap = sum(self.frames_for_samples(int(x)) for x in lengths)
@@ -170,12 +182,7 @@ class Granite:
                                                    counts.ctypes.data, frames.ctypes.data,
                                                    _stream(stream)), self.ctx.handle)
         tok = tokens if isinstance(tokens, np.ndarray) else tokens.numpy()
-        out, at = [], 0
-        for u in range(n):
-            t = tok[3 * at:3 * at + 3 * counts[u]].reshape(-1, 3)
-            out.append([Token(int(a), int(b), int(c)) for a, b, c in t])
-            at += int(frames[u])
-        return out
+        return tok.reshape(-1), counts, frames
 
     def transcribe_device(self, samples, lengths, tokens, counts, stream=None):
         """Device-resident variant: samples, tokens [3 * frames] (int32) and counts are CUDA

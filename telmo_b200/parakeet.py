@@ -136,6 +136,12 @@ class Parakeet:
     def transcribe_packed(self, samples, lengths, stream=None, tokens_buf=None):
         """As transcribe, with the utterances packed one after another in host memory (a pinned
         buffer copies fastest)."""
+        tok, counts, _ = self.transcribe_arrays(samples, lengths, stream, tokens_buf)
+        return _split(tok, counts)
+
+    def transcribe_arrays(self, samples, lengths, stream=None, tokens_buf=None):
+        """telmo_parakeet_transcribe as it is: (tokens [total, 3], counts, frames) host arrays,
+        the triples packed utterance after utterance."""
         lengths = np.ascontiguousarray(lengths, dtype=np.int64)
         n = lengths.size
         cap = 3 * self.config["max_symbols"] * sum(frames_for_samples(int(x)) for x in lengths) + 3
@@ -148,7 +154,7 @@ class Parakeet:
                                                     counts.ctypes.data, frames.ctypes.data,
                                                     _stream(stream)), self.ctx.handle)
         tok = tokens if isinstance(tokens, np.ndarray) else tokens.numpy()
-        return _split(tok.reshape(-1)[:3 * int(counts.sum())].reshape(-1, 3), counts)
+        return tok.reshape(-1)[:3 * int(counts.sum())].reshape(-1, 3), counts, frames
 
     def transcribe_device(self, samples, lengths, tokens, counts, stream=None):
         """Device-resident variant: samples, tokens (int32, 3 * max_symbols * frames) and counts
