@@ -86,13 +86,16 @@ __device__ __forceinline__ float exact_i2f(uint32_t bits) {
 
 // Step for step what oracle_epilogue_x2 computes, with no contraction into FMA. A missing bias
 // is passed as 0, which leaves every value unchanged (the sums are never -0). SiLU uses the
-// fast exponential and division (a few ulp from v / (1 + expf(-v))), the conversion unit's
-// two operations per value instead of about six.
+// fast exponential and division (a few ulp from v / (1 + expf(-v))). The conversion unit does
+// the two int-to-float conversions, except under SiLU, whose exponential and reciprocal already
+// take two of its slots per value; there the integer path above converts the low sum.
 template <int ACT>
 __device__ __forceinline__ float epilogue_value(uint32_t acc_hi, uint32_t acc_lo, float rs, float ws,
                                                 float bias, float scale) {
     const float inv254 = 1.0f / 254.0f;
-    float v = __fadd_rn(exact_i2f(acc_hi), __fmul_rn(exact_i2f(acc_lo), inv254));
+    const float fh = __int2float_rn(static_cast<int32_t>(acc_hi));
+    const float fl = ACT == kActSilu ? exact_i2f(acc_lo) : __int2float_rn(static_cast<int32_t>(acc_lo));
+    float v = __fadd_rn(fh, __fmul_rn(fl, inv254));
     v = __fmul_rn(v, rs);
     v = __fmul_rn(v, ws);
     v = __fadd_rn(v, bias);
