@@ -136,19 +136,47 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&hi)[32], const uint
     }
 }
 
-template <int ACT>
-__device__ __forceinline__ void compute_chunk(const uint32_t (&hi)[32], const uint32_t (&lo)[32], float my_rs,
-                                              float ws, float bs, float scale, float (&v)[32]) {
+// The epilogue of a staged chunk, step for step as epilogue_value:
+// v = ((float)hi + (float)lo * (1/254)) * rs * ws [+ bias] [act] [* scale], the chunk's 32 row
+// scales in registers. A bias of 0 and a scale of 1 change no value and are skipped.
+template <int ACT, bool BIAS, bool SCALE>
+__device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[32], const uint32_t (&lo)[32],
+                                               const float (&rs)[32], float ws, float bs, float scale,
+                                               float (&v)[32]) {
+    const float inv254 = 1.0f / 254.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-        v[j] = epilogue_value<ACT>(hi[j], lo[j], __shfl_sync(0xffffffffu, my_rs, j), ws, bs, scale);
+    for (int j = 0; j < 32; ++j) {
+        const float fh = __int2float_rn(static_cast<int32_t>(hi[j]));
+        const float fl = ACT == kActSilu ? exact_i2f(lo[j]) : __int2float_rn(static_cast<int32_t>(lo[j]));
+        float x = __fadd_rn(fh, __fmul_rn(fl, inv254));
+        x = __fmul_rn(__fmul_rn(x, rs[j]), ws);
+        if (BIAS) x = __fadd_rn(x, bs);
+        if (ACT == kActRelu) x = fmaxf(x, 0.0f);
+        if (ACT == kActSilu) x = __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
+        if (SCALE) x = __fmul_rn(x, scale);
+        v[j] = x;
+    }
 }
 
-__device__ __forceinline__ void compute_chunk_any(int act, const uint32_t (&hi)[32], const uint32_t (&lo)[32],
-                                                  float my_rs, float ws, float bs, float scale, float (&v)[32]) {
-    if (act == kActNone) compute_chunk<kActNone>(hi, lo, my_rs, ws, bs, scale, v);
-    else if (act == kActRelu) compute_chunk<kActRelu>(hi, lo, my_rs, ws, bs, scale, v);
-    else compute_chunk<kActSilu>(hi, lo, my_rs, ws, bs, scale, v);
+template <int ACT>
+__device__ __forceinline__ void compute_chunk_act(bool bias, bool scale_on, const uint32_t (&hi)[32],
+                                                  const uint32_t (&lo)[32], const float (&rs)[32], float ws,
+                                                  float bs, float scale, float (&v)[32]) {
+    if (bias) {
+        if (scale_on) compute_chunk2<ACT, true, true>(hi, lo, rs, ws, bs, scale, v);
+        else compute_chunk2<ACT, true, false>(hi, lo, rs, ws, bs, scale, v);
+    } else {
+        if (scale_on) compute_chunk2<ACT, false, true>(hi, lo, rs, ws, bs, scale, v);
+        else compute_chunk2<ACT, false, false>(hi, lo, rs, ws, bs, scale, v);
+    }
+}
+
+__device__ __forceinline__ void compute_chunk_any(int act, bool bias, bool scale_on, const uint32_t (&hi)[32],
+                                                  const uint32_t (&lo)[32], const float (&rs)[32], float ws,
+                                                  float bs, float scale, float (&v)[32]) {
+    if (act == kActNone) compute_chunk_act<kActNone>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
+    else if (act == kActRelu) compute_chunk_act<kActRelu>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
+    else compute_chunk_act<kActSilu>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
 }
 
 template <typename OutT>
@@ -283,6 +311,8 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         const int quad = warp & 3;  // TMEM lanes this warp may access: 32 * quad ..
         const int part = (warp - 2) / 4;
         const bool has_bias = p.bias != nullptr;
+        const bool scale_on = p.scale != 1.0f;
+        const bool rs_vec = (reinterpret_cast<uintptr_t>(p.row_scale) & 15) == 0;
         uint8_t* sbuf = staging + (warp - 2) * kStageOutBytes;
         int it = 0;
         for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
@@ -311,13 +341,30 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                 if (mc >= p.m) continue;
                 const float my_rs = (mc + lane < p.m) ? __ldg(p.row_scale + mc + lane) : 0.0f;
                 const int rows_valid = p.m - mc < 32 ? p.m - mc : 32;
+                // The chunk's 32 row scales in registers: broadcast 16-byte loads for a full,
+                // aligned chunk, else shuffles of the lanes' own loads.
+                float rs[32];
+                if (rows_valid == 32 && rs_vec) {
+                    const float4* r4 = reinterpret_cast<const float4*>(p.row_scale + mc);
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const float4 t4 = __ldg(r4 + q4);
+                        rs[4 * q4] = t4.x;
+                        rs[4 * q4 + 1] = t4.y;
+                        rs[4 * q4 + 2] = t4.z;
+                        rs[4 * q4 + 3] = t4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) rs[j] = __shfl_sync(0xffffffffu, my_rs, j);
+                }
                 const int64_t off = static_cast<int64_t>(mc) * p.ldc + n;
                 if (p.out_path != kDirect) {
                     // Stage the 32 x 32 chunk (row = activation row, column = feature) and let one
                     // lane hand it to TMA; the previous chunk's store has read the buffer by the
                     // time this chunk's values are computed, almost always.
                     float v[32];
-                    compute_chunk_any(p.act, hi, lo, my_rs, ws, bs, p.scale, v);
+                    compute_chunk_any(p.act, has_bias, scale_on, hi, lo, rs, ws, bs, p.scale, v);
                     if (lane == 0) bulk_wait_read<0>();
                     __syncwarp();
                     if (p.out_kind == kOutF32) {
@@ -349,7 +396,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     }
                 } else if (p.out_kind == kOutF16Split) {
                     float v[32];
-                    compute_chunk_any(p.act, hi, lo, my_rs, ws, bs, p.scale, v);
+                    compute_chunk_any(p.act, has_bias, scale_on, hi, lo, rs, ws, bs, p.scale, v);
                     __half* oh = static_cast<__half*>(p.out) + off;
                     __half* ol = oh + static_cast<int64_t>(p.m) * p.ldc;
 #pragma unroll
