@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -40,13 +41,20 @@ constexpr int BK = 128;  // bytes = int8 elements per stage along K (one 128-byt
 constexpr int UMMA_K = 32;
 constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each on half the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kStages = 4;
 constexpr int kTileBytes = 128 * BK;  // one 128-row operand box
-constexpr int kStageBytes = 3 * kTileBytes;
 constexpr int kTmemCols = 2 * 2 * BM;  // 2 buffers x (hi, lo) x BM columns
 constexpr int kStageOutBytes = 32 * 32 * 4;   // one 32 x 32 f32 output chunk
 constexpr int kOutStaging = kEpiWarps * kStageOutBytes;  // one buffer per epilogue warp
-constexpr int kSmemBytes = kStages * kStageBytes + kOutStaging + 1024 + 256;
+
+// Pipeline shape per variant: CG = 1, one CTA per 128-feature tile, stages of W + A_hi + A_lo
+// (48 KB); CG = 2, a CTA pair per 256-feature tile, each CTA staging its 128 weight rows and
+// one activation level (32 KB), so the same shared memory holds six stages.
+template <int CG>
+struct Shape {
+    static constexpr int kStageBytes = (CG == 1 ? 3 : 2) * kTileBytes;
+    static constexpr int kStages = CG == 1 ? 4 : 6;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kOutStaging + 1024 + 256;
+};
 
 // How the epilogue writes: TMA store of staged chunks, TMA reduce-add (accumulate), or direct
 // global stores when the output's alignment rules out TMA.
@@ -195,10 +203,13 @@ __device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_
     }
 }
 
+template <int CG>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
                  const __grid_constant__ CUtensorMap map_lo, const __grid_constant__ CUtensorMap map_out,
                  const __grid_constant__ CUtensorMap map_out_lo, const Params p) {
+    constexpr int kStages = Shape<CG>::kStages;
+    constexpr int kStageBytes = Shape<CG>::kStageBytes;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + kStages * kStageBytes;
@@ -210,7 +221,12 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_m = (p.m + BM - 1) / BM, num_n = (p.n + BN - 1) / BN;
+    // A tile is BM activation rows x CG * BN features; CTA rank r of a pair owns features
+    // n0 + r * BN ...; tiles run over "units" (single CTAs or pairs).
+    const uint32_t rank = CG == 2 ? cluster_rank() : 0;
+    const bool leader = rank == 0;
+    const int unit = blockIdx.x / CG, units = gridDim.x / CG;
+    const int num_m = (p.m + BM - 1) / BM, num_n = (p.n + CG * BN - 1) / (CG * BN);
     const int tiles = num_m * num_n;
     const int kblocks = (p.k + BK - 1) / BK;
 
@@ -221,7 +237,9 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], kEpiWarps * 32);
+            // CG = 1: every epilogue thread arrives; CG = 2: one lane per epilogue warp of both
+            // CTAs arrives on the pair's first CTA's barrier.
+            mbar_init(&tmem_empty[b], CG == 1 ? kEpiWarps * 32 : 2 * kEpiWarps);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -232,11 +250,17 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         if (p.out_path != kDirect && p.out_kind == kOutF16Split) prefetch_tensormap(&map_out_lo);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_base_slot, kTmemCols);
-        tmem_relinquish();
+        if (CG == 1) {
+            tmem_alloc(tmem_base_slot, kTmemCols);
+            tmem_relinquish();
+        } else {
+            tmem_alloc_pair(tmem_base_slot, kTmemCols);
+            tmem_relinquish_pair();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (CG == 2) cluster_sync();  // both CTAs' barriers exist before either signals the other's
     tc_fence_after();
     const uint32_t tmem_base = *tmem_base_slot;
 
@@ -248,8 +272,8 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+            for (int t = unit; t < tiles && !*abort_flag; t += units) {
+                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * CG * BN + static_cast<int>(rank) * BN;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) {
                         record_error(p.error, kErrWaitTimeout);
@@ -257,21 +281,32 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                         break;
                     }
                     uint8_t* st = smem + stage * kStageBytes;
-                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
-                    tma_load_2d(&map_w, &full[stage], st, kb * BK, n0);
-                    tma_load_2d(&map_hi, &full[stage], st + kTileBytes, kb * BK, m0);
-                    tma_load_2d(&map_lo, &full[stage], st + 2 * kTileBytes, kb * BK, m0);
+                    if (CG == 1) {
+                        mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                        tma_load_2d(&map_w, &full[stage], st, kb * BK, n0);
+                        tma_load_2d(&map_hi, &full[stage], st + kTileBytes, kb * BK, m0);
+                        tma_load_2d(&map_lo, &full[stage], st + 2 * kTileBytes, kb * BK, m0);
+                    } else {
+                        // Both CTAs' loads count on the first CTA's barrier, which expects them all.
+                        // The first CTA stages the high level (B columns 0..127), the second the low.
+                        const uint32_t bar = cluster_addr(&full[stage], 0);
+                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+                        tma_load_2d_pair(&map_w, bar, st, kb * BK, n0);
+                        tma_load_2d_pair(leader ? &map_hi : &map_lo, bar, st + kTileBytes, kb * BK, m0);
+                    }
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issuer ----------------------------------------------------------------------
-        constexpr uint32_t idesc = idesc_i8(128, 2 * BM);
+        // ---- MMA issuer (the pair's first CTA issues for both) -----------------------------
+        constexpr uint32_t idesc = idesc_i8(CG * 128, 2 * BM);
         int stage = 0;
         uint32_t phase = 0;
         int it = 0;
-        for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const uint32_t peer_empty0 = CG == 2 ? cluster_addr(&empty[0], 1) : 0;
+        const uint32_t peer_tfull0 = CG == 2 ? cluster_addr(&tmem_full[0], 1) : 0;
+        for (int t = unit; leader && t < tiles && !*abort_flag; t += units, ++it) {
             const int buf = it & 1;
             const uint32_t use = static_cast<uint32_t>(it >> 1);
             if (!mbar_wait(&tmem_empty[buf], (use & 1) ^ 1)) {
@@ -289,10 +324,17 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     const uint32_t w = smem_u32(smem + stage * kStageBytes);
                     const uint32_t x = w + kTileBytes;  // hi rows, then lo rows: N = 256
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
-                        mma_i8(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc,
-                               (kb > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(&empty[stage]);
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (CG == 1) mma_i8(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc, acc);
+                        else mma_i8_pair(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc, acc);
+                    }
+                    if (CG == 1) {
+                        mma_commit(&empty[stage]);
+                    } else {
+                        mma_commit_pair(smem_u32(&empty[stage]));
+                        mma_commit_pair(peer_empty0 + static_cast<uint32_t>(stage * sizeof(uint64_t)));
+                    }
                 }
                 __syncwarp();
                 if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -302,7 +344,14 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                 *abort_flag = 1;
                 break;
             }
-            if (lane == 0) mma_commit(&tmem_full[buf]);
+            if (lane == 0) {
+                if (CG == 1) {
+                    mma_commit(&tmem_full[buf]);
+                } else {
+                    mma_commit_pair(smem_u32(&tmem_full[buf]));
+                    mma_commit_pair(peer_tfull0 + static_cast<uint32_t>(buf * sizeof(uint64_t)));
+                }
+            }
             __syncwarp();
         }
     } else {
@@ -315,10 +364,11 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         const bool rs_vec = (reinterpret_cast<uintptr_t>(p.row_scale) & 15) == 0;
         uint8_t* sbuf = staging + (warp - 2) * kStageOutBytes;
         int it = 0;
-        for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const uint32_t tempty0 = CG == 2 ? cluster_addr(&tmem_empty[0], 0) : 0;
+        for (int t = unit; t < tiles && !*abort_flag; t += units, ++it) {
             const int buf = it & 1;
             const uint32_t use = static_cast<uint32_t>(it >> 1);
-            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * CG * BN + static_cast<int>(rank) * BN;
             const int n = n0 + quad * 32 + lane;
             const bool n_ok = n < p.n;
             const float ws = n_ok ? __ldg(p.w_scale + n) : 0.0f;
@@ -425,16 +475,25 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tmem_empty[buf]);
+            if (CG == 1) {
+                mbar_arrive(&tmem_empty[buf]);
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(buf * sizeof(uint64_t)));
+            }
         }
         if (lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
     __syncthreads();
+    // A pair's CTAs leave together: the first CTA's MMAs read the second's shared memory and
+    // write its TMEM, and the second's loads signal the first's barriers.
+    if (CG == 2) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        if (CG == 1) tmem_dealloc(tmem_base, kTmemCols);
+        else tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -510,8 +569,11 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !(configured >> dev & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Shape<1>::kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_i8x2_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Shape<2>::kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= uint64_t(1) << dev;
     }
@@ -532,9 +594,30 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
         path = kDirect;
     Params p{g.m, w.n, w.k, g.a.scale, w.scales, g.bias, g.act, g.scale, g.accumulate,
              g.out, g.ldc, g.out_kind, path, g.error};
+    // Products of at least 256 features run on CTA pairs (each MMA spans both SMs' tensor
+    // cores; each CTA stages a third less per multiply-add), narrower ones on single CTAs.
+    if (w.n >= 2 * BN) {
+        const int tiles = ((g.m + BM - 1) / BM) * ((w.n + 2 * BN - 1) / (2 * BN));
+        const int pairs = std::min(tiles, num_sms() / 2);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Shape<2>::kSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8x2_kernel<2>, mw, mh, ml, mo, mo_lo, p);
+        if (e != cudaSuccess) return e;
+        return cudaGetLastError();
+    }
     const int tiles = ((g.m + BM - 1) / BM) * ((w.n + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8x2_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, p);
+    gemm_i8x2_kernel<1><<<grid, kThreads, Shape<1>::kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, p);
     return cudaGetLastError();
 }
 
