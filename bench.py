@@ -14,7 +14,8 @@ Workloads (seeded synthetic data, telmo_b200/synthetic.py):
            the Parakeet-TDT-shaped int8 model: 128-bin log-mel, 8x convolutional subsampling,
            24-layer FastConformer encoder, greedy TDT decoding (token and duration per step),
            sharded and batched as granite.
-  linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias.
+  linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias
+           (--shape M,K,N for another product shape with the same distributions).
 
 `--impl reference` times the reference's CPU path for the same workload: the oracle's C
 restatement of telmo's CPU path (the reference is Rust and cannot be built here) on all host
@@ -388,9 +389,15 @@ class LinearWorkload:
     metric = "int8 linear TOPS (config 1: A f32 [1500,1024] x W int8 [4096,1024] + bias, f32 out)"
     unit = "TOPS"
 
-    def __init__(self, rank, world):
+    def __init__(self, rank, world, shape=None):
         from telmo_b200 import synthetic
-        self.a, (self.values, self.scales, self.n, self.k), self.bias = synthetic.config1()
+        if shape:  # another product shape (M, K, N) with config 1's distributions
+            m, k, n = shape
+            self.a, (self.values, self.scales, self.n, self.k), self.bias = synthetic.config1(m=m, k=k, n=n)
+            self.name = f"linear-{m}x{k}x{n}"
+            self.metric = f"int8 linear TOPS (A f32 [{m},{k}] x W int8 [{n},{k}] + bias, f32 out)"
+        else:
+            self.a, (self.values, self.scales, self.n, self.k), self.bias = synthetic.config1()
         self.m = self.a.shape[0]
         self.ops = 2.0 * self.m * self.n * self.k
 
@@ -433,12 +440,16 @@ class LinearWorkload:
                            threads=threads)
 
     def cpu_sample(self, threads):
+        # At most 1500 rows of A per timing (the config-1 product), best of 5.
+        from oracle import oracle
+        rows = min(self.m, 1500)
+        a = self.a[:rows]
         best = float("inf")
         for _ in range(5):
             t0 = time.perf_counter()
-            self.cpu_step(threads)
+            oracle.linear_int8(a, self.values, self.scales, self.n, self.k, self.bias, threads=threads)
             best = min(best, time.perf_counter() - t0)
-        return self.ops / best / 1e12, "config-1 product, best of 5"
+        return 2.0 * rows * self.n * self.k / best / 1e12, f"{rows} rows of the product, best of 5"
 
 
 WORKLOADS = {"granite": GraniteWorkload, "parakeet": ParakeetWorkload, "linear": LinearWorkload}
@@ -450,6 +461,8 @@ def make_workload(args, rank, world):
         return GraniteWorkload(rank, world, n_utt=args.utterances or 4096)
     if args.workload == "parakeet":
         return ParakeetWorkload(rank, world, n_utt=args.utterances or 256)
+    if args.workload == "linear" and args.shape:
+        return LinearWorkload(rank, world, shape=tuple(int(x) for x in args.shape.split(",")))
     return WORKLOADS[args.workload](rank, world)
 
 
@@ -613,6 +626,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="granite")
+    ap.add_argument("--shape", default="",
+                    help="linear: M,K,N of another product (config 1's distributions), e.g. "
+                         "53000,1024,4096 for an encoder's feed-forward up-projection")
     ap.add_argument("--utterances", type=int, default=0,
                     help="utterances in the set (default: 4096 for granite, config 5; 256 for "
                          "parakeet, config 4; fewer for profiling)")
