@@ -178,3 +178,36 @@ def test_full_size_transcribe_matches_the_oracle(full, oracle_lib):
         assert _tokens_match([(t.id, t.frame, t.duration) for t in g], want, margin)
         compared += margin > 1e-2
     assert compared >= 1
+
+
+# ---- the benchmark's own weight distribution --------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def full_spec(ctx, oracle_lib):
+    from telmo_b200.parakeet import Parakeet
+    config = synthetic.parakeet_config()
+    entries = synthetic.parakeet_entries(config, seed=3, scales="spec")
+    return Parakeet.from_entries(ctx, config, entries), oracle_lib.Parakeet(config, entries)
+
+
+def test_benchmark_model_matches_the_oracle_before_it_diverges(full_spec, oracle_lib):
+    # The config-4 model exactly as bench.py builds it (per-row scales U(1e-3, 1e-2)). Like the
+    # Granite benchmark model it is chaotic: in the oracle itself a 1e-6 relative change of the
+    # features grows to 2.9e-4 relative L2 after layer 2, 7e-2 after layer 5 and 0.48 after
+    # layer 11, so no implementation that rounds differently from the reference can meet 2e-2 at
+    # its output. The subsampling and the first layer, before the divergence builds up, are held
+    # to the north star's bar (by layer 2 the GPU's split-int8 rounding has grown to about 4e-2).
+    import torch
+    gpu, ref = full_spec
+    utts = [synthetic.audio(s, seed=70 + i) for i, s in enumerate([4.0, 9.5])]
+    feats = [oracle_lib.parakeet_features(u) for u in utts]
+    rows = [f.shape[0] for f in feats]
+    for tap in (-2, 0):
+        out, frames = gpu.encode(torch.from_numpy(np.concatenate(feats)).cuda(), rows, tap_layer=tap)
+        gpu.ctx.check()
+        got = out.cpu().numpy()
+        at = 0
+        for f, fr in zip(feats, frames):
+            want = ref.encode(f, tap_layer=tap, threads=8)
+            assert rel_l2(got[at:at + fr], want) <= 2e-2, tap
+            at += fr
