@@ -48,6 +48,20 @@ int num_sms();
 cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream);
 
 // x f32 [m, k] (rows ldx floats apart) -> hi, lo, scale (the oracle's quantize_x2 rule).
+#ifdef __CUDACC__
+// One value's split-int8 pair: hi = round(x / d) clamped to [-127, 127], lo = round((x - hi d)
+// * 254 / d) clamped; id = 1 / d and id_lo = 254 / d as the row's quantizer computes them.
+__device__ __forceinline__ void quant_split_one(float x, float d, float id, float id_lo, int8_t& h8, int8_t& l8) {
+    float h = roundf(__fmul_rn(x, id));
+    h = fminf(fmaxf(h, -127.0f), 127.0f);
+    const float e = __fmaf_rn(-h, d, x);
+    float l = roundf(__fmul_rn(e, id_lo));
+    l = fminf(fmaxf(l, -127.0f), 127.0f);
+    h8 = static_cast<int8_t>(h);
+    l8 = static_cast<int8_t>(l);
+}
+#endif
+
 cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,
                         cudaStream_t stream);
 

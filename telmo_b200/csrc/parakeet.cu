@@ -529,9 +529,9 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     const int64_t ld_d = static_cast<int64_t>(round_up(d, 16)), ld_2h = static_cast<int64_t>(round_up(2 * h, 16));
     const size_t bytes = quant_bytes(M, ld_d) + piece<float>(static_cast<size_t>(M) * h) + quant_bytes(U, ld_2h) +
                          piece<float>(static_cast<size_t>(U) * ld_logits) + piece<float>(static_cast<size_t>(U) * L * 2 * h) +
-                         4 * piece<float>(static_cast<size_t>(U) * h) + piece<float>(static_cast<size_t>(U) * 2 * h) +
-                         piece<float>(static_cast<size_t>(U) * 4 * h) + piece<TdtState>(U) + 2 * piece<int>(U) +
-                         piece<int>(4) + piece<uint32_t>(3 * static_cast<size_t>(slots) + 3);
+                         2 * piece<float>(static_cast<size_t>(U) * h) + piece<float>(static_cast<size_t>(U) * 4 * h) +
+                         piece<TdtState>(U) + 2 * piece<int>(U) + piece<int>(4) +
+                         piece<uint32_t>(3 * static_cast<size_t>(slots) + 3);
     if (int rc = dec_arena.reserve(ctx, bytes)) return rc;
     Arena& A = dec_arena;
     const QuantAct q_enc = quant_piece(A, M, ld_d);
@@ -540,10 +540,7 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     float* logits = A.take<float>(static_cast<size_t>(U) * ld_logits);
     float* state = A.take<float>(static_cast<size_t>(U) * L * 2 * h);
     float* pred = A.take<float>(static_cast<size_t>(U) * h);
-    float* z = A.take<float>(static_cast<size_t>(U) * h);
-    float* last = A.take<float>(static_cast<size_t>(U) * h);
     float* fresh = A.take<float>(static_cast<size_t>(U) * h);
-    float* input = A.take<float>(static_cast<size_t>(U) * 2 * h);
     float* gates = A.take<float>(static_cast<size_t>(U) * 4 * h);
     TdtState* st_dev = A.take<TdtState>(U);
     int* predict_token = A.take<int>(U);
@@ -554,8 +551,6 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     if (int rc = ctx->cuda(cudaMemcpyAsync(st_dev, st.data(), sizeof(TdtState) * U, cudaMemcpyHostToDevice, s), "tdt"))
         return rc;
     if (int rc = ctx->cuda(cudaMemsetAsync(state, 0, sizeof(float) * U * L * 2 * h, s), "tdt")) return rc;
-    if (int rc = ctx->cuda(cudaMemsetAsync(input, 0, sizeof(float) * U * 2 * h, s), "tdt")) return rc;
-    if (int rc = ctx->cuda(cudaMemsetAsync(z, 0, sizeof(float) * U * h, s), "tdt")) return rc;
     // The joint's projection of every frame (src/parakeet.rs:1438-1449).
     if (int rc = quant(encoded, d, M, d, q_enc, s)) return rc;
     if (int rc = gemm(q_enc, M, enc_proj, enc_proj_b.p, enc_proj_out, h, kActNone, 1.0f, 0, s)) return rc;
@@ -564,33 +559,30 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
         ++launches;
         return ctx->cuda(e, what);
     };
-    // Parakeet::predict_rows (src/parakeet.rs:1523-1577) for the utterances with a token.
+    // Parakeet::predict_rows (src/parakeet.rs:1523-1577) for the utterances with a token, from
+    // the layer-0 input rows already quantized in qd; the new projections land in `fresh`.
     auto predict = [&](cudaStream_t st) -> int {
         for (int l = 0; l < L; ++l) {
-            if (int rc = rows_kernel(lstm_input(predict_token, U, h, l, L, embedding.p, state, input, st), "lstm input"))
-                return rc;
-            if (int rc = quant(input, 2 * h, U, 2 * h, qd, st)) return rc;
             if (int rc = gemm(qd, U, lstm[l], lstm_b[l].p, gates, 4 * h, kActNone, 1.0f, 0, st)) return rc;
-            if (int rc = rows_kernel(lstm_cell(predict_token, U, h, l, L, gates, state, st), "lstm cell")) return rc;
+            if (int rc = rows_kernel(lstm_cell_prep(predict_token, U, h, l, L, gates, state, qd, st), "lstm cell"))
+                return rc;
         }
-        if (int rc = rows_kernel(lstm_last(predict_token, U, h, L, state, last, st), "lstm last")) return rc;
-        if (int rc = quant(last, h, U, h, qd, st)) return rc;
-        if (int rc = gemm(qd, U, pred_proj, pred_proj_b.p, fresh, h, kActNone, 1.0f, 0, st)) return rc;
-        return rows_kernel(pred_commit(predict_token, U, h, fresh, pred, st), "pred commit");
+        return gemm(qd, U, pred_proj, pred_proj_b.p, fresh, h, kActNone, 1.0f, 0, st);
     };
     // One joint step for every utterance (src/parakeet.rs:1455-1510).
     auto step = [&](cudaStream_t st) -> int {
-        if (int rc = rows_kernel(tdt_joint_input(enc_proj_out, st_dev, U, h, pred, z, st), "joint input")) return rc;
-        if (int rc = quant(z, h, U, h, qd, st)) return rc;
+        if (int rc = rows_kernel(tdt_joint_prep(enc_proj_out, st_dev, U, h, predict_token, fresh, pred, qd, words, st),
+                                 "joint input"))
+            return rc;
         if (int rc = gemm(qd, U, joint, joint_b.p, logits, ld_logits, kActNone, 1.0f, 0, st)) return rc;
-        if (int rc = ctx->cuda(cudaMemsetAsync(words, 0, sizeof(int), st), "tdt")) return rc;
-        if (int rc = rows_kernel(tdt_decide(logits, ld_logits, c.vocab, c.blank, durations_dev, c.n_durations,
-                                            c.max_symbols, st_dev, U, raw, predict_token, words, st),
+        if (int rc = rows_kernel(tdt_decide_prep(logits, ld_logits, c.vocab, c.blank, durations_dev, c.n_durations,
+                                                 c.max_symbols, st_dev, U, raw, predict_token, words, embedding.p,
+                                                 state, h, L, qd, st),
                                  "tdt decide"))
             return rc;
         return predict(st);
     };
-    if (int rc = rows_kernel(tdt_start(U, c.blank, predict_token, s), "tdt start")) return rc;
+    if (int rc = rows_kernel(tdt_start(U, c.blank, h, embedding.p, predict_token, qd, s), "tdt start")) return rc;
     if (int rc = predict(s)) return rc;
     // Each pass advances every unfinished utterance by a frame or emits one of its at most
     // max_symbols tokens on a frame, so frames * (max_symbols + 1) passes bound the loop.
@@ -598,8 +590,8 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     for (int u = 0; u < U; ++u) max_frames = std::max<int64_t>(max_frames, frames[u]);
     const int64_t bound = max_frames * (c.max_symbols + 1) + 1;
     // The kPollSteps passes between two completion checks are recorded once as a CUDA graph on a
-    // private stream and replayed on the caller's stream (one launch instead of about 17 per
-    // pass); if recording fails the passes are launched one by one.
+    // private stream and replayed on the caller's stream (one launch instead of 8 per pass); if
+    // recording fails the passes are launched one by one.
     GraphExec graph;
     long graph_launches = 0;
     if (max_frames > 0) {

@@ -319,40 +319,120 @@ __global__ void __launch_bounds__(256) txl_attention_kernel(const float* __restr
 }
 
 // ---- greedy TDT steps (decode_inner, src/parakeet.rs:1412-1513) --------------------------------
+//
+// One decoding pass is four of these per-utterance kernels around four matrix products:
+// joint_prep (commit the last prediction, z = relu(enc_proj[t] + pred), quantize z) -> joint
+// product -> decide_prep (token and duration, the state step, the LSTM input [emb(token) | h0]
+// quantized) -> LSTM product -> cell_prep (cell update, the next layer's input or the top
+// hidden state quantized) -> ... -> pred_proj product. Every row is quantized by the rule of
+// quantize_x2 (quant.cu), so the products see the same operands as before the fusion.
 
-// z[u] = relu(enc_proj[frame row of u] + pred[u]) for every utterance still decoding.
-__global__ void tdt_joint_input_kernel(const float* __restrict__ enc_proj, const TdtState* __restrict__ st, int n_utt,
-                                       int h, const float* __restrict__ pred, float* __restrict__ z) {
+// Split-int8 quantization (the rule of quantize_x2) of a row of k values staged in shared memory,
+// by a CTA of 128 threads; the row's padding up to ld is zeroed.
+__device__ void quantize_row_cta(const float* row, int k, int64_t ld, int8_t* hi, int8_t* lo, float* scale,
+                                 float* red) {
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    float amax = 0.0f;
+    for (int i = tid; i < k; i += 128) amax = fmaxf(amax, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float id_lo = __fmul_rn(id, 254.0f);
+    for (int i = tid; i < k; i += 128) quant_split_one(row[i], d, id, id_lo, hi[i], lo[i]);
+    for (int i = k + tid; i < ld; i += 128) hi[i] = lo[i] = 0;
+    if (tid == 0) *scale = d;
+    __syncthreads();
+}
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+
+// The start of decoding (initial_decoder_state, src/parakeet.rs:1321-1336): every utterance
+// feeds the blank token to a zero LSTM state, so its layer-0 input is [emb(blank) | 0].
+__global__ void __launch_bounds__(128) tdt_start_kernel(int n_utt, int blank, int h, const float* __restrict__ embedding,
+                                                        int* __restrict__ predict_token, QuantAct q) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
     const int u = blockIdx.x;
     if (u >= n_utt) return;
+    if (threadIdx.x == 0) predict_token[u] = blank;
+    for (int j = threadIdx.x; j < h; j += 128) {
+        row[j] = embedding[static_cast<int64_t>(blank) * h + j];
+        row[h + j] = 0.0f;
+    }
+    __syncthreads();
+    quantize_row_cta(row, 2 * h, q.ld, q.hi + static_cast<int64_t>(u) * q.ld, q.lo + static_cast<int64_t>(u) * q.ld,
+                     q.scale + u, red);
+}
+
+// pred = fresh for the utterances that predicted last pass; then z = relu(enc_proj[t] + pred)
+// for the utterances still decoding (zeros for the others), quantized.
+__global__ void __launch_bounds__(128) tdt_joint_prep_kernel(const float* __restrict__ enc_proj,
+                                                             const TdtState* __restrict__ st, int n_utt, int h,
+                                                             const int* __restrict__ predict_token,
+                                                             const float* __restrict__ fresh, float* __restrict__ pred,
+                                                             QuantAct q, int* __restrict__ active) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
+    const int u = blockIdx.x;
+    if (u >= n_utt) return;
+    if (u == 0 && threadIdx.x == 0) *active = 0;
     const TdtState s = st[u];
-    if (s.t >= s.frames) return;  // finished: its row of z is not read
-    const int64_t row = static_cast<int64_t>(s.enc_first) + s.t;
-    for (int j = threadIdx.x; j < h; j += blockDim.x)
-        z[static_cast<int64_t>(u) * h + j] =
-            fmaxf(__fadd_rn(enc_proj[row * h + j], pred[static_cast<int64_t>(u) * h + j]), 0.0f);
+    const bool commit = predict_token[u] >= 0;
+    const bool live = s.t < s.frames;
+    float* pu = pred + static_cast<int64_t>(u) * h;
+    const float* fu = fresh + static_cast<int64_t>(u) * h;
+    if (live) {
+        const float* e = enc_proj + (static_cast<int64_t>(s.enc_first) + s.t) * h;
+        for (int j = threadIdx.x; j < h; j += 128) {
+            float p = pu[j];
+            if (commit) {
+                p = fu[j];
+                pu[j] = p;
+            }
+            row[j] = fmaxf(__fadd_rn(e[j], p), 0.0f);
+        }
+    } else {
+        for (int j = threadIdx.x; j < h; j += 128) {
+            if (commit) pu[j] = fu[j];
+            row[j] = 0.0f;
+        }
+    }
+    __syncthreads();
+    quantize_row_cta(row, h, q.ld, q.hi + static_cast<int64_t>(u) * q.ld, q.lo + static_cast<int64_t>(u) * q.ld,
+                     q.scale + u, red);
 }
 
 // The token and duration choices of one joint step and the state machine after them: blank ->
 // advance by max(duration, 1); a token -> emit it, predict next, advance by its duration or,
-// for duration 0, count symbols on this frame up to max_symbols. One warp per utterance.
-__global__ void tdt_decide_kernel(const float* __restrict__ logits, int64_t ld, int vocab, int blank,
-                                  const int* __restrict__ durations, int n_dur, int max_symbols,
-                                  TdtState* __restrict__ st, int n_utt, uint32_t* __restrict__ tokens,
-                                  int* __restrict__ predict_token, int* __restrict__ active) {
-    const int u = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
+// for duration 0, count symbols on this frame up to max_symbols. A predicting utterance's LSTM
+// layer-0 input [emb(token) | h0] is quantized for the next product.
+__global__ void __launch_bounds__(128) tdt_decide_prep_kernel(
+    const float* __restrict__ logits, int64_t ld, int vocab, int blank, const int* __restrict__ durations, int n_dur,
+    int max_symbols, TdtState* __restrict__ st, int n_utt, uint32_t* __restrict__ tokens,
+    int* __restrict__ predict_token, int* __restrict__ active, const float* __restrict__ embedding,
+    const float* __restrict__ state, int h, int layers, QuantAct q) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
+    __shared__ float bv[4];
+    __shared__ int bi_sh[4];
+    __shared__ int tok_sh;
+    const int u = blockIdx.x;
     if (u >= n_utt) return;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     TdtState s = st[u];
     if (s.t >= s.frames) {
-        if (lane == 0) predict_token[u] = -1;
+        if (tid == 0) predict_token[u] = -1;
         return;
     }
-    const float* row = logits + static_cast<int64_t>(u) * ld;
+    const float* r = logits + static_cast<int64_t>(u) * ld;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = lane; i < vocab; i += 32) {
-        const float v = row[i];
+    for (int i = tid; i < vocab; i += 128) {
+        const float v = r[i];
         if (v > best) { best = v; bi = i; }
     }
 #pragma unroll
@@ -361,86 +441,90 @@ __global__ void tdt_decide_kernel(const float* __restrict__ logits, int64_t ld, 
         const int oi = __shfl_xor_sync(kFull, bi, o);
         if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
     }
-    if (lane != 0) return;
-    int di = 0;
-    for (int i = 1; i < n_dur; ++i)
-        if (row[vocab + i] > row[vocab + di]) di = i;
-    const int duration = durations[di];
-    int tok = -1;
-    if (bi == blank) {
-        s.t += duration > 1 ? duration : 1;
-        s.on_frame = 0;
-    } else {
-        uint32_t* out = tokens + 3 * static_cast<int64_t>(s.tok_first + s.count);
-        out[0] = static_cast<uint32_t>(bi);
-        out[1] = static_cast<uint32_t>(s.t);
-        out[2] = static_cast<uint32_t>(duration);
-        s.count += 1;
-        tok = bi;
-        if (duration > 0) {
-            s.t += duration;
+    if (lane == 0) {
+        bv[warp] = best;
+        bi_sh[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // The first maximum over the four warps' winners: lowest index on ties.
+        float bb = bv[0];
+        int ii = bi_sh[0];
+        for (int w = 1; w < 4; ++w)
+            if (bv[w] > bb || (bv[w] == bb && bi_sh[w] < ii)) { bb = bv[w]; ii = bi_sh[w]; }
+        int di = 0;
+        for (int i = 1; i < n_dur; ++i)
+            if (r[vocab + i] > r[vocab + di]) di = i;
+        const int duration = durations[di];
+        int tok = -1;
+        if (ii == blank) {
+            s.t += duration > 1 ? duration : 1;
             s.on_frame = 0;
         } else {
-            s.on_frame += 1;
-            if (s.on_frame >= max_symbols) {
-                s.t += 1;
+            uint32_t* out = tokens + 3 * static_cast<int64_t>(s.tok_first + s.count);
+            out[0] = static_cast<uint32_t>(ii);
+            out[1] = static_cast<uint32_t>(s.t);
+            out[2] = static_cast<uint32_t>(duration);
+            s.count += 1;
+            tok = ii;
+            if (duration > 0) {
+                s.t += duration;
                 s.on_frame = 0;
+            } else {
+                s.on_frame += 1;
+                if (s.on_frame >= max_symbols) {
+                    s.t += 1;
+                    s.on_frame = 0;
+                }
             }
         }
+        st[u] = s;
+        predict_token[u] = tok;
+        tok_sh = tok;
+        if (s.t < s.frames) atomicAdd(active, 1);
     }
-    st[u] = s;
-    predict_token[u] = tok;
-    if (s.t < s.frames) atomicAdd(active, 1);
+    __syncthreads();
+    const int tok = tok_sh;
+    if (tok < 0) return;
+    const float* h0 = state + static_cast<int64_t>(u) * layers * 2 * h;
+    for (int j = tid; j < h; j += 128) {
+        row[j] = embedding[static_cast<int64_t>(tok) * h + j];
+        row[h + j] = h0[j];
+    }
+    __syncthreads();
+    quantize_row_cta(row, 2 * h, q.ld, q.hi + static_cast<int64_t>(u) * q.ld, q.lo + static_cast<int64_t>(u) * q.ld,
+                     q.scale + u, red);
 }
 
-// The LSTM layer's input [x | h_l] for every utterance that predicts: x is the token's
-// embedding for layer 0, else the previous layer's new hidden state.
-__global__ void lstm_input_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layer, int layers,
-                                  const float* __restrict__ embedding, const float* __restrict__ state,
-                                  float* __restrict__ input) {
-    const int u = blockIdx.x;
-    if (u >= n_utt || predict_token[u] < 0) return;
-    const float* st = state + static_cast<int64_t>(u) * layers * 2 * h;
-    float* in = input + static_cast<int64_t>(u) * 2 * h;
-    for (int j = threadIdx.x; j < h; j += blockDim.x) {
-        in[j] = layer == 0 ? embedding[static_cast<int64_t>(predict_token[u]) * h + j] : st[(layer - 1) * 2 * h + j];
-        in[h + j] = st[layer * 2 * h + j];
-    }
-}
-
-// c = f c + i g, h = o tanh(c) for the utterances that predict; other states stay.
-__global__ void lstm_cell_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layer, int layers,
-                                 const float* __restrict__ gates, float* __restrict__ state) {
+// c = f c + i g, h = o tanh(c) for layer `layer` of the predicting utterances; then the next
+// layer's input [h_layer | h_(layer+1)] or, after the top layer, h_top, quantized.
+__global__ void __launch_bounds__(128) lstm_cell_prep_kernel(const int* __restrict__ predict_token, int n_utt, int h,
+                                                             int layer, int layers, const float* __restrict__ gates,
+                                                             float* __restrict__ state, QuantAct q) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
     const int u = blockIdx.x;
     if (u >= n_utt || predict_token[u] < 0) return;
     const float* g = gates + static_cast<int64_t>(u) * 4 * h;
-    float* hs = state + static_cast<int64_t>(u) * layers * 2 * h + layer * 2 * h;
+    float* base = state + static_cast<int64_t>(u) * layers * 2 * h;
+    float* hs = base + layer * 2 * h;
     float* cs = hs + h;
-    for (int j = threadIdx.x; j < h; j += blockDim.x) {
-        const float i = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[j])));
-        const float f = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[h + j])));
+    const bool top = layer + 1 == layers;
+    for (int j = threadIdx.x; j < h; j += 128) {
+        const float i = sigmoid_ref(g[j]);
+        const float f = sigmoid_ref(g[h + j]);
         const float gg = tanhf(g[2 * h + j]);
-        const float o = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[3 * h + j])));
+        const float o = sigmoid_ref(g[3 * h + j]);
         const float c = __fadd_rn(__fmul_rn(f, cs[j]), __fmul_rn(i, gg));
+        const float hn = __fmul_rn(o, tanhf(c));
         cs[j] = c;
-        hs[j] = __fmul_rn(o, tanhf(c));
+        hs[j] = hn;
+        row[j] = hn;
+        if (!top) row[h + j] = base[(layer + 1) * 2 * h + j];
     }
-}
-
-// The last layer's hidden states of the predicting utterances, gathered for pred_proj.
-__global__ void lstm_last_kernel(const int* __restrict__ predict_token, int n_utt, int h, int layers,
-                                 const float* __restrict__ state, float* __restrict__ last) {
-    const int u = blockIdx.x;
-    if (u >= n_utt) return;
-    const float* hs = state + static_cast<int64_t>(u) * layers * 2 * h + (layers - 1) * 2 * h;
-    for (int j = threadIdx.x; j < h; j += blockDim.x) last[static_cast<int64_t>(u) * h + j] = hs[j];
-}
-
-// The start of decoding (initial_decoder_state, src/parakeet.rs:1321-1336): every utterance
-// feeds the blank token to a zero LSTM state.
-__global__ void tdt_start_kernel(int n_utt, int blank, int* __restrict__ predict_token) {
-    const int u = blockIdx.x * blockDim.x + threadIdx.x;
-    if (u < n_utt) predict_token[u] = blank;
+    __syncthreads();
+    quantize_row_cta(row, top ? h : 2 * h, q.ld, q.hi + static_cast<int64_t>(u) * q.ld,
+                     q.lo + static_cast<int64_t>(u) * q.ld, q.scale + u, red);
 }
 
 // Moves each utterance's tokens from its worst-case slot (3 * tok_first words in) to the prefix
@@ -467,15 +551,6 @@ __global__ void __launch_bounds__(1024) tdt_compact_kernel(const uint32_t* __res
         for (int i = lane; i < 3 * s.count; i += 32) dst[i] = src[i];
         if (lane == 0) counts[u] = s.count;
     }
-}
-
-// pred[u] = the new projection for utterances that predicted.
-__global__ void pred_commit_kernel(const int* __restrict__ predict_token, int n_utt, int h,
-                                   const float* __restrict__ fresh, float* __restrict__ pred) {
-    const int u = blockIdx.x;
-    if (u >= n_utt || predict_token[u] < 0) return;
-    for (int j = threadIdx.x; j < h; j += blockDim.x)
-        pred[static_cast<int64_t>(u) * h + j] = fresh[static_cast<int64_t>(u) * h + j];
 }
 
 // ---- launchers ---------------------------------------------------------------------------------
@@ -538,40 +613,37 @@ cudaError_t txl_attention(const float* qkv, const float* pp, const TxlTask* task
     }
 }
 
-cudaError_t tdt_joint_input(const float* enc_proj, const TdtState* st, int n_utt, int h, const float* pred, float* z,
-                            cudaStream_t s) {
-    tdt_joint_input_kernel<<<n_utt, 128, 0, s>>>(enc_proj, st, n_utt, h, pred, z);
-    return cudaGetLastError();
-}
-
-cudaError_t tdt_decide(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
-                       int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
-                       cudaStream_t s) {
-    tdt_decide_kernel<<<(n_utt + 3) / 4, 128, 0, s>>>(logits, ld, vocab, blank, durations, n_dur, max_symbols, st, n_utt,
-                                                       tokens, predict_token, active);
-    return cudaGetLastError();
-}
-
-cudaError_t lstm_input(const int* predict_token, int n_utt, int h, int layer, int layers, const float* embedding,
-                       const float* state, float* input, cudaStream_t s) {
-    lstm_input_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layer, layers, embedding, state, input);
-    return cudaGetLastError();
-}
-
-cudaError_t lstm_cell(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
-                      float* state, cudaStream_t s) {
-    lstm_cell_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layer, layers, gates, state);
-    return cudaGetLastError();
-}
-
-cudaError_t lstm_last(const int* predict_token, int n_utt, int h, int layers, const float* state, float* last,
+cudaError_t tdt_start(int n_utt, int blank, int h, const float* embedding, int* predict_token, const QuantAct& q,
                       cudaStream_t s) {
-    lstm_last_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, layers, state, last);
+    if (n_utt <= 0) return cudaSuccess;
+    tdt_start_kernel<<<n_utt, 128, sizeof(float) * 2 * h, s>>>(n_utt, blank, h, embedding, predict_token, q);
     return cudaGetLastError();
 }
 
-cudaError_t tdt_start(int n_utt, int blank, int* predict_token, cudaStream_t s) {
-    tdt_start_kernel<<<(n_utt + 255) / 256, 256, 0, s>>>(n_utt, blank, predict_token);
+cudaError_t tdt_joint_prep(const float* enc_proj, const TdtState* st, int n_utt, int h, const int* predict_token,
+                           const float* fresh, float* pred, const QuantAct& q, int* active, cudaStream_t s) {
+    if (n_utt <= 0) return cudaSuccess;
+    tdt_joint_prep_kernel<<<n_utt, 128, sizeof(float) * h, s>>>(enc_proj, st, n_utt, h, predict_token, fresh, pred, q,
+                                                                 active);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_decide_prep(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
+                            int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
+                            const float* embedding, const float* state, int h, int layers, const QuantAct& q,
+                            cudaStream_t s) {
+    if (n_utt <= 0) return cudaSuccess;
+    tdt_decide_prep_kernel<<<n_utt, 128, sizeof(float) * 2 * h, s>>>(logits, ld, vocab, blank, durations, n_dur,
+                                                                      max_symbols, st, n_utt, tokens, predict_token,
+                                                                      active, embedding, state, h, layers, q);
+    return cudaGetLastError();
+}
+
+cudaError_t lstm_cell_prep(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
+                           float* state, const QuantAct& q, cudaStream_t s) {
+    if (n_utt <= 0) return cudaSuccess;
+    lstm_cell_prep_kernel<<<n_utt, 128, sizeof(float) * 2 * h, s>>>(predict_token, n_utt, h, layer, layers, gates,
+                                                                     state, q);
     return cudaGetLastError();
 }
 
@@ -581,9 +653,5 @@ cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int*
     return cudaGetLastError();
 }
 
-cudaError_t pred_commit(const int* predict_token, int n_utt, int h, const float* fresh, float* pred, cudaStream_t s) {
-    pred_commit_kernel<<<n_utt, 128, 0, s>>>(predict_token, n_utt, h, fresh, pred);
-    return cudaGetLastError();
-}
 
 }  // namespace telmo

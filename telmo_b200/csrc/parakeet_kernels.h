@@ -6,6 +6,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "kernels.h"
+
 namespace telmo {
 
 // One span of a stride-2 3x3 convolution over one utterance: output rows (time steps)
@@ -66,34 +68,33 @@ cudaError_t txl_attention_mma(const __half* qkv, int64_t plane, const __half* po
 cudaError_t txl_pos_bias(const __half* pos, int64_t pplane, int npos, int heads, int hd, const float* bias_u,
                          const float* bias_v, float* cpos, cudaStream_t s);
 
-// z[u] = relu(enc_proj[u's current frame] + pred[u]), z [n_utt, h].
-cudaError_t tdt_joint_input(const float* enc_proj, const TdtState* st, int n_utt, int h, const float* pred, float* z,
-                            cudaStream_t s);
+// One greedy TDT pass is joint_prep -> joint product -> decide_prep -> LSTM product ->
+// cell_prep per layer (the last followed by the pred_proj product). Each prep kernel runs one
+// CTA per utterance and leaves the next product's split-int8 operand rows in q; state is
+// [n_utt, layers, 2, h] (hidden, cell); predict_token[u] is the token that utterance feeds the
+// prediction network this pass, or -1.
 
-// Token and duration choice from logits [n_utt, ld] and the state step after it; tokens are
-// (id, frame, duration) triples; predict_token[u] is the token to feed the prediction network
-// or -1; *active counts the utterances with frames left afterwards.
-cudaError_t tdt_decide(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
-                       int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
-                       cudaStream_t s);
-
-// LSTM layer input [x | h_layer] (x the token's embedding, or the layer below's new hidden state)
-// for the utterances with predict_token >= 0; state [n_utt, layers, 2, h] (hidden, cell).
-cudaError_t lstm_input(const int* predict_token, int n_utt, int h, int layer, int layers, const float* embedding,
-                       const float* state, float* input, cudaStream_t s);
-// The LSTM cell update from gates [n_utt, 4h] (i, f, g, o) for predicting utterances.
-cudaError_t lstm_cell(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
-                      float* state, cudaStream_t s);
-// last[u] = the top layer's hidden state.
-cudaError_t lstm_last(const int* predict_token, int n_utt, int h, int layers, const float* state, float* last,
+// Start of decoding: predict_token[u] = blank and q row u = [emb(blank) | 0] for every utterance.
+cudaError_t tdt_start(int n_utt, int blank, int h, const float* embedding, int* predict_token, const QuantAct& q,
                       cudaStream_t s);
-// predict_token[u] = blank for every utterance (the start of decoding).
-cudaError_t tdt_start(int n_utt, int blank, int* predict_token, cudaStream_t s);
+// pred[u] = fresh[u] where predict_token[u] >= 0; then q row u = relu(enc_proj[u's current frame]
+// + pred[u]) (zeros for finished utterances); *active = 0.
+cudaError_t tdt_joint_prep(const float* enc_proj, const TdtState* st, int n_utt, int h, const int* predict_token,
+                           const float* fresh, float* pred, const QuantAct& q, int* active, cudaStream_t s);
+// Token and duration choice from logits [n_utt, ld] and the state step after it; tokens are
+// (id, frame, duration) triples; *active counts the utterances with frames left afterwards.
+// For an utterance that emitted a token, q row u = [emb(token) | h_0].
+cudaError_t tdt_decide_prep(const float* logits, int64_t ld, int vocab, int blank, const int* durations, int n_dur,
+                            int max_symbols, TdtState* st, int n_utt, uint32_t* tokens, int* predict_token, int* active,
+                            const float* embedding, const float* state, int h, int layers, const QuantAct& q,
+                            cudaStream_t s);
+// The cell update of `layer` from gates [n_utt, 4h] (i, f, g, o) for the predicting utterances,
+// then q row u = [h_layer | h_(layer+1)], or h_top after the top layer.
+cudaError_t lstm_cell_prep(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
+                           float* state, const QuantAct& q, cudaStream_t s);
 // Tokens from each utterance's worst-case slot (3 * tok_first words into raw) to consecutive
 // places in out (prefix sums of the counts, kept in offsets [n_utt]); counts[u] and *total.
 cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int* offsets, uint32_t* out, int* counts,
                         int* total, cudaStream_t s);
-// pred[u] = fresh[u] for predicting utterances.
-cudaError_t pred_commit(const int* predict_token, int n_utt, int h, const float* fresh, float* pred, cudaStream_t s);
 
 }  // namespace telmo

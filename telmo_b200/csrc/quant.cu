@@ -16,17 +16,6 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-__device__ __forceinline__ void quant_one(float x, float d, float id, float id_lo, int8_t& h8,
-                                          int8_t& l8) {
-    float h = roundf(__fmul_rn(x, id));
-    h = fminf(fmaxf(h, -127.0f), 127.0f);
-    const float e = __fmaf_rn(-h, d, x);
-    float l = roundf(__fmul_rn(e, id_lo));
-    l = fminf(fmaxf(l, -127.0f), 127.0f);
-    h8 = static_cast<int8_t>(h);
-    l8 = static_cast<int8_t>(l);
-}
-
 __global__ void quantize_x2_kernel(const float* __restrict__ x, int64_t ldx, int m, int k,
                                    int8_t* __restrict__ hi, int8_t* __restrict__ lo, int64_t ldq,
                                    float* __restrict__ scale) {
@@ -55,15 +44,15 @@ __global__ void quantize_x2_kernel(const float* __restrict__ x, int64_t ldx, int
         for (int i = lane * 4; i < k; i += 128) {
             const float4 v = *reinterpret_cast<const float4*>(xr + i);
             char4 h, l;
-            quant_one(v.x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
-            quant_one(v.y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
-            quant_one(v.z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
-            quant_one(v.w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
+            quant_split_one(v.x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
+            quant_split_one(v.y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
+            quant_split_one(v.z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
+            quant_split_one(v.w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
             *reinterpret_cast<char4*>(hr + i) = h;
             *reinterpret_cast<char4*>(lr + i) = l;
         }
     } else {
-        for (int i = lane; i < k; i += 32) quant_one(xr[i], d, id, id_lo, hr[i], lr[i]);
+        for (int i = lane; i < k; i += 32) quant_split_one(xr[i], d, id, id_lo, hr[i], lr[i]);
     }
     for (int i = k + lane; i < ldq; i += 32) hr[i] = lr[i] = 0;
     if (lane == 0) scale[row] = d;
@@ -108,10 +97,10 @@ __global__ void __launch_bounds__(256) quantize_x2_regs_kernel(const float* __re
 #pragma unroll
     for (int c = 0; c < CW; ++c) {
         char4 h, l;
-        quant_one(v[c].x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
-        quant_one(v[c].y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
-        quant_one(v[c].z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
-        quant_one(v[c].w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
+        quant_split_one(v[c].x, d, id, id_lo, reinterpret_cast<int8_t&>(h.x), reinterpret_cast<int8_t&>(l.x));
+        quant_split_one(v[c].y, d, id, id_lo, reinterpret_cast<int8_t&>(h.y), reinterpret_cast<int8_t&>(l.y));
+        quant_split_one(v[c].z, d, id, id_lo, reinterpret_cast<int8_t&>(h.z), reinterpret_cast<int8_t&>(l.z));
+        quant_split_one(v[c].w, d, id, id_lo, reinterpret_cast<int8_t&>(h.w), reinterpret_cast<int8_t&>(l.w));
         *reinterpret_cast<char4*>(hr + (c * 32 + lane) * 4) = h;
         *reinterpret_cast<char4*>(lr + (c * 32 + lane) * 4) = l;
     }
