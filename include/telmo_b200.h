@@ -288,6 +288,19 @@ int telmo_parakeet_transcribe(telmo_parakeet *p, const float *samples, const int
 int telmo_parakeet_transcribe_device(telmo_parakeet *p, const float *samples,
                                      const int64_t *lengths, int n_utt, uint32_t *tokens,
                                      int *counts, int *frames, void *stream);
+/* Selects the greedy TDT decoder: 1 (the default) runs the whole loop as one persistent
+ * cooperative kernel with the prediction and joint weights held in shared memory, where the
+ * model fits (pred_hidden a multiple of 64, the weights within the SMs' shared memory); 0 runs
+ * it as a replayed CUDA graph of per-phase launches. Both give the same tokens bit for bit.
+ * Replaces the decoder choice the reference makes implicitly (it has one CPU decoder). */
+int telmo_parakeet_set_decoder(telmo_parakeet *p, int persistent);
+/* Which decoder the last decode ran: 1 persistent, 0 per-phase launches, -1 none yet. */
+int telmo_parakeet_last_decoder(const telmo_parakeet *p);
+/* The persistent decoder's own clock for the last decode run with profiling on: ms[10], per
+ * phase kind (start, joint, decide, LSTM products, cells, pred_proj product, prepare; each from
+ * one grid barrier to the next), then CTA 0's time inside the products and, of that, waiting
+ * for staged activation rows and in epilogues; and the passes it ran. */
+int telmo_parakeet_decoder_profile(const telmo_parakeet *p, double *ms, long *passes);
 /* CUDA kernels this model has launched so far (front end included). */
 long telmo_parakeet_launches(const telmo_parakeet *p);
 /* Per-class timing as telmo_granite_profile / telmo_granite_profile_read give it. */

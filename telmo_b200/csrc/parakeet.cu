@@ -129,8 +129,12 @@ struct Parakeet {
     DevVec embedding, pred_proj_b, enc_proj_b, joint_b;
     DevWeights pred_proj, enc_proj, joint;
     int* durations_dev = nullptr;
-    int* host_words = nullptr;  // pinned: [0] active utterances, [1] total tokens
+    int* host_words = nullptr;  // pinned: [0] active utterances, [1] total tokens, [2..3] decoder words
     bool finalized = false;
+    int decoder = 1;       // 1: the persistent kernel where the model and device allow it; 0: phases
+    int last_decoder = -1;  // which one the last decode ran
+    double phase_ms[kTdtClocks] = {};  // the persistent decoder's clock, last profiled decode
+    long phase_passes = 0;
     long launches = 0;
 
     Arena enc_arena, dec_arena, e2e_arena;
@@ -531,7 +535,8 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
                          piece<float>(static_cast<size_t>(U) * ld_logits) + piece<float>(static_cast<size_t>(U) * L * 2 * h) +
                          2 * piece<float>(static_cast<size_t>(U) * h) + piece<float>(static_cast<size_t>(U) * 4 * h) +
                          piece<TdtState>(U) + 2 * piece<int>(U) + piece<int>(4) +
-                         piece<uint32_t>(3 * static_cast<size_t>(slots) + 3);
+                         piece<uint32_t>(3 * static_cast<size_t>(slots) + 3) + piece<int>(4 * static_cast<size_t>(U)) +
+                         piece<unsigned long long>(2 * static_cast<size_t>(U) + kTdtClocks) + piece<unsigned>(8);
     if (int rc = dec_arena.reserve(ctx, bytes)) return rc;
     Arena& A = dec_arena;
     const QuantAct q_enc = quant_piece(A, M, ld_d);
@@ -547,6 +552,9 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     int* offsets = A.take<int>(U);
     int* words = A.take<int>(4);
     uint32_t* raw = A.take<uint32_t>(3 * static_cast<size_t>(slots) + 3);
+    int* lists = A.take<int>(4 * static_cast<size_t>(U));
+    unsigned long long* keys = A.take<unsigned long long>(2 * static_cast<size_t>(U) + kTdtClocks);
+    unsigned* pwords = A.take<unsigned>(8);
 
     if (int rc = ctx->cuda(cudaMemcpyAsync(st_dev, st.data(), sizeof(TdtState) * U, cudaMemcpyHostToDevice, s), "tdt"))
         return rc;
@@ -559,6 +567,91 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
         ++launches;
         return ctx->cuda(e, what);
     };
+    int64_t max_frames = 0;
+    for (int u = 0; u < U; ++u) max_frames = std::max<int64_t>(max_frames, frames[u]);
+    // Each pass advances every unfinished utterance by a frame or emits one of its at most
+    // max_symbols tokens on a frame, so frames * (max_symbols + 1) passes bound the loop.
+    const int64_t bound = max_frames * (c.max_symbols + 1) + 1;
+
+    // The persistent decoder: the whole loop in one cooperative launch (tdt_persistent.cu).
+    if (decoder == 1 && max_frames > 0) {
+        TdtPersistentArgs pa;
+        auto mat = [](const DevWeights& w, const float* bias) {
+            TdtMatrix m;
+            m.w = w.values;
+            m.ld = w.ld;
+            m.ws = w.scales;
+            m.bias = bias;
+            m.n = w.n;
+            m.k = w.k;
+            return m;
+        };
+        pa.mats[0] = mat(joint, joint_b.p);
+        for (int l = 0; l < L; ++l) pa.mats[1 + l] = mat(lstm[l], lstm_b[l].p);
+        pa.mats[L + 1] = mat(pred_proj, pred_proj_b.p);
+        pa.n_mats = L + 2;
+        pa.layers = L;
+        pa.h = h;
+        pa.n_utt = U;
+        pa.vocab = c.vocab;
+        pa.blank = c.blank;
+        pa.n_dur = c.n_durations;
+        pa.max_symbols = c.max_symbols;
+        for (int i = 0; i < c.n_durations; ++i) pa.durations[i] = c.durations[i];
+        pa.enc_proj = enc_proj_out;
+        pa.embedding = embedding.p;
+        pa.state = state;
+        pa.pred = pred;
+        pa.fresh = fresh;
+        pa.gates = gates;
+        pa.q_hi = qd.hi;
+        pa.q_lo = qd.lo;
+        pa.q_scale = qd.scale;
+        pa.q_ld = qd.ld;
+        pa.st = st_dev;
+        pa.tokens = raw;
+        pa.lists = lists;
+        pa.plist = lists + 2 * U;
+        pa.ps_of = lists + 3 * U;
+        pa.tok_key = keys;
+        pa.dur_key = keys + U;
+        pa.words = pwords;
+        pa.max_passes = bound;
+        pa.phase_ns = prof.on ? keys + 2 * U : nullptr;
+        size_t smem = 0;
+        if (L + 2 <= kTdtMaxMats && tdt_persistent_plan(pa, ctx->sms, &smem)) {
+            if (int rc = ctx->cuda(cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * (2 * U + kTdtClocks), s), "tdt"))
+                return rc;
+            if (int rc = ctx->cuda(cudaMemsetAsync(pwords, 0, sizeof(unsigned) * 8, s), "tdt")) return rc;
+            if (prof.on) prof.begin(kProfRows, s);
+            if (int rc = rows_kernel(tdt_persistent(pa, ctx->sms, smem, s), "tdt persistent")) return rc;
+            if (prof.on) prof.end(kProfRows, s);
+            if (int rc = rows_kernel(tdt_compact(raw, st_dev, U, offsets, tokens, counts, words + 1, s), "tdt compact"))
+                return rc;
+            if (int rc = ctx->cuda(cudaMemcpyAsync(host_words + 1, words + 1, sizeof(int), cudaMemcpyDeviceToHost, s),
+                                   "tdt"))
+                return rc;
+            if (int rc = ctx->cuda(cudaMemcpyAsync(host_words + 2, pwords, 2 * sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                                   s),
+                                   "tdt"))
+                return rc;
+            if (int rc = ctx->cuda(cudaStreamSynchronize(s), "tdt")) return rc;
+            if (host_words[2] == kTdtErrBarrier)
+                return ctx->fail(TELMO_ERR_CUDA, "parakeet_decode: a grid barrier of the decoder timed out");
+            if (host_words[2] != 0) return ctx->fail(TELMO_ERR_CUDA, "parakeet_decode: decoding did not finish");
+            last_decoder = 1;
+            if (total) *total = host_words[1];
+            if (pa.phase_ns) {
+                unsigned long long ns[kTdtClocks];
+                if (int rc = ctx->cuda(cudaMemcpy(ns, pa.phase_ns, sizeof ns, cudaMemcpyDeviceToHost), "tdt")) return rc;
+                for (int i = 0; i < kTdtClocks; ++i) phase_ms[i] = ns[i] * 1e-6;
+                phase_passes = host_words[3];
+            }
+            return TELMO_OK;
+        }
+    }
+    last_decoder = 0;
+
     // Parakeet::predict_rows (src/parakeet.rs:1523-1577) for the utterances with a token, from
     // the layer-0 input rows already quantized in qd; the new projections land in `fresh`.
     auto predict = [&](cudaStream_t st) -> int {
@@ -584,11 +677,6 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     };
     if (int rc = rows_kernel(tdt_start(U, c.blank, h, embedding.p, predict_token, qd, s), "tdt start")) return rc;
     if (int rc = predict(s)) return rc;
-    // Each pass advances every unfinished utterance by a frame or emits one of its at most
-    // max_symbols tokens on a frame, so frames * (max_symbols + 1) passes bound the loop.
-    int64_t max_frames = 0;
-    for (int u = 0; u < U; ++u) max_frames = std::max<int64_t>(max_frames, frames[u]);
-    const int64_t bound = max_frames * (c.max_symbols + 1) + 1;
     // The kPollSteps passes between two completion checks are recorded once as a CUDA graph on a
     // private stream and replayed on the caller's stream (one launch instead of 8 per pass); if
     // recording fails the passes are launched one by one.
@@ -838,6 +926,27 @@ extern "C" int telmo_parakeet_transcribe(telmo_parakeet* pp, const float* sample
     if (int rc = ctx->cuda(cudaMemcpyAsync(counts, cnt_dev, sizeof(int) * n_utt, cudaMemcpyDeviceToHost, s), "transcribe"))
         return rc;
     return ctx->cuda(cudaStreamSynchronize(s), "transcribe");
+}
+
+extern "C" int telmo_parakeet_set_decoder(telmo_parakeet* pp, int persistent) {
+    auto* p = reinterpret_cast<Parakeet*>(pp);
+    if (!p) return TELMO_ERR_ARGUMENT;
+    if (persistent != 0 && persistent != 1) return p->ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_set_decoder: 0 or 1");
+    p->decoder = persistent;
+    return TELMO_OK;
+}
+
+extern "C" int telmo_parakeet_last_decoder(const telmo_parakeet* pp) {
+    const auto* p = reinterpret_cast<const Parakeet*>(pp);
+    return p ? p->last_decoder : -1;
+}
+
+extern "C" int telmo_parakeet_decoder_profile(const telmo_parakeet* pp, double* ms, long* passes) {
+    const auto* p = reinterpret_cast<const Parakeet*>(pp);
+    if (!p || !ms) return TELMO_ERR_ARGUMENT;
+    for (int i = 0; i < kTdtClocks; ++i) ms[i] = p->phase_ms[i];
+    if (passes) *passes = p->phase_passes;
+    return TELMO_OK;
 }
 
 extern "C" long telmo_parakeet_launches(const telmo_parakeet* pp) {

@@ -92,6 +92,67 @@ cudaError_t tdt_decide_prep(const float* logits, int64_t ld, int vocab, int blan
 // then q row u = [h_layer | h_(layer+1)], or h_top after the top layer.
 cudaError_t lstm_cell_prep(const int* predict_token, int n_utt, int h, int layer, int layers, const float* gates,
                            float* state, const QuantAct& q, cudaStream_t s);
+// ---- the persistent decoder (tdt_persistent.cu) ----
+
+constexpr int kTdtMaxMats = 10;  // joint, up to 8 LSTM layers, pred_proj
+// Phase kinds of the persistent decoder's clock: start, joint, decide, LSTM products, cells,
+// pred_proj product, prepare; then CTA 0's own time in the products and, of that, the time its
+// thread 0 waited for staged activation rows and spent in epilogues.
+constexpr int kTdtPhases = 7;
+constexpr int kTdtClocks = kTdtPhases + 3;
+enum TdtError : unsigned { kTdtErrBarrier = 1, kTdtErrPasses = 2 };
+
+// One matrix of the prediction or joint network: int8 [n, ld] weights, per-row scales, bias
+// (or null), k inputs. units .. smem_stride are filled in by tdt_persistent_plan.
+struct TdtMatrix {
+    const int8_t* w = nullptr;
+    int64_t ld = 0;
+    const float* ws = nullptr;
+    const float* bias = nullptr;
+    int n = 0, k = 0;
+    int units = 0, max_units = 0, offset = 0, smem_stride = 0;
+};
+
+// Everything the persistent decoder reads and writes. Rows of q, gates and fresh are compacted
+// slots; state is [n_utt, layers, 2, h]; lists holds the two live lists [2][n_utt], plist
+// [n_utt] the predicting utterances by slot, ps_of [n_utt] each utterance's predicting slot or
+// -1. tok_key, dur_key [n_utt] and words [8] start zeroed.
+struct TdtPersistentArgs {
+    TdtMatrix mats[kTdtMaxMats];  // 0 joint, 1 .. layers LSTM, layers + 1 pred_proj
+    int n_mats = 0, layers = 0, h = 0, n_utt = 0;
+    int vocab = 0, blank = 0, n_dur = 0, max_symbols = 0;
+    int durations[8] = {};
+    const float* enc_proj = nullptr;   // [frames, h]
+    const float* embedding = nullptr;  // [vocab, h]
+    float* state = nullptr;
+    float* pred = nullptr;   // [n_utt, h]
+    float* fresh = nullptr;  // [n_utt, h] by slot
+    float* gates = nullptr;  // [n_utt, 4h] by slot
+    int8_t* q_hi = nullptr;
+    int8_t* q_lo = nullptr;
+    float* q_scale = nullptr;
+    int64_t q_ld = 0;
+    TdtState* st = nullptr;
+    uint32_t* tokens = nullptr;
+    int* lists = nullptr;
+    int* plist = nullptr;
+    int* ps_of = nullptr;
+    unsigned long long* tok_key = nullptr;
+    unsigned long long* dur_key = nullptr;
+    unsigned* words = nullptr;  // error code, passes, barrier state, counters
+    unsigned long long* phase_ns = nullptr;  // [kTdtClocks] or null: time per phase kind
+    long long max_passes = 0;
+    int ring_offset = 0;  // shared memory: the weight units, then the warps' rings
+    int chunk = 0;        // k bytes per ring stage: 128 where every k allows, else 64
+};
+
+// Assigns every matrix's 16-row units to `sms` CTAs and sizes the shared memory; false if the
+// model does not fit (h not a multiple of 64, more than 4 units of a matrix per CTA, or more
+// than 227 KB), in which case the launch-per-phase decoder is used.
+bool tdt_persistent_plan(TdtPersistentArgs& a, int sms, size_t* smem_bytes);
+// Runs the whole greedy decode; the error code lands in words[0], the passes in words[1].
+cudaError_t tdt_persistent(const TdtPersistentArgs& a, int grid, size_t smem_bytes, cudaStream_t s);
+
 // Tokens from each utterance's worst-case slot (3 * tok_first words into raw) to consecutive
 // places in out (prefix sums of the counts, kept in offsets [n_utt]); counts[u] and *total.
 cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int* offsets, uint32_t* out, int* counts,

@@ -166,6 +166,24 @@ class Parakeet:
             counts.data_ptr(), frames.ctypes.data, _stream(stream)), self.ctx.handle)
         return frames
 
+    def set_decoder(self, persistent: bool):
+        """1/True: the persistent decoder kernel (the default); 0/False: per-phase launches."""
+        check(_lib.load().telmo_parakeet_set_decoder(self._h, int(persistent)), self.ctx.handle)
+
+    def last_decoder(self) -> int:
+        """1 if the last decode ran the persistent kernel, 0 per-phase launches, -1 none yet."""
+        return _lib.load().telmo_parakeet_last_decoder(self._h)
+
+    def decoder_profile(self):
+        """The persistent decoder's clock for the last profiled decode: ({phase: ms}, passes)."""
+        ms = (ctypes.c_double * 10)()
+        passes = ctypes.c_long(0)
+        check(_lib.load().telmo_parakeet_decoder_profile(self._h, ms, ctypes.byref(passes)),
+              self.ctx.handle)
+        names = ("start", "joint", "decide", "lstm", "cell", "pred", "prepare", "cta0_products",
+                 "cta0_waiting", "cta0_epilogue")
+        return dict(zip(names, list(ms))), passes.value
+
     def launches(self) -> int:
         return _lib.load().telmo_parakeet_launches(self._h)
 

@@ -211,3 +211,53 @@ def test_benchmark_model_matches_the_oracle_before_it_diverges(full_spec, oracle
             want = ref.encode(f, tap_layer=tap, threads=8)
             assert rel_l2(got[at:at + fr], want) <= 2e-2, tap
             at += fr
+
+
+# ---- the two decoders -------------------------------------------------------------------------
+
+def _decode_both(gpu, enc, frames):
+    gpu.set_decoder(True)
+    tok_p, cnt_p, total_p = gpu.decode_packed(enc, frames)
+    assert gpu.last_decoder() == 1
+    gpu.set_decoder(False)
+    try:
+        tok_g, cnt_g, total_g = gpu.decode_packed(enc, frames)
+        assert gpu.last_decoder() == 0
+    finally:
+        gpu.set_decoder(True)
+    gpu.ctx.check()
+    return (tok_p.cpu().numpy(), cnt_p.cpu().numpy(), total_p), (tok_g.cpu().numpy(), cnt_g.cpu().numpy(), total_g)
+
+
+def test_persistent_decoder_equals_the_per_phase_decoder(tiny):
+    # Same products, same epilogue, same quantization: the same tokens bit for bit, including
+    # for an utterance with no frames and one that finishes on the first pass.
+    import torch
+    gpu, ref = tiny
+    rows = [203, 57, 450, 9, 320, 1]
+    encs = [ref.encode(_features(r, 90 + i)) for i, r in enumerate(rows)]
+    frames = [e.shape[0] for e in encs[:-1]] + [0]
+    enc = torch.from_numpy(np.concatenate(encs[:-1])).cuda()
+    (tp, cp, np_), (tg, cg, ng) = _decode_both(gpu, enc, frames)
+    assert np_ == ng > 0 and np.array_equal(cp, cg) and cp[-1] == 0
+    assert np.array_equal(tp, tg)
+
+
+def test_persistent_decoder_on_the_benchmark_model(full_spec):
+    # The config-4 decoder at its full size on 48 utterances of 1..374 frames: many passes, the
+    # live and predicting rows shrinking as utterances finish, both row halves of the stage ring.
+    import torch
+    gpu, _ = full_spec
+    rng = synthetic.rng(5)
+    frames = [int(x) for x in rng.integers(1, 375, 48)] + [374]
+    enc = torch.from_numpy(rng.standard_normal((sum(frames), 1024)).astype(np.float32)).cuda()
+    (tp, cp, np_), (tg, cg, ng) = _decode_both(gpu, enc, frames)
+    assert np_ == ng > 0 and np.array_equal(cp, cg)
+    assert np.array_equal(tp, tg)
+
+
+def test_decoder_choice_is_checked(tiny):
+    from telmo_b200 import TelmoError
+    gpu, _ = tiny
+    with pytest.raises(TelmoError):
+        gpu.set_decoder(2)
