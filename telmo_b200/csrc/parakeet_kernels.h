@@ -103,7 +103,7 @@ constexpr int kTdtClocks = kTdtPhases + 3;
 enum TdtError : unsigned { kTdtErrBarrier = 1, kTdtErrPasses = 2 };
 
 // One matrix of the prediction or joint network: int8 [n, ld] weights, per-row scales, bias
-// (or null), k inputs. units .. smem_stride are filled in by tdt_persistent_plan.
+// (or null), k inputs. units (of 8 rows) .. smem_stride are filled in by tdt_persistent_plan.
 struct TdtMatrix {
     const int8_t* w = nullptr;
     int64_t ld = 0;
@@ -146,8 +146,8 @@ struct TdtPersistentArgs {
     int chunk = 0;        // k bytes per ring stage: 128 where every k allows, else 64
 };
 
-// Assigns every matrix's 16-row units to `sms` CTAs and sizes the shared memory; false if the
-// model does not fit (h not a multiple of 64, more than 4 units of a matrix per CTA, or more
+// Assigns every matrix's 8-row units to `sms` CTAs and sizes the shared memory; false if the
+// model does not fit (h not a multiple of 64, more than 8 units of a matrix per CTA, or more
 // than 227 KB), in which case the launch-per-phase decoder is used.
 bool tdt_persistent_plan(TdtPersistentArgs& a, int sms, size_t* smem_bytes);
 // Runs the whole greedy decode; the error code lands in words[0], the passes in words[1].

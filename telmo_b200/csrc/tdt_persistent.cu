@@ -3,7 +3,7 @@
 // The whole of decode_inner (src/parakeet.rs:1412-1513) with predict_rows (:1523-1577) for every
 // utterance of the batch runs inside one cooperative launch of one CTA per SM. The prediction
 // and joint networks' int8 weights (joint, every LSTM layer, pred_proj: about 12 MB at the
-// benchmark's shape) are spread over the CTAs in units of 16 output rows and stay in shared
+// benchmark's shape) are spread over the CTAs in units of 8 output rows and stay in shared
 // memory for the whole decode, so a pass streams only the activations. Each pass is
 //
 //   joint    logits of every live utterance; the token and duration argmax folded into the
@@ -237,11 +237,11 @@ __device__ void product(const TdtPersistentArgs& a, const Smem& sm, int m, int r
         cp_commit();
     };
 
-    // This thread's output columns (two per 8-column subtile) with their scales and biases.
-    float wsv[2 * NU][2], bsv[2 * NU][2];
+    // This thread's output columns (two per 8-row unit) with their scales and biases.
+    float wsv[NU][2], bsv[NU][2];
 #pragma unroll
-    for (int j = 0; j < 2 * NU; ++j) {
-        const int col0 = (sm.first[m] + (j / 2) * static_cast<int>(gridDim.x)) * 16 + (j % 2) * 8 + 2 * q;
+    for (int j = 0; j < NU; ++j) {
+        const int col0 = (sm.first[m] + j * static_cast<int>(gridDim.x)) * 8 + 2 * q;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const bool ok = col0 + e < M.n;
@@ -250,15 +250,18 @@ __device__ void product(const TdtPersistentArgs& a, const Smem& sm, int m, int r
         }
     }
 
-    int acc_h[2 * NU][4], acc_l[2 * NU][4];
+    int acc_h[NU][4], acc_l[NU][4];
 #pragma unroll
-    for (int j = 0; j < 2 * NU; ++j)
+    for (int j = 0; j < NU; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc_h[j][e] = acc_l[j][e] = 0;
 
     for (int c = 0; c < STAGES - 1; ++c) issue();
     int tile = warp, kk = 0, kc = rot;  // the chunk to multiply: tile, position in its walk, k chunk
-    const int8_t* wrow = sm.w[m] + g * stride + 16 * q;
+    // Weight rows hold their 16-byte segments XOR-swizzled (seg ^ xr): rows g and g + 1 of a
+    // fragment read land in different halves of a 128-byte line.
+    const int xr = stride % 128 == 0 ? (g & 1) << 2 : 0;
+    const int8_t* wrow = sm.w[m] + g * stride;
     for (int c = 0; c < total; ++c) {
         const long long tw = clock ? clock64() : 0;
         cp_wait<STAGES - 2>();
@@ -266,24 +269,24 @@ __device__ void product(const TdtPersistentArgs& a, const Smem& sm, int m, int r
         if (clock) waited += clock64() - tw;
         issue();
         const int8_t* st = ring + (c % STAGES) * kStage + 16 * q;
-        const int8_t* wk = wrow + kc * CH;
 #pragma unroll
         for (int p = 0; p < STEPS / 2; ++p) {  // 64 k bytes: two k32 products per plane
-            uint4 b[2 * NU];
+            const int8_t* wk = wrow + ((((kc * CH + 64 * p) >> 4) + q) ^ xr) * 16;
+            uint4 b[NU];
 #pragma unroll
-            for (int j = 0; j < 2 * NU; ++j) b[j] = lds128(wk + j * 8 * stride + 64 * p);
+            for (int j = 0; j < NU; ++j) b[j] = lds128(wk + j * 8 * stride);
             const int pa = CH == 128 ? 64 * (p ^ (g & 1)) : 64 * p;  // rows g and g + 8: same parity
             const uint4 h0 = lds128(st + g * CH + pa);
             const uint4 h1 = lds128(st + (g + 8) * CH + pa);
             const uint4 l0 = lds128(st + 16 * CH + g * CH + pa);
             const uint4 l1 = lds128(st + 16 * CH + (g + 8) * CH + pa);
 #pragma unroll
-            for (int j = 0; j < 2 * NU; ++j) {
+            for (int j = 0; j < NU; ++j) {
                 mma_s8(acc_h[j], h0.x, h1.x, h0.y, h1.y, b[j].x, b[j].y);
                 mma_s8(acc_l[j], l0.x, l1.x, l0.y, l1.y, b[j].x, b[j].y);
             }
 #pragma unroll
-            for (int j = 0; j < 2 * NU; ++j) {
+            for (int j = 0; j < NU; ++j) {
                 mma_s8(acc_h[j], h0.z, h1.z, h0.w, h1.w, b[j].z, b[j].w);
                 mma_s8(acc_l[j], l0.z, l1.z, l0.w, l1.w, b[j].z, b[j].w);
             }
@@ -295,8 +298,8 @@ __device__ void product(const TdtPersistentArgs& a, const Smem& sm, int m, int r
             const float rs[2] = {__ldcg(a.q_scale + min(r0, rows - 1)), __ldcg(a.q_scale + min(r0 + 8, rows - 1))};
             unsigned long long tok[2] = {0ull, 0ull}, dur[2] = {0ull, 0ull};
 #pragma unroll
-            for (int j = 0; j < 2 * NU; ++j) {
-                const int col0 = (sm.first[m] + (j / 2) * static_cast<int>(gridDim.x)) * 16 + (j % 2) * 8 + 2 * q;
+            for (int j = 0; j < NU; ++j) {
+                const int col0 = (sm.first[m] + j * static_cast<int>(gridDim.x)) * 8 + 2 * q;
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
                     const int row = r0 + 8 * rr;
@@ -344,7 +347,7 @@ __device__ void product(const TdtPersistentArgs& a, const Smem& sm, int m, int r
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 2 * NU; ++j)
+            for (int j = 0; j < NU; ++j)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc_h[j][e] = acc_l[j][e] = 0;
             kk = 0;
@@ -370,7 +373,11 @@ __device__ void product_units(const TdtPersistentArgs& a, const Smem& sm, int m,
     case 1: product<1, CH, JOINT>(a, sm, m, rows, out, ldo); break;
     case 2: product<2, CH, JOINT>(a, sm, m, rows, out, ldo); break;
     case 3: product<3, CH, JOINT>(a, sm, m, rows, out, ldo); break;
-    default: product<4, CH, JOINT>(a, sm, m, rows, out, ldo); break;
+    case 4: product<4, CH, JOINT>(a, sm, m, rows, out, ldo); break;
+    case 5: product<5, CH, JOINT>(a, sm, m, rows, out, ldo); break;
+    case 6: product<6, CH, JOINT>(a, sm, m, rows, out, ldo); break;
+    case 7: product<7, CH, JOINT>(a, sm, m, rows, out, ldo); break;
+    default: product<8, CH, JOINT>(a, sm, m, rows, out, ldo); break;
     }
 }
 
@@ -446,18 +453,19 @@ __global__ void __launch_bounds__(kThreads, 1) tdt_persistent_kernel(const __gri
             sm.first[m] = first;
             sm.units[m] = units;
             sm.w[m] = smem + at;
-            at += units * 16 * M.smem_stride;
+            at += units * 8 * M.smem_stride;
         }
         sm.ring = smem + a.ring_offset;
         for (int m = 0; m < a.n_mats; ++m) {
             const TdtMatrix& M = a.mats[m];
-            const int segs = M.k / 16, per_unit = 16 * segs;
+            const int segs = M.k / 16, per_unit = 8 * segs;
             for (int i = tid; i < sm.units[m] * per_unit; i += kThreads) {
                 const int unit = i / per_unit, r = (i % per_unit) / segs, seg = i % segs;
-                const int row = (sm.first[m] + unit * G) * 16 + r;
+                const int row = (sm.first[m] + unit * G) * 8 + r;
+                const int xr = M.smem_stride % 128 == 0 ? (r & 1) << 2 : 0;
                 uint4 v = make_uint4(0u, 0u, 0u, 0u);
                 if (row < M.n) v = __ldg(reinterpret_cast<const uint4*>(M.w + static_cast<int64_t>(row) * M.ld) + seg);
-                *reinterpret_cast<uint4*>(sm.w[m] + (unit * 16 + r) * M.smem_stride + seg * 16) = v;
+                *reinterpret_cast<uint4*>(sm.w[m] + (unit * 8 + r) * M.smem_stride + (seg ^ xr) * 16) = v;
             }
         }
     }
@@ -660,10 +668,10 @@ bool tdt_persistent_plan(TdtPersistentArgs& a, int sms, size_t* smem_bytes) {
     for (int m = 0; m < a.n_mats; ++m) {
         TdtMatrix& M = a.mats[m];
         if (M.k % kChunk || M.ld % 16 || M.n <= 0) return false;
-        M.units = (M.n + 15) / 16;
+        M.units = (M.n + 7) / 8;
         M.max_units = (M.units + sms - 1) / sms;
-        if (M.max_units > 4) return false;
-        M.smem_stride = M.k + ((64 - M.k % 128) + 128) % 128;  // = 64 (mod 128): conflict-free rows
+        if (M.max_units > 8) return false;
+        M.smem_stride = M.k;  // rows unpadded; their segments are swizzled instead
     }
     int off = 0;
     for (int m = 0; m < a.n_mats; ++m) {
@@ -676,7 +684,7 @@ bool tdt_persistent_plan(TdtPersistentArgs& a, int sms, size_t* smem_bytes) {
             const TdtMatrix& M = a.mats[m];
             const int first = (c - M.offset + sms) % sms;
             const int units = first < M.units ? (M.units - first + sms - 1) / sms : 0;
-            total += static_cast<long>(units) * 16 * M.smem_stride;
+            total += static_cast<long>(units) * 8 * M.smem_stride;
         }
         max_total = total > max_total ? total : max_total;
     }
