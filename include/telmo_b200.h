@@ -72,10 +72,17 @@ int telmo_ctx_device(const telmo_ctx *ctx);
  * [n, k] matrix becomes 16-output panels (ceil(n/16) * 16 * k int8 values) and
  * ceil(n/16) * 16 f32 scales, one per output row, amax / 127 (src/quant.rs:190-198). */
 int telmo_encode_int8(const float *rows, size_t n, size_t k, int8_t *panel_values, float *scales);
+/* quant::encode for Precision::Q8_0 (src/quant.rs:202-269, quantize_q8_0_block :172-183): k a
+ * multiple of 32; the same panels of int8 values and ceil(n/16) * (k/32) * 16 f32 scales (f16
+ * values), panel, then block, then output. */
+int telmo_encode_q8_0(const float *rows, size_t n, size_t k, int8_t *panel_values, float *scales);
 
 /* Uploads a weight matrix in the reference's panel layout -- PackedWeights::from_parts
  * (src/kernels/mod.rs:214-237) over a pack's bytes (src/pack.rs:280-304) -- and lays it out for
- * the tensor cores. Only TELMO_PRECISION_INT8 runs in this build. */
+ * the tensor cores. TELMO_PRECISION_INT8 (one scale per output) and TELMO_PRECISION_Q8_0 (one
+ * scale per 32 inputs of each output, k a multiple of 32) run in this build; a Q8_0 row is
+ * re-encoded as two int8 levels under one row scale, within 1/64516 of the row's largest
+ * weight of the pack's exact values. */
 int telmo_weights_upload(telmo_ctx *ctx, int precision, size_t n, size_t k,
                          const void *panel_values, const float *scales, telmo_weights **out);
 void telmo_weights_free(telmo_weights *w);

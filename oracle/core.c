@@ -59,6 +59,52 @@ void oracle_decode_int8(const int8_t *values, const float *scales, size_t n, siz
     }
 }
 
+/* quantize_q8_0_block (src/quant.rs:172-183): d = amax / 127, q = round(x * (1 / d)) with the
+ * unrounded d, saturating to i8 as Rust's `as i8` does; returns d as its f16 value. */
+static float quantize_q8_0_block(const float *x, int8_t *q)
+{
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(x[i]));
+    float d = amax / 127.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float v = roundf(x[i] * id);
+        if (v < -128.0f) v = -128.0f;
+        if (v > 127.0f) v = 127.0f;
+        q[i] = (int8_t)v;
+    }
+    return oracle_f16_to_f32(oracle_f32_to_f16(d));
+}
+
+void oracle_encode_q8_0(const float *w, size_t n, size_t k, int8_t *values, float *scales)
+{
+    /* src/quant.rs:202-269, Precision::Q8_0: the int8 panels as Int8's; scales per block of 32
+     * inputs, in panel order, then block order, then output. k is a multiple of 32. */
+    size_t panels = (n + PANEL - 1) / PANEL, blocks = k / 32;
+    memset(values, 0, panels * k * PANEL);
+    memset(scales, 0, panels * blocks * PANEL * sizeof(float));
+    int8_t q[32];
+    for (size_t o = 0; o < n; o++) {
+        size_t p = o / PANEL, j = o % PANEL;
+        for (size_t b = 0; b < blocks; b++) {
+            scales[(p * blocks + b) * PANEL + j] = quantize_q8_0_block(w + o * k + 32 * b, q);
+            for (int i = 0; i < 32; i++) values[(p * k + 32 * b + i) * PANEL + j] = q[i];
+        }
+    }
+}
+
+void oracle_decode_q8_0(const int8_t *values, const float *scales, size_t n, size_t k, float *out)
+{
+    /* src/quant.rs:281-303: w = (q as f32) * d[block], exact (d is an f16 value). */
+    size_t blocks = k / 32;
+    for (size_t o = 0; o < n; o++) {
+        size_t p = o / PANEL, j = o % PANEL;
+        for (size_t i = 0; i < k; i++)
+            out[o * k + i] =
+                (float)values[(p * k + i) * PANEL + j] * scales[(p * blocks + i / 32) * PANEL + j];
+    }
+}
+
 uint16_t oracle_f32_to_bf16(float x)
 {
     /* src/quant.rs:149-156 */
@@ -290,6 +336,7 @@ typedef struct {
     size_t lda, m;
     const int8_t *values; /* int8 panels, or NULL for a row-major f32 b */
     const float *scales;
+    int q8;               /* values are Q8_0: one scale per 32 inputs */
     const float *b;       /* row-major f32 [k, ldb] */
     size_t ldb, n, k;
     float *c;
@@ -319,8 +366,15 @@ static void gemm_panels(const gemm_job *J, size_t p0, size_t p1)
             const float *bp;
             size_t k_stride;
             if (J->values) {
-                /* widen (src/kernels/scalar.rs:82-90): q as f32 * scale. */
+                /* widen (src/kernels/scalar.rs:82-106): q as f32 * scale, the scale of the
+                 * input's block of 32 for Q8_0 (src/kernels/mod.rs:577). */
                 const int8_t *src = J->values + (p * k + k0) * PANEL;
+                if (J->q8) {
+                    const float *s = J->scales + (p * (k / 32) + k0 / 32) * PANEL;
+                    for (size_t i = 0; i < kc; i++)
+                        for (int j = 0; j < PANEL; j++)
+                            wide[i * PANEL + j] = (float)src[i * PANEL + j] * s[(i / 32) * PANEL + j];
+                } else {
                 const float *s = J->scales + p * PANEL;
 #if defined(__x86_64__)
                 if (avx512)
@@ -330,6 +384,7 @@ static void gemm_panels(const gemm_job *J, size_t p0, size_t p1)
                     for (size_t i = 0; i < kc; i++)
                         for (int j = 0; j < PANEL; j++)
                             wide[i * PANEL + j] = (float)src[i * PANEL + j] * s[j];
+                }
                 bp = wide;
                 k_stride = PANEL;
             } else {
@@ -385,7 +440,16 @@ void oracle_linear_int8(const float *a, size_t lda, size_t m, const int8_t *valu
                         const float *scales, size_t n, size_t k, float *c, size_t ldc,
                         const float *bias, int act, float scale, int accumulate, int threads)
 {
-    gemm_job J = {a, lda, m, values, scales, NULL, 0, n, k, c, ldc, bias, act, scale, accumulate,
+    gemm_job J = {a, lda, m, values, scales, 0, NULL, 0, n, k, c, ldc, bias, act, scale, accumulate,
+                  0, 0};
+    run_gemm(&J, threads);
+}
+
+void oracle_linear_q8_0(const float *a, size_t lda, size_t m, const int8_t *values,
+                        const float *scales, size_t n, size_t k, float *c, size_t ldc,
+                        const float *bias, int act, float scale, int accumulate, int threads)
+{
+    gemm_job J = {a, lda, m, values, scales, 1, NULL, 0, n, k, c, ldc, bias, act, scale, accumulate,
                   0, 0};
     run_gemm(&J, threads);
 }
@@ -394,7 +458,7 @@ void oracle_matmul_rowmajor(const float *a, size_t lda, size_t m, const float *b
                             size_t n, size_t ldb, float *c, size_t ldc, const float *bias, int act,
                             float scale, int accumulate)
 {
-    gemm_job J = {a, lda, m, NULL, NULL, b, ldb, n, k, c, ldc, bias, act, scale, accumulate, 0, 0};
+    gemm_job J = {a, lda, m, NULL, NULL, 0, b, ldb, n, k, c, ldc, bias, act, scale, accumulate, 0, 0};
     run_gemm(&J, 1);
 }
 
@@ -436,6 +500,39 @@ void oracle_gemm_i8_x2_acc(const int8_t *hi, const int8_t *lo, size_t ldq, size_
                 int32_t wv = w[t * PANEL];
                 sh += (int32_t)hi[i * ldq + t] * wv;
                 sl += (int32_t)lo[i * ldq + t] * wv;
+            }
+            acc_hi[i * n + j] = sh;
+            acc_lo[i * n + j] = sl;
+        }
+}
+
+void oracle_q8_0_two_level(const int8_t *values, const float *scales, size_t n, size_t k,
+                           int8_t *w_hi, int8_t *w_lo, float *w_scale)
+{
+    /* The CUDA upload's re-encoding of a Q8_0 row (test restatement): w = q * d[block] exact,
+     * then the split rule of oracle_quantize_x2 with one scale per row. */
+    float *w = (float *)malloc((k ? k : 1) * sizeof(float));
+    for (size_t o = 0; o < n; o++) {
+        size_t p = o / PANEL, j = o % PANEL, blocks = k / 32;
+        for (size_t i = 0; i < k; i++)
+            w[i] = (float)values[(p * k + i) * PANEL + j] * scales[(p * blocks + i / 32) * PANEL + j];
+        oracle_quantize_x2(w, 1, k, k, w_hi + o * k, w_lo + o * k, k, w_scale + o);
+    }
+    free(w);
+}
+
+void oracle_gemm_i8_x2w_acc(const int8_t *hi, const int8_t *lo, size_t ldq, size_t m,
+                            const int8_t *w_hi, const int8_t *w_lo, size_t n, size_t k,
+                            int32_t *acc_hi, int32_t *acc_lo)
+{
+    /* Two-level weights (row-major [n, k]): acc_hi = hi . W_hi, acc_lo = lo . W_hi + hi . W_lo. */
+    for (size_t i = 0; i < m; i++)
+        for (size_t j = 0; j < n; j++) {
+            int32_t sh = 0, sl = 0;
+            for (size_t t = 0; t < k; t++) {
+                int32_t a = hi[i * ldq + t], b = lo[i * ldq + t];
+                sh += a * w_hi[j * k + t];
+                sl += b * w_hi[j * k + t] + a * w_lo[j * k + t];
             }
             acc_hi[i * n + j] = sh;
             acc_lo[i * n + j] = sl;

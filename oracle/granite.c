@@ -14,7 +14,20 @@ typedef struct {
     int8_t *v;
     float *s;
     size_t n, k;
+    int q8; /* Precision::Q8_0: one scale per 32 inputs */
 } mat;
+
+/* Kernels::linear over a matrix in either 8-bit precision. */
+static void mat_linear(const float *a, size_t lda, size_t m, const mat *w, float *c, size_t ldc,
+                       const float *bias, int act, float scale, int accumulate, int threads)
+{
+    if (w->q8)
+        oracle_linear_q8_0(a, lda, m, w->v, w->s, w->n, w->k, c, ldc, bias, act, scale, accumulate,
+                           threads);
+    else
+        oracle_linear_int8(a, lda, m, w->v, w->s, w->n, w->k, c, ldc, bias, act, scale, accumulate,
+                           threads);
+}
 typedef struct {
     float *p;
     size_t len;
@@ -151,21 +164,34 @@ static vec *find_vec(oracle_granite *g, const char *name, size_t *len)
     return NULL;
 }
 
-int oracle_granite_set_matrix(oracle_granite *g, const char *name, size_t n, size_t k,
-                              const int8_t *values, const float *scales)
+static int set_matrix(oracle_granite *g, const char *name, size_t n, size_t k, const int8_t *values,
+                      const float *scales, int q8)
 {
     size_t en, ek;
     mat *m = find_mat(g, name, &en, &ek);
-    if (!m || en != n || ek != k) return -1;
-    size_t panels = (n + 15) / 16;
+    if (!m || en != n || ek != k || (q8 && k % 32)) return -1;
+    size_t panels = (n + 15) / 16, nscales = panels * 16 * (q8 ? k / 32 : 1);
     free_mat(m);
     m->v = (int8_t *)malloc(panels * 16 * k);
-    m->s = (float *)malloc(panels * 16 * sizeof(float));
+    m->s = (float *)malloc(nscales * sizeof(float));
     memcpy(m->v, values, panels * 16 * k);
-    memcpy(m->s, scales, panels * 16 * sizeof(float));
+    memcpy(m->s, scales, nscales * sizeof(float));
     m->n = n;
     m->k = k;
+    m->q8 = q8;
     return 0;
+}
+
+int oracle_granite_set_matrix(oracle_granite *g, const char *name, size_t n, size_t k,
+                              const int8_t *values, const float *scales)
+{
+    return set_matrix(g, name, n, k, values, scales, 0);
+}
+
+int oracle_granite_set_matrix_q8_0(oracle_granite *g, const char *name, size_t n, size_t k,
+                                   const int8_t *values, const float *scales)
+{
+    return set_matrix(g, name, n, k, values, scales, 1);
 }
 
 int oracle_granite_set_vector(oracle_granite *g, const char *name, size_t len, const float *data)
@@ -223,8 +249,7 @@ size_t oracle_granite_frames_for(const oracle_granite *g, size_t rows)
 static void linear(const float *a, size_t m, const lin *l, float *c, int act, float scale,
                    int accumulate, int threads)
 {
-    oracle_linear_int8(a, l->w.k, m, l->w.v, l->w.s, l->w.n, l->w.k, c, l->w.n, l->b.p, act,
-                       scale, accumulate, threads);
+    mat_linear(a, l->w.k, m, &l->w, c, l->w.n, l->b.p, act, scale, accumulate, threads);
 }
 
 /* Row-wise work split into chunks of rows across threads, as for_rows does
@@ -342,8 +367,7 @@ static void attention_task(void *ctx, size_t task)
     oracle_matmul_rowmajor(q, 3 * d, len, kt, hd, len, ld, scores, len, NULL, ORACLE_ACT_NONE,
                            scale, 0);
     float *pos = (float *)malloc(len * positions * sizeof(float));
-    oracle_linear_int8(q, 3 * d, len, J->b->rel.v, J->b->rel.s, positions, hd, pos, positions,
-                       NULL, ORACLE_ACT_NONE, scale, 0, 1);
+    mat_linear(q, 3 * d, len, &J->b->rel, pos, positions, NULL, ORACLE_ACT_NONE, scale, 0, 1);
     for (size_t i = 0; i < len; i++) {
         float *row = scores + i * len;
         const float *p = pos + i * positions + ctxn - 1 - i;
@@ -366,8 +390,7 @@ static void block_span(const oracle_granite *g, const block *b, float *x, size_t
     size_t d = (size_t)c->d_model, cc = (size_t)c->conv_channels;
     feed_forward(g, &b->ff1, x, t, s, threads);
     layer_norm_rows(&b->norm_att, x, s->h, t, d);
-    oracle_linear_int8(s->h, d, t, b->qkv.v, b->qkv.s, 3 * d, d, s->big, 3 * d, NULL,
-                       ORACLE_ACT_NONE, 1.0f, 0, threads);
+    mat_linear(s->h, d, t, &b->qkv, s->big, 3 * d, NULL, ORACLE_ACT_NONE, 1.0f, 0, threads);
     att_job J = {g, b, s->big, t, (t + (size_t)c->context - 1) / (size_t)c->context, s->att};
     oracle_parallel_for((size_t)c->heads * J.blocks, threads, attention_task, &J);
     linear(s->att, t, &b->out, x, ORACLE_ACT_NONE, 1.0f, 1, threads);

@@ -36,6 +36,10 @@ float oracle_quantize_row_int8(const float *x, size_t k, int8_t *q);
 void oracle_encode_int8(const float *w, size_t n, size_t k, int8_t *values, float *scales);
 /* decode (src/quant.rs:272-303) for Precision::Int8. out is row-major [n, k]. */
 void oracle_decode_int8(const int8_t *values, const float *scales, size_t n, size_t k, float *out);
+/* encode / decode for Precision::Q8_0 (src/quant.rs:202-303, quantize_q8_0_block :172-183): k a
+ * multiple of 32, scales per block of 32 inputs in panel, block, output order. */
+void oracle_encode_q8_0(const float *w, size_t n, size_t k, int8_t *values, float *scales);
+void oracle_decode_q8_0(const int8_t *values, const float *scales, size_t n, size_t k, float *out);
 /* f32_to_bf16 / bf16_to_f32 / f32_to_f16 / f16_to_f32 (src/quant.rs:92-164). */
 uint16_t oracle_f32_to_bf16(float x);
 float oracle_bf16_to_f32(uint16_t h);
@@ -48,6 +52,11 @@ float oracle_f16_to_f32(uint16_t h);
  * weights widened per panel. threads > 1 splits panels like Pool::run (mod.rs:678-687); results
  * are bit-identical for every thread count. */
 void oracle_linear_int8(const float *a, size_t lda, size_t m, const int8_t *values,
+                        const float *scales, size_t n, size_t k, float *c, size_t ldc,
+                        const float *bias, int act, float scale, int accumulate, int threads);
+/* The same product over Q8_0 panels: widen with each input's block scale
+ * (src/kernels/scalar.rs:92-106, src/kernels/mod.rs:577). */
+void oracle_linear_q8_0(const float *a, size_t lda, size_t m, const int8_t *values,
                         const float *scales, size_t n, size_t k, float *c, size_t ldc,
                         const float *bias, int act, float scale, int accumulate, int threads);
 /* Kernels::matmul_serial with BView::row_major (src/kernels/mod.rs:324-340, :732-765):
@@ -70,6 +79,13 @@ void oracle_gemm_i8_x2_acc(const int8_t *hi, const int8_t *lo, size_t ldq, size_
 /* The CUDA epilogue over those sums, step for step:
  * v = ((float)acc_hi + (float)acc_lo * (1/254)) * row_scale[i] * w_scale[j]; then bias, act,
  * scale and accumulate as Epilogue (src/kernels/mod.rs:366-398, scalar.rs:110-124). */
+/* The CUDA build's re-encoding of Q8_0 panels into two int8 levels under one scale per row
+ * (row-major [n, k] outputs), and its integer sums with them: acc_lo = lo . W_hi + hi . W_lo. */
+void oracle_q8_0_two_level(const int8_t *values, const float *scales, size_t n, size_t k,
+                           int8_t *w_hi, int8_t *w_lo, float *w_scale);
+void oracle_gemm_i8_x2w_acc(const int8_t *hi, const int8_t *lo, size_t ldq, size_t m,
+                            const int8_t *w_hi, const int8_t *w_lo, size_t n, size_t k,
+                            int32_t *acc_hi, int32_t *acc_lo);
 void oracle_epilogue_x2(const int32_t *acc_hi, const int32_t *acc_lo, size_t m, size_t n,
                         const float *row_scale, const float *w_scales, const float *bias, int act,
                         float scale, int accumulate, float *c, size_t ldc);
@@ -115,6 +131,9 @@ void oracle_granite_free(oracle_granite *g);
  * The data is copied. Returns 0, or -1 for an unknown name or a wrong size. */
 int oracle_granite_set_matrix(oracle_granite *g, const char *name, size_t n, size_t k,
                               const int8_t *values, const float *scales);
+/* The same for a Q8_0 matrix (scales per 32 inputs, as oracle_encode_q8_0 lays them out). */
+int oracle_granite_set_matrix_q8_0(oracle_granite *g, const char *name, size_t n, size_t k,
+                                   const int8_t *values, const float *scales);
 int oracle_granite_set_vector(oracle_granite *g, const char *name, size_t len, const float *data);
 /* Names that were never set; 0 when the model is complete. */
 int oracle_granite_missing(const oracle_granite *g, char *first_missing, size_t cap);
@@ -144,6 +163,9 @@ void oracle_parakeet_free(oracle_parakeet *p);
 /* Pack entries by name, as Parakeet::from_pack reads them (src/parakeet.rs:691-795). */
 int oracle_parakeet_set_matrix(oracle_parakeet *p, const char *name, size_t n, size_t k,
                                const int8_t *values, const float *scales);
+/* The same for a Q8_0 matrix (scales per 32 inputs, as oracle_encode_q8_0 lays them out). */
+int oracle_parakeet_set_matrix_q8_0(oracle_parakeet *p, const char *name, size_t n, size_t k,
+                                    const int8_t *values, const float *scales);
 int oracle_parakeet_set_vector(oracle_parakeet *p, const char *name, size_t len, const float *data);
 /* Encoder frames for a number of feature frames (three stride-2 convolutions). */
 size_t oracle_parakeet_frames_for(size_t feature_frames);

@@ -61,6 +61,14 @@ def lib():
     L.oracle_linear_int8.argtypes = [_f32p, _sz, _sz, _i8p, _f32p, _sz, _sz, _f32p, _sz,
                                      ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int,
                                      ctypes.c_int]
+    L.oracle_linear_q8_0.argtypes = L.oracle_linear_int8.argtypes
+    L.oracle_granite_set_matrix_q8_0.restype = ctypes.c_int
+    L.oracle_granite_set_matrix_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _sz, _sz, _i8p,
+                                                 _f32p]
+    L.oracle_encode_q8_0.argtypes = [_f32p, _sz, _sz, _i8p, _f32p]
+    L.oracle_decode_q8_0.argtypes = [_i8p, _f32p, _sz, _sz, _f32p]
+    L.oracle_q8_0_two_level.argtypes = [_i8p, _f32p, _sz, _sz, _i8p, _i8p, _f32p]
+    L.oracle_gemm_i8_x2w_acc.argtypes = [_i8p, _i8p, _sz, _sz, _i8p, _i8p, _sz, _sz, _i32p, _i32p]
     L.oracle_matmul_rowmajor.argtypes = [_f32p, _sz, _sz, _f32p, _sz, _sz, _sz, _f32p, _sz,
                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_float,
                                          ctypes.c_int]
@@ -139,6 +147,24 @@ def decode_int8(values, scales, n, k):
     return out
 
 
+def encode_q8_0(w):
+    """Row-major [n, k] f32 (k a multiple of 32) -> Q8_0 panels: (values int8
+    [ceil(n/16)*16*k], scales f32 [ceil(n/16)*(k/32)*16])."""
+    w = _c(w, np.float32)
+    n, k = w.shape
+    panels = (n + 15) // 16
+    values = np.zeros(panels * 16 * k, np.int8)
+    scales = np.zeros(panels * (k // 32) * 16, np.float32)
+    lib().oracle_encode_q8_0(w.reshape(-1), n, k, values, scales)
+    return values, scales
+
+
+def decode_q8_0(values, scales, n, k):
+    out = np.zeros((n, k), np.float32)
+    lib().oracle_decode_q8_0(_c(values, np.int8), _c(scales, np.float32), n, k, out.reshape(-1))
+    return out
+
+
 # ---- the matrix product -----------------------------------------------------------------------
 
 def linear_int8(a, values, scales, n, k, bias=None, act=ACT_NONE, scale=1.0, c=None,
@@ -153,6 +179,52 @@ def linear_int8(a, values, scales, n, k, bias=None, act=ACT_NONE, scale=1.0, c=N
                              out.reshape(-1) if m else np.zeros(1, np.float32), n, _ptr(b), act,
                              float(scale), int(accumulate), int(threads))
     return out
+
+
+def linear_q8_0(a, values, scales, n, k, bias=None, act=ACT_NONE, scale=1.0, c=None,
+                accumulate=False, threads=1):
+    """Kernels::linear with Q8_0 PackedWeights: returns c [m, n] f32."""
+    a = _c(a, np.float32)
+    m = a.shape[0]
+    out = np.zeros((m, n), np.float32) if c is None else np.array(c, np.float32, copy=True)
+    b = None if bias is None else _c(bias, np.float32)
+    lib().oracle_linear_q8_0(a.reshape(-1), a.shape[1], m, _c(values, np.int8),
+                             _c(scales, np.float32), n, k, out.reshape(-1), n, _ptr(b), act,
+                             float(scale), int(accumulate), int(threads))
+    return out
+
+
+def q8_0_two_level(values, scales, n, k):
+    """The CUDA upload's re-encoding of Q8_0 panels: (w_hi [n, k], w_lo [n, k], w_scale [n])."""
+    w_hi = np.zeros((n, k), np.int8)
+    w_lo = np.zeros((n, k), np.int8)
+    ws = np.zeros(n, np.float32)
+    lib().oracle_q8_0_two_level(_c(values, np.int8), _c(scales, np.float32), n, k,
+                                w_hi.reshape(-1), w_lo.reshape(-1), ws)
+    return w_hi, w_lo, ws
+
+
+def gemm_i8_x2w_acc(hi, lo, w_hi, w_lo, n, k):
+    """Integer sums against two-level weights: (hi . W_hi, lo . W_hi + hi . W_lo)."""
+    hi = _c(hi, np.int8)
+    lo = _c(lo, np.int8)
+    m = hi.shape[0]
+    acc_hi = np.zeros((m, n), np.int32)
+    acc_lo = np.zeros((m, n), np.int32)
+    lib().oracle_gemm_i8_x2w_acc(hi.reshape(-1), lo.reshape(-1), k, m, _c(w_hi, np.int8).reshape(-1),
+                                 _c(w_lo, np.int8).reshape(-1), n, k, acc_hi.reshape(-1),
+                                 acc_lo.reshape(-1))
+    return acc_hi, acc_lo
+
+
+def linear_x2_q8_0(a, values, scales, n, k, bias=None, act=ACT_NONE, scale=1.0, c=None,
+                   accumulate=False):
+    """The CUDA linear's exact arithmetic over Q8_0 panels: the two-level re-encoding, split
+    activations, i32 sums (lo . W_hi + hi . W_lo into the low sums), the x2 epilogue."""
+    w_hi, w_lo, ws = q8_0_two_level(values, scales, n, k)
+    hi, lo, s = quantize_x2(a)
+    acc_hi, acc_lo = gemm_i8_x2w_acc(hi, lo, w_hi, w_lo, n, k)
+    return epilogue_x2(acc_hi, acc_lo, s, ws, bias, act, scale, c, accumulate)
 
 
 def quantize_x2(x):
@@ -270,9 +342,10 @@ class Granite:
             raise ValueError("the Granite config does not fit together")
         for name, entry in entries.items():
             if isinstance(entry, tuple):
-                values, scales, n, k = entry
-                rc = lib().oracle_granite_set_matrix(self._h, name.encode(), n, k,
-                                                     _c(values, np.int8), _c(scales, np.float32))
+                values, scales, n, k = entry[:4]
+                q8 = len(entry) > 4 and entry[4] == "q8_0"
+                setter = lib().oracle_granite_set_matrix_q8_0 if q8 else lib().oracle_granite_set_matrix
+                rc = setter(self._h, name.encode(), n, k, _c(values, np.int8), _c(scales, np.float32))
             else:
                 data = _c(entry, np.float32).reshape(-1)
                 rc = lib().oracle_granite_set_vector(self._h, name.encode(), data.size, data)
@@ -340,6 +413,9 @@ def _parakeet_lib():
     L.oracle_parakeet_new.restype = ctypes.c_void_p
     L.oracle_parakeet_new.argtypes = [ctypes.POINTER(ParakeetConfig)]
     L.oracle_parakeet_free.argtypes = [ctypes.c_void_p]
+    L.oracle_parakeet_set_matrix_q8_0.restype = ctypes.c_int
+    L.oracle_parakeet_set_matrix_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _sz, _sz, _i8p,
+                                                  _f32p]
     L.oracle_parakeet_set_matrix.restype = ctypes.c_int
     L.oracle_parakeet_set_matrix.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _sz, _sz, _i8p,
                                              _f32p]
@@ -402,9 +478,10 @@ class Parakeet:
             raise ValueError("the Parakeet config does not fit together")
         for name, entry in entries.items():
             if isinstance(entry, tuple):
-                values, scales, n, k = entry
-                rc = L.oracle_parakeet_set_matrix(self._h, name.encode(), n, k,
-                                                  _c(values, np.int8), _c(scales, np.float32))
+                values, scales, n, k = entry[:4]
+                q8 = len(entry) > 4 and entry[4] == "q8_0"
+                setter = L.oracle_parakeet_set_matrix_q8_0 if q8 else L.oracle_parakeet_set_matrix
+                rc = setter(self._h, name.encode(), n, k, _c(values, np.int8), _c(scales, np.float32))
             else:
                 data = _c(entry, np.float32).reshape(-1)
                 rc = L.oracle_parakeet_set_vector(self._h, name.encode(), data.size, data)

@@ -14,6 +14,7 @@ typedef struct {
     int8_t *v;
     float *s;
     size_t n, k;
+    int q8; /* Precision::Q8_0: one scale per 32 inputs */
 } pmat;
 typedef struct {
     float *p;
@@ -149,21 +150,34 @@ static pvec *pfind_v(oracle_parakeet *p, const char *name, size_t *len)
     return NULL;
 }
 
-int oracle_parakeet_set_matrix(oracle_parakeet *p, const char *name, size_t n, size_t k,
-                               const int8_t *values, const float *scales)
+static int pset_matrix(oracle_parakeet *p, const char *name, size_t n, size_t k, const int8_t *values,
+                       const float *scales, int q8)
 {
     size_t en, ek;
     pmat *m = pfind_m(p, name, &en, &ek);
-    if (!m || en != n || ek != k) return -1;
-    size_t panels = (n + 15) / 16;
+    if (!m || en != n || ek != k || (q8 && k % 32)) return -1;
+    size_t panels = (n + 15) / 16, nscales = panels * 16 * (q8 ? k / 32 : 1);
     pfree_m(m);
     m->v = (int8_t *)malloc(panels * 16 * k);
-    m->s = (float *)malloc(panels * 16 * sizeof(float));
+    m->s = (float *)malloc(nscales * sizeof(float));
     memcpy(m->v, values, panels * 16 * k);
-    memcpy(m->s, scales, panels * 16 * sizeof(float));
+    memcpy(m->s, scales, nscales * sizeof(float));
     m->n = n;
     m->k = k;
+    m->q8 = q8;
     return 0;
+}
+
+int oracle_parakeet_set_matrix(oracle_parakeet *p, const char *name, size_t n, size_t k,
+                               const int8_t *values, const float *scales)
+{
+    return pset_matrix(p, name, n, k, values, scales, 0);
+}
+
+int oracle_parakeet_set_matrix_q8_0(oracle_parakeet *p, const char *name, size_t n, size_t k,
+                                    const int8_t *values, const float *scales)
+{
+    return pset_matrix(p, name, n, k, values, scales, 1);
 }
 
 int oracle_parakeet_set_vector(oracle_parakeet *p, const char *name, size_t len, const float *data)
@@ -181,8 +195,12 @@ int oracle_parakeet_set_vector(oracle_parakeet *p, const char *name, size_t len,
 static void plinear(const pmat *w, const float *a, size_t m, float *c, const float *bias, int act,
                     float scale, int accumulate, int threads)
 {
-    oracle_linear_int8(a, w->k, m, w->v, w->s, w->n, w->k, c, w->n, bias, act, scale, accumulate,
-                       threads);
+    if (w->q8)
+        oracle_linear_q8_0(a, w->k, m, w->v, w->s, w->n, w->k, c, w->n, bias, act, scale, accumulate,
+                           threads);
+    else
+        oracle_linear_int8(a, w->k, m, w->v, w->s, w->n, w->k, c, w->n, bias, act, scale, accumulate,
+                           threads);
 }
 
 static void pnorm(const pvec *g, const pvec *b, const float *x, float *out, size_t t, size_t d)

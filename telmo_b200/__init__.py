@@ -133,15 +133,19 @@ class DeviceWeights:
 
 class PackedWeights:
     """A weight matrix of ``n`` outputs and ``k`` inputs in the reference's panel layout
-    (src/kernels/mod.rs:177-304): 16-output panels, int8 values, one f32 scale per output."""
+    (src/kernels/mod.rs:177-304): 16-output panels of int8 values with one f32 scale per output
+    (Int8) or per block of 32 inputs of each output (Q8_0, src/quant.rs:8-13)."""
 
     def __init__(self, n: int, k: int, precision: Precision, values: np.ndarray,
                  scales: np.ndarray):
         panels = (n + 15) // 16
-        if precision != Precision.INT8:
+        if precision not in (Precision.INT8, Precision.Q8_0):
             raise TelmoError(_lib.TELMO_ERR_UNSUPPORTED,
-                             f"{precision.name}: this build runs int8 weights only")
-        if values.size != panels * 16 * k or scales.size != panels * 16:
+                             f"{precision.name}: this build runs int8 weights (INT8, Q8_0) only")
+        if precision == Precision.Q8_0 and k % 32:
+            raise TelmoError(_lib.TELMO_ERR_ARGUMENT, "Q8_0 needs inputs in multiples of 32")
+        n_scales = panels * 16 * (k // 32 if precision == Precision.Q8_0 else 1)
+        if values.size != panels * 16 * k or scales.size != n_scales:
             raise TelmoError(_lib.TELMO_ERR_ARGUMENT, "panel sizes do not match n and k")
         self.n, self.k, self.precision = n, k, precision
         self.values = np.ascontiguousarray(values, dtype=np.int8)
@@ -154,9 +158,13 @@ class PackedWeights:
         rows = np.ascontiguousarray(rows, dtype=np.float32).reshape(n, k)
         panels = (n + 15) // 16
         values = np.zeros(panels * 16 * k, np.int8)
-        scales = np.zeros(panels * 16, np.float32)
-        check(_lib.load().telmo_encode_int8(rows.ctypes.data, n, k, values.ctypes.data,
-                                            scales.ctypes.data))
+        if precision == Precision.Q8_0:
+            scales = np.zeros(panels * 16 * (k // 32), np.float32)
+            encode = _lib.load().telmo_encode_q8_0
+        else:
+            scales = np.zeros(panels * 16, np.float32)
+            encode = _lib.load().telmo_encode_int8
+        check(encode(rows.ctypes.data, n, k, values.ctypes.data, scales.ctypes.data))
         return PackedWeights(n, k, precision, values, scales)
 
     def upload(self, ctx: Context) -> DeviceWeights:

@@ -18,6 +18,16 @@ TELMO_ERR_DEVICE_TIMEOUT = -3
 TELMO_ERR_UNSUPPORTED = -4
 TELMO_ERR_MODEL = -5
 
+# Weight precisions (include/telmo_b200.h, telmo's Precision).
+PRECISIONS = {"f32": 0, "f16": 1, "bf16": 2, "int8": 3, "q8_0": 4}
+
+
+def precision_code(name: str) -> int:
+    try:
+        return PRECISIONS[name]
+    except KeyError:
+        raise ValueError(f"unknown weight precision {name!r}") from None
+
 _c = ctypes
 _vp = _c.c_void_p
 _sz = _c.c_size_t
@@ -32,6 +42,7 @@ SIGNATURES = {
     "telmo_ctx_check": (_int, [_vp, _vp]),
     "telmo_ctx_device": (_int, [_vp]),
     "telmo_encode_int8": (_int, [_vp, _sz, _sz, _vp, _vp]),
+    "telmo_encode_q8_0": (_int, [_vp, _sz, _sz, _vp, _vp]),
     "telmo_weights_upload": (_int, [_vp, _int, _sz, _sz, _vp, _vp, _c.POINTER(_vp)]),
     "telmo_weights_free": (None, [_vp]),
     "telmo_weights_shape": (_int, [_vp, _c.POINTER(_sz), _c.POINTER(_sz)]),

@@ -4,6 +4,8 @@
 #include "frontend.h"
 #include "kernels.h"
 
+#include <cuda_fp16.h>
+
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -138,6 +140,12 @@ extern "C" int telmo_encode_int8(const float* rows, size_t n, size_t k, int8_t* 
     return TELMO_OK;
 }
 
+extern "C" int telmo_encode_q8_0(const float* rows, size_t n, size_t k, int8_t* values, float* scales) {
+    if (!rows || !values || !scales || k % 32) return TELMO_ERR_ARGUMENT;
+    encode_q8_0_panels(rows, n, k, values, scales);
+    return TELMO_OK;
+}
+
 namespace telmo {
 
 void encode_int8_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales) {
@@ -162,24 +170,80 @@ void encode_int8_panels(const float* rows, size_t n, size_t k, int8_t* values, f
     }
 }
 
+void encode_q8_0_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales) {
+    // quant::encode, Precision::Q8_0 (src/quant.rs:202-269) with quantize_q8_0_block
+    // (:172-183): per block of 32 inputs d = amax / 127, q = round(x / d) with the unrounded
+    // reciprocal, the scale kept as its f16 value; scales run panel, then block, then output.
+    const size_t panels = (n + 15) / 16, blocks = k / 32;
+    memset(values, 0, panels * 16 * k);
+    memset(scales, 0, panels * blocks * 16 * sizeof(float));
+    for (size_t o = 0; o < n; ++o) {
+        const float* x = rows + o * k;
+        const size_t p = o / 16, j = o % 16;
+        for (size_t b = 0; b < blocks; ++b) {
+            float amax = 0.0f;
+            for (size_t i = 32 * b; i < 32 * b + 32; ++i) amax = std::fmax(amax, std::fabs(x[i]));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            for (size_t i = 32 * b; i < 32 * b + 32; ++i) {
+                const float q = std::fmin(std::fmax(std::round(x[i] * id), -128.0f), 127.0f);
+                values[(p * k + i) * 16 + j] = static_cast<int8_t>(q);
+            }
+            scales[(p * blocks + b) * 16 + j] = __half2float(__float2half_rn(d));
+        }
+    }
+}
+
 int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
-                   const float* scales, DevWeights* out) {
-    if (precision != TELMO_PRECISION_INT8)
+                   const float* scales, DevWeights* out, const int* col_perm) {
+    if (precision != TELMO_PRECISION_INT8 && precision != TELMO_PRECISION_Q8_0)
         return ctx->fail(TELMO_ERR_UNSUPPORTED,
-                         "precision %d: this build runs int8 weights (TELMO_PRECISION_INT8) only",
+                         "precision %d: this build runs int8 weights (TELMO_PRECISION_INT8, "
+                         "TELMO_PRECISION_Q8_0) only",
                          precision);
     if (!panel_values || !scales || n == 0 || k == 0 || n > (1u << 30) || k > (1u << 30))
         return ctx->fail(TELMO_ERR_ARGUMENT, "weights: bad sizes n=%zu k=%zu or null data", n, k);
+    const bool q8 = precision == TELMO_PRECISION_Q8_0;
+    if (q8 && k % 32)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: Q8_0 needs inputs in multiples of 32 (k=%zu)", k);
     const size_t ld = round_up(k, 16);
-    std::vector<int8_t> rows(n * ld, 0);
+    std::vector<int8_t> rows(n * ld, 0), lo(q8 ? n * ld : 0, 0);
     std::vector<float> sc(n);
+    std::vector<float> w(q8 ? k : 0);
     const int8_t* v = static_cast<const int8_t*>(panel_values);
+    const size_t blocks = k / 32;
     for (size_t o = 0; o < n; ++o) {
         const size_t p = o / 16, j = o % 16;
         const int8_t* src = v + p * k * 16 + j;
         int8_t* dst = rows.data() + o * ld;
-        for (size_t i = 0; i < k; ++i) dst[i] = src[i * 16];
-        sc[o] = scales[p * 16 + j];
+        if (!q8) {
+            for (size_t i = 0; i < k; ++i) dst[i] = src[(col_perm ? col_perm[i] : i) * 16];
+            sc[o] = scales[p * 16 + j];
+            continue;
+        }
+        // Q8_0 (src/quant.rs:8-13): w = q * d[block], exact in f32 (d is an f16 value). The row
+        // is re-encoded as s * (hi + lo / 254) with one scale per row, by the rule the
+        // activations use (quant.cu): s = amax / 127, hi = round(w / s), lo = round((w - hi s) *
+        // 254 / s), each clamped to [-127, 127]; the representation is within s / 508 (1/64516 of
+        // the row's largest weight) of w. The GEMM adds hi_a . lo_w to the low-level sum.
+        float amax = 0.0f;
+        for (size_t i = 0; i < k; ++i) {
+            const size_t c = col_perm ? static_cast<size_t>(col_perm[i]) : i;
+            w[i] = static_cast<float>(src[c * 16]) * scales[(p * blocks + c / 32) * 16 + j];
+            amax = std::fmax(amax, std::fabs(w[i]));
+        }
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const float id_lo = id * 254.0f;
+        int8_t* dlo = lo.data() + o * ld;
+        for (size_t i = 0; i < k; ++i) {
+            const float h = std::fmin(std::fmax(std::round(w[i] * id), -127.0f), 127.0f);
+            const float e = std::fma(-h, d, w[i]);
+            const float l = std::fmin(std::fmax(std::round(e * id_lo), -127.0f), 127.0f);
+            dst[i] = static_cast<int8_t>(h);
+            dlo[i] = static_cast<int8_t>(l);
+        }
+        sc[o] = d;
     }
     out->n = static_cast<int>(n);
     out->k = static_cast<int>(k);
@@ -188,13 +252,20 @@ int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* pane
     if (int rc = ctx->cuda(cudaMalloc(&out->scales, n * sizeof(float)), "weights")) return rc;
     if (int rc = ctx->cuda(cudaMemcpy(out->values, rows.data(), rows.size(), cudaMemcpyHostToDevice), "weights"))
         return rc;
+    if (q8) {
+        if (int rc = ctx->cuda(cudaMalloc(&out->lo_values, lo.size()), "weights")) return rc;
+        if (int rc = ctx->cuda(cudaMemcpy(out->lo_values, lo.data(), lo.size(), cudaMemcpyHostToDevice), "weights"))
+            return rc;
+    }
     return ctx->cuda(cudaMemcpy(out->scales, sc.data(), n * sizeof(float), cudaMemcpyHostToDevice), "weights");
 }
 
 void free_weights(DevWeights* w) {
     if (w->values) cudaFree(w->values);
+    if (w->lo_values) cudaFree(w->lo_values);
     if (w->scales) cudaFree(w->scales);
     w->values = nullptr;
+    w->lo_values = nullptr;
     w->scales = nullptr;
 }
 

@@ -36,8 +36,10 @@ struct Weights {
 inline Ctx* as_ctx(telmo_ctx* c) { return reinterpret_cast<Ctx*>(c); }
 
 void encode_int8_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales);
+void encode_q8_0_panels(const float* rows, size_t n, size_t k, int8_t* values, float* scales);
+// col_perm (or null): column i of the uploaded matrix is the pack's column col_perm[i].
 int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
-                   const float* scales, DevWeights* out);
+                   const float* scales, DevWeights* out, const int* col_perm = nullptr);
 void free_weights(DevWeights* w);
 
 }  // namespace telmo

@@ -2,7 +2,9 @@
 //
 // C[m, n] = epilogue(A[m, k] . W[n, k]^T) where A arrives as two int8 levels per element
 // (A = s_row * (hi + lo / 254)) and W is int8 with one scale per output row, the reference's
-// Precision::Int8 (src/quant.rs:1-13). Each level is an exact int8 x int8 -> s32 product
+// Precision::Int8 (src/quant.rs:1-13), or -- for Q8_0 packs, re-encoded at upload -- two int8
+// levels under one row scale, W = s_w * (W_hi + W_lo / 254), whose W_lo . A_hi product joins the
+// low-level sums. Each level is an exact int8 x int8 -> s32 product
 // accumulated in TMEM, so both i32 sums are bit-exact; the epilogue combines them, applies the
 // row and weight scales and the reference's Epilogue (bias, act, scale, accumulate;
 // src/kernels/mod.rs:366-398) and stores f32 or bf16.
@@ -48,11 +50,12 @@ constexpr int kOutStaging = kEpiWarps * kStageOutBytes;  // one buffer per epilo
 
 // Pipeline shape per variant: CG = 1, one CTA per 128-feature tile, stages of W + A_hi + A_lo
 // (48 KB); CG = 2, a CTA pair per 256-feature tile, each CTA staging its 128 weight rows and
-// one activation level (32 KB), so the same shared memory holds six stages.
-template <int CG>
+// one activation level (32 KB), so the same shared memory holds six stages. WL (two-level
+// weights, from Q8_0 packs; single CTAs only): W + A_hi + A_lo + W_lo (64 KB), three stages.
+template <int CG, bool WL = false>
 struct Shape {
-    static constexpr int kStageBytes = (CG == 1 ? 3 : 2) * kTileBytes;
-    static constexpr int kStages = CG == 1 ? 4 : 6;
+    static constexpr int kStageBytes = (CG == 1 ? (WL ? 4 : 3) : 2) * kTileBytes;
+    static constexpr int kStages = CG == 1 ? (WL ? 3 : 4) : 6;
     static constexpr int kSmemBytes = kStages * kStageBytes + kOutStaging + 1024 + 256;
 };
 
@@ -203,13 +206,15 @@ __device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_
     }
 }
 
-template <int CG>
+template <int CG, bool WL>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
                  const __grid_constant__ CUtensorMap map_lo, const __grid_constant__ CUtensorMap map_out,
-                 const __grid_constant__ CUtensorMap map_out_lo, const Params p) {
-    constexpr int kStages = Shape<CG>::kStages;
-    constexpr int kStageBytes = Shape<CG>::kStageBytes;
+                 const __grid_constant__ CUtensorMap map_out_lo, const __grid_constant__ CUtensorMap map_wl,
+                 const Params p) {
+    static_assert(!WL || CG == 1, "two-level weights run on single CTAs");
+    constexpr int kStages = Shape<CG, WL>::kStages;
+    constexpr int kStageBytes = Shape<CG, WL>::kStageBytes;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + kStages * kStageBytes;
@@ -246,6 +251,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         prefetch_tensormap(&map_w);
         prefetch_tensormap(&map_hi);
         prefetch_tensormap(&map_lo);
+        if (WL) prefetch_tensormap(&map_wl);
         if (p.out_path != kDirect) prefetch_tensormap(&map_out);
         if (p.out_path != kDirect && p.out_kind == kOutF16Split) prefetch_tensormap(&map_out_lo);
     }
@@ -286,6 +292,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                         tma_load_2d(&map_w, &full[stage], st, kb * BK, n0);
                         tma_load_2d(&map_hi, &full[stage], st + kTileBytes, kb * BK, m0);
                         tma_load_2d(&map_lo, &full[stage], st + 2 * kTileBytes, kb * BK, m0);
+                        if (WL) tma_load_2d(&map_wl, &full[stage], st + 3 * kTileBytes, kb * BK, n0);
                     } else {
                         // Both CTAs' loads count on the first CTA's barrier, which expects them all.
                         // The first CTA stages the high level (B columns 0..127), the second the low.
@@ -301,6 +308,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
     } else if (warp == 1) {
         // ---- MMA issuer (the pair's first CTA issues for both) -----------------------------
         constexpr uint32_t idesc = idesc_i8(CG * 128, 2 * BM);
+        constexpr uint32_t idesc_wl = idesc_i8(128, BM);  // W_lo x the high level only
         int stage = 0;
         uint32_t phase = 0;
         int it = 0;
@@ -323,11 +331,16 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                 if (lane == 0) {
                     const uint32_t w = smem_u32(smem + stage * kStageBytes);
                     const uint32_t x = w + kTileBytes;  // hi rows, then lo rows: N = 256
+                    const uint32_t wl = w + 3 * kTileBytes;
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; ++kk) {
                         const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
                         if (CG == 1) mma_i8(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc, acc);
                         else mma_i8_pair(d, sw128_desc(w + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc, acc);
+                        // Two-level weights: W_lo . A_hi joins A_lo . W into the low sums (both
+                        // carry the 1/254 step); A_lo . W_lo (1/254^2) is left out.
+                        if (WL)
+                            mma_i8(d + BM, sw128_desc(wl + kk * UMMA_K), sw128_desc(x + kk * UMMA_K), idesc_wl, 1u);
                     }
                     if (CG == 1) {
                         mma_commit(&empty[stage]);
@@ -561,19 +574,25 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     if (g.m <= 0 || !g.w || g.w->n <= 0) return cudaSuccess;
     if ((g.a.ld % 16) || (g.w->ld % 16)) return cudaErrorInvalidValue;
     const DevWeights& w = *g.w;
-    CUtensorMap mw, mh, ml;
+    CUtensorMap mw, mh, ml, mwl;
     if (!make_map(&mw, w.values, w.n, w.k, w.ld) || !make_map(&mh, g.a.hi, g.m, w.k, g.a.ld) ||
         !make_map(&ml, g.a.lo, g.m, w.k, g.a.ld))
         return cudaErrorInvalidValue;
+    const bool two_level = w.lo_values != nullptr;
+    if (two_level ? !make_map(&mwl, w.lo_values, w.n, w.k, w.ld) : false) return cudaErrorInvalidValue;
+    if (!two_level) mwl = mw;  // not read
     static uint64_t configured = 0;  // one bit per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !(configured >> dev & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Shape<1>::kSmemBytes);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_i8x2_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            e = cudaFuncSetAttribute(gemm_i8x2_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Shape<2>::kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_i8x2_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Shape<1, true>::kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= uint64_t(1) << dev;
     }
@@ -596,7 +615,7 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
              g.out, g.ldc, g.out_kind, path, g.error};
     // Products of at least 256 features run on CTA pairs (each MMA spans both SMs' tensor
     // cores; each CTA stages a third less per multiply-add), narrower ones on single CTAs.
-    if (w.n >= 2 * BN) {
+    if (w.n >= 2 * BN && !two_level) {
         const int tiles = ((g.m + BM - 1) / BM) * ((w.n + 2 * BN - 1) / (2 * BN));
         const int pairs = std::min(tiles, num_sms() / 2);
         cudaLaunchConfig_t cfg = {};
@@ -611,13 +630,16 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8x2_kernel<2>, mw, mh, ml, mo, mo_lo, p);
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8x2_kernel<2, false>, mw, mh, ml, mo, mo_lo, mwl, p);
         if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
     const int tiles = ((g.m + BM - 1) / BM) * ((w.n + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8x2_kernel<1><<<grid, kThreads, Shape<1>::kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, p);
+    if (two_level)
+        gemm_i8x2_kernel<1, true><<<grid, kThreads, Shape<1, true>::kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, mwl, p);
+    else
+        gemm_i8x2_kernel<1, false><<<grid, kThreads, Shape<1>::kSmemBytes, stream>>>(mw, mh, ml, mo, mo_lo, mwl, p);
     return cudaGetLastError();
 }
 

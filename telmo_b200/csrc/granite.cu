@@ -589,6 +589,12 @@ extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int
     if (static_cast<size_t>(e.n) != n || static_cast<size_t>(e.k) != k)
         return g->ctx->fail(TELMO_ERR_MODEL, "granite: %s is [%zu, %zu], expected [%d, %d]", name, n, k, e.n, e.k);
     if (int rc = g->ctx->use_device()) return rc;
+    for (auto& b : g->blocks)
+        if (e.mat == &b.rel && precision != TELMO_PRECISION_INT8)
+            return g->ctx->fail(TELMO_ERR_UNSUPPORTED,
+                                "granite: %s feeds the attention kernel as exact integers; it needs "
+                                "TELMO_PRECISION_INT8",
+                                name);
     free_weights(e.mat);
     g->finalized = false;
     if (int rc = upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat)) return rc;

@@ -22,11 +22,13 @@ struct QuantAct {
 };
 
 // Device weights of one linear layer: int8 row-major [n, ld] (ld = k rounded up to 16 bytes,
-// zero padded), per-output f32 scales.
+// zero padded), per-output f32 scales. Q8_0 packs carry a second int8 level: the row stands for
+// scale * (values + lo_values / 254), the split the activations use.
 struct DevWeights {
     int n = 0, k = 0;
     int64_t ld = 0;
     int8_t* values = nullptr;
+    int8_t* lo_values = nullptr;  // null for Int8 packs
     float* scales = nullptr;
 };
 

@@ -573,8 +573,11 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     // max_symbols tokens on a frame, so frames * (max_symbols + 1) passes bound the loop.
     const int64_t bound = max_frames * (c.max_symbols + 1) + 1;
 
-    // The persistent decoder: the whole loop in one cooperative launch (tdt_persistent.cu).
-    if (decoder == 1 && max_frames > 0) {
+    // The persistent decoder: the whole loop in one cooperative launch (tdt_persistent.cu), for
+    // one-level (Int8) prediction and joint weights.
+    bool one_level = joint.lo_values == nullptr && pred_proj.lo_values == nullptr;
+    for (const DevWeights& w : lstm) one_level = one_level && w.lo_values == nullptr;
+    if (decoder == 1 && max_frames > 0 && one_level) {
         TdtPersistentArgs pa;
         auto mat = [](const DevWeights& w, const float* bias) {
             TdtMatrix m;
@@ -809,18 +812,14 @@ extern "C" int telmo_parakeet_set_matrix(telmo_parakeet* pp, const char* name, i
     if (int rc = p->ctx->use_device()) return rc;
     free_weights(e.mat);
     p->finalized = false;
-    if (e.mat == &p->linear && precision == TELMO_PRECISION_INT8 && panel_values) {
-        // Column f * ch + c of the uploaded matrix is the pack's column c * freqs + f.
+    if (e.mat == &p->linear) {
+        // Column f * ch + c of the uploaded matrix is the pack's column c * freqs + f (a Q8_0
+        // row is re-encoded with one row scale, which no column order changes).
         const int ch = p->c.sub_channels, freqs = p->c.n_mels / 8;
-        const size_t panels = (n + 15) / 16;
-        const int8_t* v = static_cast<const int8_t*>(panel_values);
-        std::vector<int8_t> perm(panels * 16 * k);
-        for (size_t pn = 0; pn < panels; ++pn)
-            for (int f = 0; f < freqs; ++f)
-                for (int cc = 0; cc < ch; ++cc)
-                    memcpy(&perm[(pn * k + static_cast<size_t>(f) * ch + cc) * 16],
-                           &v[(pn * k + static_cast<size_t>(cc) * freqs + f) * 16], 16);
-        return upload_weights(p->ctx, precision, n, k, perm.data(), scales, e.mat);
+        std::vector<int> perm(k);
+        for (int f = 0; f < freqs; ++f)
+            for (int cc = 0; cc < ch; ++cc) perm[static_cast<size_t>(f) * ch + cc] = cc * freqs + f;
+        return upload_weights(p->ctx, precision, n, k, panel_values, scales, e.mat, perm.data());
     }
     return upload_weights(p->ctx, precision, n, k, panel_values, scales, e.mat);
 }

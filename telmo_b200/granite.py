@@ -62,15 +62,17 @@ class Granite:
     @staticmethod
     def from_entries(ctx, config: dict, entries: dict) -> "Granite":
         """Builds the model from named pack entries: matrices as (values, scales, n, k) in the
-        panel layout, vectors as f32 arrays (Granite::from_pack, src/granite.rs:424-500)."""
+        panel layout (Int8), or (values, scales, n, k, "q8_0") for Q8_0 panels; vectors as f32
+        arrays (Granite::from_pack, src/granite.rs:424-500)."""
         g = Granite(ctx, config)
         L = _lib.load()
         for name, entry in entries.items():
             if isinstance(entry, tuple):
-                values, scales, n, k = entry
+                values, scales, n, k = entry[:4]
+                precision = _lib.precision_code(entry[4] if len(entry) > 4 else "int8")
                 values = np.ascontiguousarray(values, dtype=np.int8)
                 scales = np.ascontiguousarray(scales, dtype=np.float32)
-                rc = L.telmo_granite_set_matrix(g._h, name.encode(), 3, n, k, values.ctypes.data,
+                rc = L.telmo_granite_set_matrix(g._h, name.encode(), precision, n, k, values.ctypes.data,
                                                 scales.ctypes.data)
             else:
                 data = np.ascontiguousarray(entry, dtype=np.float32).reshape(-1)

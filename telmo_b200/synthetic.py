@@ -63,6 +63,40 @@ def int8_matrix(g: np.random.Generator, n: int, k: int, scales: str = "spec"):
     return values, s, n, k
 
 
+def q8_0_panels(w: np.ndarray):
+    """quant::encode for Precision::Q8_0 (src/quant.rs:202-269, quantize_q8_0_block :172-183) of
+    a row-major f32 [n, k] matrix, k a multiple of 32: per block of 32 inputs d = amax / 127,
+    q = round(x * (1 / d)) half away from zero, the scale kept as its f16 value. Returns (values
+    int8 panels, scales f32 in panel, block, output order)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    blocks = k // 32
+    b = w.reshape(n, blocks, 32)
+    d = (np.abs(b).max(axis=2) / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+    x = (b * inv[..., None]).astype(np.float32)
+    q = np.sign(x) * np.floor(np.abs(x).astype(np.float64) + 0.5)
+    q = np.clip(q, -128, 127).astype(np.int8).reshape(n, k)
+    panels = (n + 15) // 16
+    qp = np.zeros((panels * 16, k), np.int8)
+    qp[:n] = q
+    sp = np.zeros((panels * 16, blocks), np.float32)
+    sp[:n] = d.astype(np.float16).astype(np.float32)
+    values = qp.reshape(panels, 16, k).transpose(0, 2, 1).reshape(-1)
+    scales = sp.reshape(panels, 16, blocks).transpose(0, 2, 1).reshape(-1)
+    return np.ascontiguousarray(values), np.ascontiguousarray(scales)
+
+
+def as_q8_0(entry):
+    """An Int8 matrix entry (values, scales, n, k) re-quantized to Q8_0 from its f32 values:
+    (values, scales, n, k, "q8_0")."""
+    values, s, n, k = entry
+    w = rows_from_panels(values, n, k).astype(np.float32) * np.asarray(s, np.float32)[:n, None]
+    v, sc = q8_0_panels(w)
+    return v, sc, n, k, "q8_0"
+
+
 def config1(seed: int = 0, m: int = 1500, k: int = 1024, n: int = 4096):
     """Config 1: (a [m, k] f32, (values, scales, n, k) int8 panels, bias [n] f32)."""
     g = rng(seed)
@@ -83,9 +117,11 @@ def granite_config(**overrides) -> dict:
     return c
 
 
-def granite_entries(config: dict, seed: int = 1, scales: str = "spec") -> dict:
+def granite_entries(config: dict, seed: int = 1, scales: str = "spec", precision: str = "int8") -> dict:
     """Random-init weights of a Granite-shaped model, named as the reference's pack entries
-    (src/granite.rs:224-371): matrices as (values, scales, n, k), vectors as f32 arrays.
+    (src/granite.rs:224-371): matrices as (values, scales, n, k), vectors as f32 arrays. With
+    precision="q8_0" the matrices whose inputs come in whole blocks of 32 are re-quantized to
+    Q8_0, except the relative-position tables, which stay Int8.
 
     With scales="spec" (the benchmark's distribution) the model is chaotic: its attention and
     self-conditioning softmaxes are nearly one-hot, and a 1e-6 relative change of the input
@@ -126,6 +162,11 @@ def granite_entries(config: dict, seed: int = 1, scales: str = "spec") -> dict:
         norm(f"{o}.norm_out")
     lin("head", c["vocab"], d)
     lin("mid", d, c["vocab"])
+    if precision == "q8_0":
+        e = {name: as_q8_0(v) if isinstance(v, tuple) and v[3] % 32 == 0 and not name.endswith(".rel")
+             else v for name, v in e.items()}
+    elif precision != "int8":
+        raise ValueError(f"unknown precision {precision}")
     return e
 
 
@@ -140,9 +181,11 @@ def parakeet_config(**overrides) -> dict:
     return c
 
 
-def parakeet_entries(config: dict, seed: int = 3, scales: str = "spec") -> dict:
+def parakeet_entries(config: dict, seed: int = 3, scales: str = "spec", precision: str = "int8") -> dict:
     """Random-init weights of a Parakeet-TDT-shaped model, named as the reference's pack entries
-    (src/parakeet.rs:341-486): matrices as (values, scales, n, k), vectors as f32 arrays. The
+    (src/parakeet.rs:341-486): matrices as (values, scales, n, k), vectors as f32 arrays; with
+    precision="q8_0" every matrix is then re-quantized to Q8_0, the reference's recommended
+    Parakeet precision (src/model.rs:94-102), as (values, scales, n, k, "q8_0"). The
     subsampling convolutions draw N(0, 1/9) (weights [9, channels], tap first), layer norms
     gamma 1 + N(0, 0.02) and beta N(0, 0.02), biases N(0, 0.02), depthwise weights
     N(0, 1/kernel), bias_u and bias_v N(0, 0.02), the embedding N(0, 1)."""
@@ -194,6 +237,10 @@ def parakeet_entries(config: dict, seed: int = 3, scales: str = "spec") -> dict:
     e["dec.enc_proj.b"] = f32(h, 0.02)
     e["dec.joint"] = int8m(outputs, h)
     e["dec.joint.b"] = f32(outputs, 0.02)
+    if precision == "q8_0":
+        e = {name: as_q8_0(v) if isinstance(v, tuple) else v for name, v in e.items()}
+    elif precision != "int8":
+        raise ValueError(f"unknown precision {precision}")
     return e
 
 

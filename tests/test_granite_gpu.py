@@ -95,6 +95,35 @@ def test_incomplete_or_wrong_entries_are_errors(ctx):
     g.close()
 
 
+def test_q8_0_linears_match_the_oracle(ctx, oracle_lib):
+    # Every linear whose inputs come in whole blocks of 32 as Q8_0 (the relative tables stay
+    # Int8): each block within the north star's bar of the reference's f32 path.
+    import torch
+    from telmo_b200.granite import Granite
+    config = dict(TINY, n_mels=16)
+    entries = synthetic.granite_entries(config, seed=15, scales="conditioned", precision="q8_0")
+    assert sum(isinstance(v, tuple) and len(v) == 5 for v in entries.values()) > 10
+    gpu, ref = Granite.from_entries(ctx, config, entries), oracle_lib.Granite(config, entries)
+    feats = _features(61, 64, 16)
+    for tap in (0, 3):
+        out, frames = gpu.encode(torch.from_numpy(feats).cuda(), [61], tap_layer=tap)
+        gpu.ctx.check()
+        want = ref.encode(feats, tap_layer=tap)
+        assert rel_l2(out.cpu().numpy(), want) <= 2e-2
+
+
+def test_q8_0_relative_tables_are_refused(ctx):
+    from telmo_b200 import TelmoError
+    from telmo_b200._lib import TELMO_ERR_UNSUPPORTED
+    from telmo_b200.granite import Granite
+    entries = synthetic.granite_entries(TINY, seed=3)
+    v, s, n, k = entries["blocks.1.rel"]
+    entries["blocks.1.rel"] = synthetic.as_q8_0((v, s, n, k))
+    with pytest.raises(TelmoError) as e:
+        Granite.from_entries(ctx, TINY, entries)
+    assert e.value.status == TELMO_ERR_UNSUPPORTED
+
+
 def test_ctc_tokens_match_the_oracle(ctx, oracle_lib):
     import torch
     from telmo_b200.granite import ctc_tokens

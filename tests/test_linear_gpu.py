@@ -140,6 +140,95 @@ def test_bf16_output(ctx, oracle_lib):
     assert np.array_equal(c.float().cpu().numpy(), want)
 
 
+# ---- Q8_0 weights (src/quant.rs:8-13): one scale per 32 inputs of each output ---------------------
+
+Q8_SHAPES = [(1, 32, 1), (5, 64, 17), (7, 96, 31), (129, 320, 257), (200, 1024, 384),
+             (300, 2048, 130), (64, 4096, 96)]
+
+
+def _q8_case(m, k, n, seed):
+    # Rows and blocks of very different magnitudes, so the blocks' scales matter.
+    g = synthetic.rng(seed)
+    a = g.standard_normal((m, k), dtype=np.float32)
+    w = g.standard_normal((n, k)) * np.exp(g.standard_normal((n, 1)))
+    w = (w * np.repeat(np.exp(g.standard_normal((n, k // 32))), 32, axis=1) / np.sqrt(k)).astype(np.float32)
+    values, scales = synthetic.q8_0_panels(w)
+    bias = (g.standard_normal(n) * 0.02).astype(np.float32)
+    c0 = g.standard_normal((m, n), dtype=np.float32)
+    return a, values, scales, bias, c0
+
+
+def _upload_q8(ctx, values, scales, n, k):
+    from telmo_b200 import PackedWeights, Precision
+    return PackedWeights(n, k, Precision.Q8_0, values, scales).upload(ctx)
+
+
+@pytest.mark.parametrize("m,k,n", Q8_SHAPES)
+@pytest.mark.parametrize("act,accumulate,with_bias,scale", [
+    (0, False, False, 1.0), (1, False, True, 0.5), (2, True, True, 0.5), (0, True, False, 0.5)])
+def test_q8_0_linear_matches_the_oracle(ctx, oracle_lib, m, k, n, act, accumulate, with_bias, scale):
+    # Bit-exact against the restated GPU arithmetic (two-level weights, split activations), and
+    # within the north star's 1e-3 max-relative of the reference's exact Q8_0 product.
+    from telmo_b200 import Act, Epilogue, Kernels
+    a, values, scales, bias, c0 = _q8_case(m, k, n, 5)
+    w = _upload_q8(ctx, values, scales, n, k)
+    b = bias if with_bias else None
+    c = _dev(c0)
+    Kernels(ctx).linear(_dev(a), m, w, c, Epilogue(bias=None if b is None else _dev(b),
+                                                   act=Act(act), scale=scale,
+                                                   accumulate=accumulate))
+    ctx.check()
+    got = c.cpu().numpy()
+    exact = oracle_lib.linear_x2_q8_0(a, values, scales, n, k, b, act, scale, c0, accumulate)
+    if act == 2:
+        assert np.allclose(got, exact, rtol=1e-5, atol=1e-6)
+    else:
+        assert np.array_equal(got.view(np.uint32), exact.view(np.uint32))
+    ref = oracle_lib.linear_q8_0(a, values, scales, n, k, b, act, scale, c0, accumulate)
+    assert max_rel(got, ref) <= 1e-3
+
+
+def test_q8_0_config1_shape(ctx, oracle_lib):
+    """Config 1's shape with Q8_0 weights: the reference's product within 2e-4 max-relative and
+    the i32 sums (hi . W_hi, lo . W_hi + hi . W_lo) bit-exact on sampled rows."""
+    import torch
+    from telmo_b200 import DType, Epilogue, Kernels
+    a, (v8, s8, n, k), bias = synthetic.config1()
+    m = a.shape[0]
+    w = synthetic.rows_from_panels(v8, n, k).astype(np.float32) * s8[:n, None]
+    values, scales = synthetic.q8_0_panels(w)
+    dw = _upload_q8(ctx, values, scales, n, k)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    kern = Kernels(ctx)
+    kern.linear(_dev(a), m, dw, c, Epilogue(bias=_dev(bias)))
+    sums = torch.zeros((2, m, n), dtype=torch.int32, device="cuda")
+    kern.matmul(_dev(a), k, m, dw, sums, n, out_dtype=DType.I32_PAIR)
+    ctx.check()
+    ref = oracle_lib.linear_q8_0(a, values, scales, n, k, bias, threads=8)
+    assert max_rel(c.cpu().numpy(), ref) <= 2e-4
+    rows = np.array([0, 1, 127, 128, 777, 1499])
+    hi, lo, _ = oracle_lib.quantize_x2(a[rows])
+    w_hi, w_lo, _ = oracle_lib.q8_0_two_level(values, scales, n, k)
+    want_hi, want_lo = oracle_lib.gemm_i8_x2w_acc(hi, lo, w_hi, w_lo, n, k)
+    got_sums = sums.cpu().numpy()
+    assert np.array_equal(got_sums[0][rows], want_hi)
+    assert np.array_equal(got_sums[1][rows], want_lo)
+
+
+def test_q8_0_inputs_must_be_whole_blocks(ctx):
+    import ctypes
+    from telmo_b200 import _lib
+    values = np.zeros(16 * 48, np.int8)
+    scales = np.zeros(16 * 2, np.float32)
+    h = ctypes.c_void_p()
+    rc = _lib.load().telmo_weights_upload(ctx.handle, _lib.precision_code("q8_0"), 16, 48,
+                                          values.ctypes.data, scales.ctypes.data, ctypes.byref(h))
+    assert rc == _lib.TELMO_ERR_ARGUMENT
+    rc = _lib.load().telmo_weights_upload(ctx.handle, _lib.precision_code("f16"), 16, 48,
+                                          values.ctypes.data, scales.ctypes.data, ctypes.byref(h))
+    assert rc == _lib.TELMO_ERR_UNSUPPORTED
+
+
 def test_bad_arguments_are_errors_not_crashes(ctx):
     import torch
     from telmo_b200 import Epilogue, Kernels, TelmoError

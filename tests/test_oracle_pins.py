@@ -155,6 +155,48 @@ def test_host_encode_matches_the_oracle(oracle_lib):
     assert np.array_equal(p.values, v) and np.array_equal(p.scales, s)
 
 
+def test_q8_0_rows_round_trip_within_the_reference_tolerance(oracle_lib):
+    # src/quant.rs:400-420: Q8_0 rounds with the exact scale and stores it as f16, so a value
+    # comes back within 0.6 of a step of its row's amax / 127.
+    n, k = 37, 96
+    i = np.arange(n * k)
+    w = ((((i * 7919) % 1000) / 500.0 - 1.0) * (1.0 + (i // k))).astype(np.float32).reshape(n, k)
+    values, scales = oracle_lib.encode_q8_0(w)
+    back = oracle_lib.decode_q8_0(values, scales, n, k)
+    amax = np.abs(w).max(axis=1, keepdims=True)
+    assert np.all(np.abs(back - w) <= amax / 127.0 * 0.6)
+
+
+def test_q8_0_blocks_are_laid_out_unchanged(oracle_lib):
+    # src/quant.rs:424-455: blocks laid out as the pack stores them decode to q * d exactly.
+    n, k = 20, 64
+    q = (np.arange(n * k) % 255).astype(np.uint8).view(np.int8).reshape(n, k)
+    L = oracle_lib.lib()
+    d = np.array([L.oracle_f16_to_f32(L.oracle_f32_to_f16(0.01 * (i + 1)))
+                  for i in range(n * k // 32)], np.float32).reshape(n, k // 32)
+    panels = (n + 15) // 16
+    qp = np.zeros((panels * 16, k), np.int8)
+    qp[:n] = q
+    dp = np.zeros((panels * 16, k // 32), np.float32)
+    dp[:n] = d
+    values = qp.reshape(panels, 16, k).transpose(0, 2, 1).reshape(-1)
+    scales = dp.reshape(panels, 16, k // 32).transpose(0, 2, 1).reshape(-1)
+    back = oracle_lib.decode_q8_0(values, scales, n, k)
+    assert np.array_equal(back, q.astype(np.float32) * np.repeat(d, 32, axis=1))
+
+
+def test_q8_0_encoders_agree(oracle_lib):
+    from telmo_b200 import PackedWeights, Precision, synthetic
+    g = np.random.default_rng(8)
+    w = (g.standard_normal((45, 160)) * np.exp(g.standard_normal((45, 1)))).astype(np.float32)
+    w[4, 32:64] = 0.0
+    v, s = oracle_lib.encode_q8_0(w)
+    p = PackedWeights.encode(w, 45, 160, Precision.Q8_0)
+    assert np.array_equal(p.values, v) and np.array_equal(p.scales, s)
+    v2, s2 = synthetic.q8_0_panels(w)
+    assert np.array_equal(v2, v) and np.array_equal(s2, s)
+
+
 # ---- the matrix product (src/kernels/mod.rs:885-1128) -------------------------------------------
 
 def _reference_f64(a, w, bias, act, scale, c0, accumulate):
@@ -184,6 +226,23 @@ def test_matmul_matches_the_f64_reference(oracle_lib, m, k, n):
                                        (0, True, False)]:
         b = bias if with_bias else None
         got = oracle_lib.linear_int8(a, values, scales, n, k, b, act, 0.5, c0, accumulate)
+        want = _reference_f64(a, wide, b, act, 0.5, c0, accumulate)
+        assert np.all(np.abs(got - want) <= 1e-5 * math.sqrt(k) * (1 + np.abs(want)))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 32, 1), (5, 64, 17), (13, 96, 50), (64, 320, 96)])
+def test_q8_0_matmul_matches_the_f64_reference(oracle_lib, m, k, n):
+    # The widening is exact (src/kernels/mod.rs:1160-1183), so the Q8_0 product is the f32
+    # product of the decoded weights.
+    a = xorshift(m * k, 11).reshape(m, k)
+    w = xorshift(n * k, 12).reshape(n, k)
+    bias = xorshift(n, 13)
+    c0 = xorshift(m * n, 14).reshape(m, n)
+    values, scales = oracle_lib.encode_q8_0(w)
+    wide = oracle_lib.decode_q8_0(values, scales, n, k)
+    for act, accumulate, with_bias in [(0, False, False), (1, False, True), (2, True, True)]:
+        b = bias if with_bias else None
+        got = oracle_lib.linear_q8_0(a, values, scales, n, k, b, act, 0.5, c0, accumulate)
         want = _reference_f64(a, wide, b, act, 0.5, c0, accumulate)
         assert np.all(np.abs(got - want) <= 1e-5 * math.sqrt(k) * (1 + np.abs(want)))
 

@@ -261,3 +261,61 @@ def test_decoder_choice_is_checked(tiny):
     gpu, _ = tiny
     with pytest.raises(TelmoError):
         gpu.set_decoder(2)
+
+
+# ---- Q8_0 weights, the reference's recommended Parakeet precision (src/model.rs:94-102) --------
+
+@pytest.fixture(scope="module")
+def tiny_q8(ctx, oracle_lib):
+    from telmo_b200.parakeet import Parakeet
+    entries = synthetic.parakeet_entries(TINY, seed=21, scales="conditioned", precision="q8_0")
+    return Parakeet.from_entries(ctx, TINY, entries), oracle_lib.Parakeet(TINY, entries)
+
+
+@pytest.mark.parametrize("tap", [-2, 0, -1])
+def test_q8_0_tiny_encoder_matches(tiny_q8, tap):
+    import torch
+    gpu, ref = tiny_q8
+    feats = _features(203, 12)
+    out, frames = gpu.encode(torch.from_numpy(feats).cuda(), [203], tap_layer=tap)
+    gpu.ctx.check()
+    want = ref.encode(feats, tap_layer=tap)
+    err = rel_l2(out.cpu().numpy(), want)
+    assert err <= layer_bar(None if tap == -2 else (tap if tap >= 0 else 1)), err
+
+
+def test_q8_0_tiny_transcribe_matches_and_uses_the_phase_decoder(tiny_q8, oracle_lib):
+    # Two-level weights do not fit the persistent decoder's shared memory plan: the per-phase
+    # decoder runs them.
+    gpu, ref = tiny_q8
+    utts = [synthetic.audio(s, seed=80 + i) for i, s in enumerate([1.3, 2.7])]
+    got = gpu.transcribe(utts)
+    gpu.ctx.check()
+    assert gpu.last_decoder() == 0
+    compared = 0
+    for u, g in zip(utts, got):
+        want, margin = ref.decode(ref.encode(oracle_lib.parakeet_features(u)))
+        assert _tokens_match([(t.id, t.frame, t.duration) for t in g], want, margin)
+        compared += margin > 1e-2
+    assert compared >= 1
+
+
+def test_q8_0_full_size_layers_and_tokens_match(ctx, oracle_lib):
+    import torch
+    from telmo_b200.parakeet import Parakeet
+    config = synthetic.parakeet_config()
+    entries = synthetic.parakeet_entries(config, seed=4, scales="conditioned", precision="q8_0")
+    gpu, ref = Parakeet.from_entries(ctx, config, entries), oracle_lib.Parakeet(config, entries)
+    feats = _features(520, 91)
+    for tap in (-2, 0, 23):
+        out, frames = gpu.encode(torch.from_numpy(feats).cuda(), [520], tap_layer=tap)
+        gpu.ctx.check()
+        want = ref.encode(feats, tap_layer=tap, threads=8)
+        err = rel_l2(out.cpu().numpy(), want)
+        assert err <= 2e-2, (tap, err)
+        assert err <= layer_bar(None if tap == -2 else tap), (tap, err)
+    utts = [synthetic.audio(3.1, seed=64)]
+    got = gpu.transcribe(utts)
+    gpu.ctx.check()
+    want, margin = ref.decode(ref.encode(oracle_lib.parakeet_features(utts[0]), threads=8), threads=8)
+    assert len(want) > 0 and _tokens_match([(t.id, t.frame, t.duration) for t in got[0]], want, margin)
