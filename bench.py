@@ -117,10 +117,11 @@ class GraniteWorkload:
     unit = "audio-s/s"
     POOL = 64  # distinct 30 s base waveforms; utterance u is a slice of waveform u % 64
 
-    def __init__(self, rank, world, n_utt=4096, batch_seconds=2048.0):
+    def __init__(self, rank, world, n_utt=4096, batch_seconds=2048.0, precision="int8"):
         from telmo_b200 import sharding, synthetic
         self.synthetic = synthetic
         self.n_utt = n_utt
+        self.precision = precision
         secs = synthetic.lengths_log_uniform(n_utt, 1.0, 30.0, seed=0)
         self.samples = np.maximum((secs * SR).astype(np.int64), 2 * 160)
         self.total_seconds = float(self.samples.sum()) / SR
@@ -130,6 +131,9 @@ class GraniteWorkload:
         self.mine = [u for b in self.batches for u in b]
         self.rank_seconds = float(self.samples[self.mine].sum()) / SR
         self.batch_seconds = batch_seconds
+
+    def _entries(self, cfg):
+        return self.synthetic.granite_entries(cfg, seed=1, scales="spec", precision=self.precision)
 
     def utterance(self, u, pool):
         n = int(self.samples[u])
@@ -146,6 +150,9 @@ class GraniteWorkload:
                 "lengths": "log-uniform 1-30 s (seed 0)",
                 "model": "Granite-shaped: d 1024, 16 blocks, 8 heads x 128, ff 4096, conv 2048 x k15, "
                          "context 128, vocab 2049, int8 weights (scales U(1e-3,1e-2))",
+                "weights": self.precision if self.precision == "int8" else
+                "q8_0 (Int8 weights re-quantized per 32 inputs; the relative tables and the "
+                "2049-input mid projection stay Int8)",
                 "global_batch": self.n_utt, "sharding": f"utterances over {world} GPU(s), "
                                                         "longest-first greedy, no collective",
                 "per_rank_batches": len(self.batches), "batch_seconds_max": self.batch_seconds,
@@ -158,7 +165,7 @@ class GraniteWorkload:
         import torch
         from telmo_b200.granite import Granite
         cfg = self.synthetic.granite_config()
-        entries = self.synthetic.granite_entries(cfg, seed=1, scales="spec")
+        entries = self._entries(cfg)
         self.model = Granite.from_entries(ctx, cfg, entries)
         del entries
         pool = self.make_pool()
@@ -269,7 +276,7 @@ class GraniteWorkload:
     def cpu_setup(self):
         from oracle import oracle
         cfg = self.synthetic.granite_config()
-        entries = self.synthetic.granite_entries(cfg, seed=1, scales="spec")
+        entries = self._entries(cfg)
         self.oracle = oracle
         self.ref = oracle.Granite(cfg, entries)
         del entries
@@ -304,10 +311,11 @@ class ParakeetWorkload(GraniteWorkload):
     PROFILE = "telmo_parakeet_profile"
 
     # The whole set (about 4,240 s) fits one batch: every matrix product runs over all frames.
-    def __init__(self, rank, world, n_utt=256, batch_seconds=4500.0):
+    def __init__(self, rank, world, n_utt=256, batch_seconds=4500.0, precision="int8"):
         from telmo_b200 import sharding, synthetic
         self.synthetic = synthetic
         self.n_utt = n_utt
+        self.precision = precision
         secs = synthetic.lengths_uniform(n_utt, 1.0, 30.0, seed=0)
         self.samples = np.maximum((secs * SR).astype(np.int64), 2 * 160)
         self.total_seconds = float(self.samples.sum()) / SR
@@ -325,12 +333,15 @@ class ParakeetWorkload(GraniteWorkload):
                            "24 layers, 8 heads x 128, ff 4096, conv k9, Transformer-XL positions; "
                            "2-layer LSTM 640, joint 640 -> 8193 + 5 durations, max 10 symbols "
                            "per frame; int8 weights (scales U(1e-3,1e-2))",
+                  "weights": self.precision if self.precision == "int8" else
+                  "q8_0 (the Int8 weights re-quantized per 32 inputs; the reference's "
+                  "recommended Parakeet precision)",
                   "l2": "inputs larger than L2 (127 MB of audio, ~10 GB of activations per "
                         "batch)"})
         return c
 
-    def _entries(self):
-        return self.synthetic.parakeet_entries(self.cfg, seed=3, scales="spec")
+    def _entries(self, cfg=None):
+        return self.synthetic.parakeet_entries(self.cfg, seed=3, scales="spec", precision=self.precision)
 
     def setup_gpu(self, ctx):
         import torch
@@ -389,7 +400,7 @@ class LinearWorkload:
     metric = "int8 linear TOPS (config 1: A f32 [1500,1024] x W int8 [4096,1024] + bias, f32 out)"
     unit = "TOPS"
 
-    def __init__(self, rank, world, shape=None):
+    def __init__(self, rank, world, shape=None, precision="int8"):
         from telmo_b200 import synthetic
         if shape:  # another product shape (M, K, N) with config 1's distributions
             m, k, n = shape
@@ -398,18 +409,24 @@ class LinearWorkload:
             self.metric = f"int8 linear TOPS (A f32 [{m},{k}] x W int8 [{n},{k}] + bias, f32 out)"
         else:
             self.a, (self.values, self.scales, self.n, self.k), self.bias = synthetic.config1()
+        self.precision = precision
+        if precision == "q8_0":  # the same weights re-quantized per block of 32 inputs
+            self.values, self.scales, _, _, _ = synthetic.as_q8_0((self.values, self.scales, self.n, self.k))
+            self.metric = self.metric.replace("W int8", "W Q8_0")
+            self.name += "-q8_0"
         self.m = self.a.shape[0]
         self.ops = 2.0 * self.m * self.n * self.k
 
     def config(self, world):
-        return {"workload": self.name, "m": self.m, "k": self.k, "n": self.n,
+        return {"workload": self.name, "m": self.m, "k": self.k, "n": self.n, "weights": self.precision,
                 "activations": "split int8 (2 levels), i32 accumulate", "l2": "flushed"}
 
     def setup_gpu(self, ctx):
         import torch
         from telmo_b200 import Kernels, PackedWeights, Precision
         self.kern = Kernels(ctx)
-        self.w = PackedWeights(self.n, self.k, Precision.INT8, self.values, self.scales).upload(ctx)
+        prec = Precision.Q8_0 if self.precision == "q8_0" else Precision.INT8
+        self.w = PackedWeights(self.n, self.k, prec, self.values, self.scales).upload(ctx)
         self.da = torch.from_numpy(self.a).cuda()
         self.dbias = torch.from_numpy(self.bias).cuda()
         self.dc = torch.empty((self.m, self.n), dtype=torch.float32, device="cuda")
@@ -434,10 +451,13 @@ class LinearWorkload:
     def units_per_step(self):
         return self.ops / 1e12
 
-    def cpu_step(self, threads):
+    def _oracle_linear(self):
         from oracle import oracle
-        oracle.linear_int8(self.a, self.values, self.scales, self.n, self.k, self.bias,
-                           threads=threads)
+        return oracle.linear_q8_0 if self.precision == "q8_0" else oracle.linear_int8
+
+    def cpu_step(self, threads):
+        self._oracle_linear()(self.a, self.values, self.scales, self.n, self.k, self.bias,
+                              threads=threads)
 
     def cpu_sample(self, threads):
         # At most 1500 rows of A per timing (the config-1 product), best of 5.
@@ -447,7 +467,7 @@ class LinearWorkload:
         best = float("inf")
         for _ in range(5):
             t0 = time.perf_counter()
-            oracle.linear_int8(a, self.values, self.scales, self.n, self.k, self.bias, threads=threads)
+            self._oracle_linear()(a, self.values, self.scales, self.n, self.k, self.bias, threads=threads)
             best = min(best, time.perf_counter() - t0)
         return 2.0 * rows * self.n * self.k / best / 1e12, f"{rows} rows of the product, best of 5"
 
@@ -458,12 +478,11 @@ SPEECH = ("granite", "parakeet")
 
 def make_workload(args, rank, world):
     if args.workload == "granite":
-        return GraniteWorkload(rank, world, n_utt=args.utterances or 4096)
+        return GraniteWorkload(rank, world, n_utt=args.utterances or 4096, precision=args.precision)
     if args.workload == "parakeet":
-        return ParakeetWorkload(rank, world, n_utt=args.utterances or 256)
-    if args.workload == "linear" and args.shape:
-        return LinearWorkload(rank, world, shape=tuple(int(x) for x in args.shape.split(",")))
-    return WORKLOADS[args.workload](rank, world)
+        return ParakeetWorkload(rank, world, n_utt=args.utterances or 256, precision=args.precision)
+    shape = tuple(int(x) for x in args.shape.split(",")) if args.shape else None
+    return LinearWorkload(rank, world, shape=shape, precision=args.precision)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -629,6 +648,8 @@ def main():
     ap.add_argument("--shape", default="",
                     help="linear: M,K,N of another product (config 1's distributions), e.g. "
                          "53000,1024,4096 for an encoder's feed-forward up-projection")
+    ap.add_argument("--precision", choices=["int8", "q8_0"], default="int8",
+                    help="weight precision (the reference's Precision::Int8 or Q8_0)")
     ap.add_argument("--utterances", type=int, default=0,
                     help="utterances in the set (default: 4096 for granite, config 5; 256 for "
                          "parakeet, config 4; fewer for profiling)")
