@@ -295,6 +295,23 @@ int telmo_parakeet_transcribe(telmo_parakeet *p, const float *samples, const int
 int telmo_parakeet_transcribe_device(telmo_parakeet *p, const float *samples,
                                      const int64_t *lengths, int n_utt, uint32_t *tokens,
                                      int *counts, int *frames, void *stream);
+/* The networks the reference's biased TDT beam search reads (Networks, src/parakeet.rs:1641-1676;
+ * tdt_beam::TdtNetwork, src/biasing/tdt_beam.rs:15-26), batched on the device:
+ *  - telmo_parakeet_enc_proj: the joint's projection of encoder frames (device [frames, d_model]
+ *    -> device out [frames, pred_hidden]), as decode_inner computes it once (:1438-1449);
+ *  - telmo_parakeet_joint: TdtNetwork::joint at one frame -- out row r (device, ld_out >= vocab +
+ *    n_durations floats apart) = joint(relu(enc_row + preds[r])) + b for device enc_row
+ *    [pred_hidden] (a row of telmo_parakeet_enc_proj's output) and preds [rows, pred_hidden];
+ *  - telmo_parakeet_predict: TdtNetwork::predict / predict_rows (:1524-1577) -- host tokens
+ *    [rows], each row's device state [rows][pred_layers][2][pred_hidden] (hidden, cell) updated
+ *    in place, device preds [rows, pred_hidden] written.
+ * Calls on one model run in stream order; a token outside the vocabulary is TELMO_ERR_ARGUMENT. */
+int telmo_parakeet_enc_proj(telmo_parakeet *p, const float *encoded, size_t frames, float *out,
+                            void *stream);
+int telmo_parakeet_joint(telmo_parakeet *p, const float *enc_row, const float *preds, int rows,
+                         float *out, size_t ld_out, void *stream);
+int telmo_parakeet_predict(telmo_parakeet *p, const int *tokens, int rows, float *states,
+                           float *preds, void *stream);
 /* Selects the greedy TDT decoder: 1 (the default) runs the whole loop as one persistent
  * cooperative kernel with the prediction and joint weights held in shared memory, where the
  * model fits (pred_hidden a multiple of 64, the weights within the SMs' shared memory); 0 runs

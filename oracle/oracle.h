@@ -180,6 +180,16 @@ long oracle_parakeet_encode(const oracle_parakeet *p, const float *features, siz
  * token or duration choice. Returns the token count. */
 size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, size_t frames,
                               uint32_t *tokens, float *min_margin, int threads);
+/* The networks the biased beam search reads (src/parakeet.rs:1641-1676): the joint's projection
+ * of encoder frames [frames, h]; the joint's outputs [rows, vocab + durations] for prediction
+ * rows at one projected frame; predict_rows for one token per row, states [rows][layers][2][h]
+ * updated in place, preds [rows, h]. */
+void oracle_parakeet_enc_proj(const oracle_parakeet *p, const float *encoded, size_t frames,
+                              float *out, int threads);
+void oracle_parakeet_joint(const oracle_parakeet *p, const float *enc_row, const float *preds,
+                           size_t rows, float *out);
+void oracle_parakeet_predict(const oracle_parakeet *p, const int *tokens, size_t rows, float *states,
+                             float *preds);
 /* One step of the greedy TDT loop after the joint (src/parakeet.rs:1482-1510): the first
  * argmax over logits[0, vocab) is the token, durations[first argmax over the n_durations
  * logits after them] the duration; a blank moves *t on by max(duration, 1); a token is written

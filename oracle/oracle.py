@@ -434,6 +434,9 @@ def _parakeet_lib():
     L.oracle_tdt_step.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                   ctypes.c_int, ctypes.c_int, ctypes.POINTER(_sz),
                                   ctypes.POINTER(ctypes.c_int), _u32p]
+    L.oracle_parakeet_enc_proj.argtypes = [ctypes.c_void_p, _f32p, _sz, _f32p, ctypes.c_int]
+    L.oracle_parakeet_joint.argtypes = [ctypes.c_void_p, _f32p, _f32p, _sz, _f32p]
+    L.oracle_parakeet_predict.argtypes = [ctypes.c_void_p, _i32p, _sz, _f32p, _f32p]
     L._parakeet_declared = True
     return L
 
@@ -516,3 +519,27 @@ class Parakeet:
         n = _parakeet_lib().oracle_parakeet_decode(self._h, e.reshape(-1), frames, out,
                                                    ctypes.byref(margin), threads)
         return [tuple(int(v) for v in out[3 * i:3 * i + 3]) for i in range(n)], margin.value
+
+    # The networks the biased beam search reads (src/parakeet.rs:1641-1676).
+    def enc_proj(self, encoded, threads=1):
+        e = _c(encoded, np.float32)
+        out = np.zeros((e.shape[0], self.config["pred_hidden"]), np.float32)
+        _parakeet_lib().oracle_parakeet_enc_proj(self._h, e.reshape(-1), e.shape[0], out.reshape(-1),
+                                                 threads)
+        return out
+
+    def joint(self, enc_row, preds):
+        p = _c(preds, np.float32)
+        rows = p.shape[0]
+        out = np.zeros((rows, self.config["vocab"] + len(self.config["durations"])), np.float32)
+        _parakeet_lib().oracle_parakeet_joint(self._h, _c(enc_row, np.float32).reshape(-1),
+                                              p.reshape(-1), rows, out.reshape(-1))
+        return out
+
+    def predict(self, tokens, states):
+        """predict_rows: (new states [rows, layers * 2 * h], preds [rows, h])."""
+        t = _c(tokens, np.int32).reshape(-1)
+        st = np.array(states, np.float32, copy=True)
+        preds = np.zeros((t.size, self.config["pred_hidden"]), np.float32)
+        _parakeet_lib().oracle_parakeet_predict(self._h, t, t.size, st.reshape(-1), preds.reshape(-1))
+        return st, preds

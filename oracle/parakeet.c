@@ -398,6 +398,34 @@ static void predict(const oracle_parakeet *p, size_t token, float *state, float 
     free(gates);
 }
 
+/* ---- the networks the biased beam search reads (src/parakeet.rs:1641-1676) ------------------ */
+
+void oracle_parakeet_enc_proj(const oracle_parakeet *p, const float *encoded, size_t frames,
+                              float *out, int threads)
+{
+    plinear(&p->enc_proj, encoded, frames, out, p->enc_proj_b.p, ORACLE_ACT_NONE, 1.0f, 0, threads);
+}
+
+void oracle_parakeet_joint(const oracle_parakeet *p, const float *enc_row, const float *preds,
+                           size_t rows, float *out)
+{
+    /* TdtNetwork::joint (:1653-1670): z = relu(e + p) per row, then one product over the rows. */
+    size_t h = (size_t)p->c.pred_hidden;
+    float *z = (float *)malloc((rows ? rows : 1) * h * sizeof(float));
+    for (size_t r = 0; r < rows; r++)
+        for (size_t j = 0; j < h; j++) z[r * h + j] = fmaxf(enc_row[j] + preds[r * h + j], 0.0f);
+    plinear(&p->joint, z, rows, out, p->joint_b.p, ORACLE_ACT_NONE, 1.0f, 0, 1);
+    free(z);
+}
+
+void oracle_parakeet_predict(const oracle_parakeet *p, const int *tokens, size_t rows, float *states,
+                             float *preds)
+{
+    /* TdtNetwork::predict (:1672-1675) -> predict_rows: each row's state and prediction. */
+    size_t h = (size_t)p->c.pred_hidden, sw = (size_t)p->c.pred_layers * 2 * h;
+    for (size_t r = 0; r < rows; r++) predict(p, (size_t)tokens[r], states + r * sw, preds + r * h, 1);
+}
+
 static size_t argmax_first(const float *v, size_t n)
 {
     size_t best = 0;

@@ -84,6 +84,9 @@ SIGNATURES = {
     "telmo_parakeet_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_parakeet_launches": (_c.c_long, [_vp]),
     "telmo_parakeet_set_decoder": (_c.c_int, [_vp, _c.c_int]),
+    "telmo_parakeet_enc_proj": (_c.c_int, [_vp, _vp, _c.c_size_t, _vp, _vp]),
+    "telmo_parakeet_joint": (_c.c_int, [_vp, _vp, _vp, _c.c_int, _vp, _c.c_size_t, _vp]),
+    "telmo_parakeet_predict": (_c.c_int, [_vp, _vp, _c.c_int, _vp, _vp, _vp]),
     "telmo_parakeet_last_decoder": (_c.c_int, [_vp]),
     "telmo_parakeet_decoder_profile": (_c.c_int, [_vp, _c.c_void_p, _c.c_void_p]),
     "telmo_parakeet_profile": (_int, [_vp, _int]),

@@ -137,7 +137,7 @@ struct Parakeet {
     long phase_passes = 0;
     long launches = 0;
 
-    Arena enc_arena, dec_arena, e2e_arena;
+    Arena enc_arena, dec_arena, e2e_arena, net_arena;
     cudaStream_t capture_stream = nullptr;  // records the decoding passes as a graph
     float* audio_dev = nullptr;
     size_t audio_cap = 0;
@@ -158,6 +158,9 @@ struct Parakeet {
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int decode(const float* encoded, const int* frames, int n_utt, uint32_t* tokens, int* counts, long* total,
                cudaStream_t s);
+    int enc_proj_rows(const float* encoded, int64_t frames, float* out, cudaStream_t s);
+    int joint_rows(const float* enc_row, const float* preds, int rows, float* out, int64_t ld_out, cudaStream_t s);
+    int predict_rows(const int* tokens, int rows, float* states, float* preds, cudaStream_t s);
     int transcribe_device(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
                           int* frames_out, long* total, cudaStream_t s);
 };
@@ -736,6 +739,64 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
     return TELMO_OK;
 }
 
+// ---- the networks the biased beam search reads (Networks, src/parakeet.rs:1641-1676) -----------
+
+int Parakeet::enc_proj_rows(const float* encoded, int64_t frames, float* out, cudaStream_t s) {
+    if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "parakeet: the model is not finalized");
+    if (frames <= 0 || frames > (1 << 28) || !encoded || !out)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_enc_proj: bad arguments");
+    const int d = c.d_model, h = c.pred_hidden, M = static_cast<int>(frames);
+    const int64_t ld = static_cast<int64_t>(round_up(d, 16));
+    if (int rc = net_arena.reserve(ctx, quant_bytes(M, ld))) return rc;
+    const QuantAct q = quant_piece(net_arena, M, ld);
+    if (int rc = quant(encoded, d, M, d, q, s)) return rc;
+    return gemm(q, M, enc_proj, enc_proj_b.p, out, h, kActNone, 1.0f, 0, s);
+}
+
+int Parakeet::joint_rows(const float* enc_row, const float* preds, int rows, float* out, int64_t ld_out,
+                         cudaStream_t s) {
+    if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "parakeet: the model is not finalized");
+    const int h = c.pred_hidden, outputs = c.vocab + c.n_durations;
+    if (rows <= 0 || rows > (1 << 24) || !enc_row || !preds || !out || ld_out < outputs)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_joint: bad arguments");
+    const int64_t ld = static_cast<int64_t>(round_up(h, 16));
+    if (int rc = net_arena.reserve(ctx, quant_bytes(rows, ld))) return rc;
+    const QuantAct q = quant_piece(net_arena, rows, ld);
+    ++launches;
+    if (int rc = ctx->cuda(tdt_joint_rows(enc_row, preds, rows, h, q, s), "parakeet joint")) return rc;
+    return gemm(q, rows, joint, joint_b.p, out, ld_out, kActNone, 1.0f, 0, s);
+}
+
+int Parakeet::predict_rows(const int* tokens, int rows, float* states, float* preds, cudaStream_t s) {
+    if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "parakeet: the model is not finalized");
+    const int h = c.pred_hidden, L = c.pred_layers;
+    if (rows <= 0 || rows > (1 << 24) || !tokens || !states || !preds)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_predict: bad arguments");
+    for (int r = 0; r < rows; ++r)
+        if (tokens[r] < 0 || tokens[r] >= c.vocab)
+            return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_predict: token %d of row %d is not in the vocabulary",
+                              tokens[r], r);
+    const int64_t ld = static_cast<int64_t>(round_up(2 * h, 16));
+    if (int rc = net_arena.reserve(ctx, quant_bytes(rows, ld) + piece<float>(static_cast<size_t>(rows) * 4 * h) +
+                                            piece<int>(rows)))
+        return rc;
+    const QuantAct q = quant_piece(net_arena, rows, ld);
+    float* gates = net_arena.take<float>(static_cast<size_t>(rows) * 4 * h);
+    int* tok = net_arena.take<int>(rows);
+    if (int rc = ctx->cuda(cudaMemcpyAsync(tok, tokens, sizeof(int) * rows, cudaMemcpyHostToDevice, s), "predict"))
+        return rc;
+    // Parakeet::predict_rows (src/parakeet.rs:1524-1577): layer l's input [x | h_l] quantized,
+    // the gate product, the cell update (which quantizes the next layer's input), pred_proj.
+    ++launches;
+    if (int rc = ctx->cuda(tdt_predict_input(tok, rows, h, L, embedding.p, states, q, s), "predict")) return rc;
+    for (int l = 0; l < L; ++l) {
+        if (int rc = gemm(q, rows, lstm[l], lstm_b[l].p, gates, 4 * h, kActNone, 1.0f, 0, s)) return rc;
+        ++launches;
+        if (int rc = ctx->cuda(lstm_cell_prep(tok, rows, h, l, L, gates, states, q, s), "predict")) return rc;
+    }
+    return gemm(q, rows, pred_proj, pred_proj_b.p, preds, h, kActNone, 1.0f, 0, s);
+}
+
 int Parakeet::transcribe_device(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
                                 int* frames_out, long* total, cudaStream_t s) {
     // Parakeet::transcribe (src/parakeet.rs:842-867) without biasing or detokenising.
@@ -925,6 +986,30 @@ extern "C" int telmo_parakeet_transcribe(telmo_parakeet* pp, const float* sample
     if (int rc = ctx->cuda(cudaMemcpyAsync(counts, cnt_dev, sizeof(int) * n_utt, cudaMemcpyDeviceToHost, s), "transcribe"))
         return rc;
     return ctx->cuda(cudaStreamSynchronize(s), "transcribe");
+}
+
+extern "C" int telmo_parakeet_enc_proj(telmo_parakeet* pp, const float* encoded, size_t frames, float* out,
+                                       void* stream) {
+    Parakeet* p = as_parakeet(pp);
+    if (!p) return TELMO_ERR_ARGUMENT;
+    if (int rc = p->ctx->use_device()) return rc;
+    return p->enc_proj_rows(encoded, static_cast<int64_t>(frames), out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_parakeet_joint(telmo_parakeet* pp, const float* enc_row, const float* preds, int rows,
+                                    float* out, size_t ld_out, void* stream) {
+    Parakeet* p = as_parakeet(pp);
+    if (!p) return TELMO_ERR_ARGUMENT;
+    if (int rc = p->ctx->use_device()) return rc;
+    return p->joint_rows(enc_row, preds, rows, out, static_cast<int64_t>(ld_out), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_parakeet_predict(telmo_parakeet* pp, const int* tokens, int rows, float* states, float* preds,
+                                      void* stream) {
+    Parakeet* p = as_parakeet(pp);
+    if (!p) return TELMO_ERR_ARGUMENT;
+    if (int rc = p->ctx->use_device()) return rc;
+    return p->predict_rows(tokens, rows, states, preds, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int telmo_parakeet_set_decoder(telmo_parakeet* pp, int persistent) {

@@ -527,6 +527,42 @@ __global__ void __launch_bounds__(128) lstm_cell_prep_kernel(const int* __restri
                      q.lo + static_cast<int64_t>(u) * q.ld, q.scale + u, red);
 }
 
+// ---- the networks the biased beam search reads (src/parakeet.rs:1641-1676) --------------------
+
+// q row r = relu(enc_row + preds[r]), one CTA per prediction row (TdtNetwork::joint, :1653-1670).
+__global__ void __launch_bounds__(128) tdt_joint_rows_kernel(const float* __restrict__ enc_row,
+                                                             const float* __restrict__ preds, int rows, int h,
+                                                             QuantAct q) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const float* p = preds + static_cast<int64_t>(r) * h;
+    for (int j = threadIdx.x; j < h; j += 128) row[j] = fmaxf(__fadd_rn(enc_row[j], p[j]), 0.0f);
+    __syncthreads();
+    quantize_row_cta(row, h, q.ld, q.hi + static_cast<int64_t>(r) * q.ld, q.lo + static_cast<int64_t>(r) * q.ld,
+                     q.scale + r, red);
+}
+
+// q row r = [emb(tokens[r]) | h_0 of state row r], the first LSTM layer's input (predict_rows).
+__global__ void __launch_bounds__(128) tdt_predict_input_kernel(const int* __restrict__ tokens, int rows, int h,
+                                                                int layers, const float* __restrict__ embedding,
+                                                                const float* __restrict__ states, QuantAct q) {
+    extern __shared__ float row[];
+    __shared__ float red[4];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const float* e = embedding + static_cast<int64_t>(tokens[r]) * h;
+    const float* h0 = states + static_cast<int64_t>(r) * layers * 2 * h;
+    for (int j = threadIdx.x; j < h; j += 128) {
+        row[j] = e[j];
+        row[h + j] = h0[j];
+    }
+    __syncthreads();
+    quantize_row_cta(row, 2 * h, q.ld, q.hi + static_cast<int64_t>(r) * q.ld, q.lo + static_cast<int64_t>(r) * q.ld,
+                     q.scale + r, red);
+}
+
 // Moves each utterance's tokens from its worst-case slot (3 * tok_first words in) to the prefix
 // sum of the counts before it; counts[u] gets its count and *total the sum. One CTA: thread 0
 // forms the prefix sums in `offsets`, then every warp copies whole utterances.
@@ -644,6 +680,20 @@ cudaError_t lstm_cell_prep(const int* predict_token, int n_utt, int h, int layer
     if (n_utt <= 0) return cudaSuccess;
     lstm_cell_prep_kernel<<<n_utt, 128, sizeof(float) * 2 * h, s>>>(predict_token, n_utt, h, layer, layers, gates,
                                                                      state, q);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_joint_rows(const float* enc_row, const float* preds, int rows, int h, const QuantAct& q,
+                           cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    tdt_joint_rows_kernel<<<rows, 128, sizeof(float) * h, s>>>(enc_row, preds, rows, h, q);
+    return cudaGetLastError();
+}
+
+cudaError_t tdt_predict_input(const int* tokens, int rows, int h, int layers, const float* embedding,
+                              const float* states, const QuantAct& q, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    tdt_predict_input_kernel<<<rows, 128, sizeof(float) * 2 * h, s>>>(tokens, rows, h, layers, embedding, states, q);
     return cudaGetLastError();
 }
 

@@ -153,6 +153,12 @@ bool tdt_persistent_plan(TdtPersistentArgs& a, int sms, size_t* smem_bytes);
 // Runs the whole greedy decode; the error code lands in words[0], the passes in words[1].
 cudaError_t tdt_persistent(const TdtPersistentArgs& a, int grid, size_t smem_bytes, cudaStream_t s);
 
+// The networks the biased beam search reads: q row r = relu(enc_row + preds[r]) (the joint's
+// operand), and q row r = [emb(tokens[r]) | h_0 of state row r] (the first LSTM layer's).
+cudaError_t tdt_joint_rows(const float* enc_row, const float* preds, int rows, int h, const QuantAct& q,
+                           cudaStream_t s);
+cudaError_t tdt_predict_input(const int* tokens, int rows, int h, int layers, const float* embedding,
+                              const float* states, const QuantAct& q, cudaStream_t s);
 // Tokens from each utterance's worst-case slot (3 * tok_first words into raw) to consecutive
 // places in out (prefix sums of the counts, kept in offsets [n_utt]); counts[u] and *total.
 cudaError_t tdt_compact(const uint32_t* raw, const TdtState* st, int n_utt, int* offsets, uint32_t* out, int* counts,

@@ -168,6 +168,35 @@ class Parakeet:
             counts.data_ptr(), frames.ctypes.data, _stream(stream)), self.ctx.handle)
         return frames
 
+    # -- the networks the reference's biased beam search reads (src/parakeet.rs:1641-1676) --------
+    def enc_proj(self, encoded, stream=None):
+        """The joint's projection of encoder frames: CUDA [frames, d_model] -> [frames, h]."""
+        import torch
+        out = torch.empty((encoded.shape[0], self.config["pred_hidden"]), dtype=torch.float32,
+                          device=encoded.device)
+        check(_lib.load().telmo_parakeet_enc_proj(self._h, encoded.data_ptr(), encoded.shape[0],
+                                                  out.data_ptr(), _stream(stream)), self.ctx.handle)
+        return out
+
+    def joint(self, enc_row, preds, stream=None):
+        """TdtNetwork::joint: [rows, vocab + durations] for CUDA preds [rows, h] at one projected
+        frame enc_row [h]."""
+        import torch
+        rows = preds.shape[0]
+        outputs = self.config["vocab"] + len(self.config["durations"])
+        out = torch.empty((rows, outputs), dtype=torch.float32, device=preds.device)
+        check(_lib.load().telmo_parakeet_joint(self._h, enc_row.data_ptr(), preds.data_ptr(), rows,
+                                               out.data_ptr(), outputs, _stream(stream)),
+              self.ctx.handle)
+        return out
+
+    def predict(self, tokens, states, preds, stream=None):
+        """TdtNetwork::predict: host tokens [rows]; CUDA states [rows, layers * 2 * h] updated in
+        place and preds [rows, h] written."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(_lib.load().telmo_parakeet_predict(self._h, t.ctypes.data, t.size, states.data_ptr(),
+                                                 preds.data_ptr(), _stream(stream)), self.ctx.handle)
+
     def set_decoder(self, persistent: bool):
         """1/True: the persistent decoder kernel (the default); 0/False: per-phase launches."""
         check(_lib.load().telmo_parakeet_set_decoder(self._h, int(persistent)), self.ctx.handle)

@@ -319,3 +319,48 @@ def test_q8_0_full_size_layers_and_tokens_match(ctx, oracle_lib):
     gpu.ctx.check()
     want, margin = ref.decode(ref.encode(oracle_lib.parakeet_features(utts[0]), threads=8), threads=8)
     assert len(want) > 0 and _tokens_match([(t.id, t.frame, t.duration) for t in got[0]], want, margin)
+
+
+# ---- the networks the biased beam search reads (src/parakeet.rs:1641-1676) ---------------------
+
+@pytest.mark.parametrize("which", ["tiny", "full"])
+def test_beam_search_networks_match_the_oracle(request, which):
+    # enc_proj, joint at one frame for many hypotheses, and predict_rows over caller-held
+    # states, against the oracle's restatement of the reference's Networks; each within the
+    # north star's 1e-3 max-relative per product.
+    import torch
+    gpu, ref = request.getfixturevalue(which)
+    c = gpu.config
+    h, L = c["pred_hidden"], c["pred_layers"]
+    g = synthetic.rng(33)
+    enc = g.standard_normal((37, c["d_model"])).astype(np.float32)
+    ep = gpu.enc_proj(torch.from_numpy(enc).cuda())
+    gpu.ctx.check()
+    want_ep = ref.enc_proj(enc)
+    assert np.max(np.abs(ep.cpu().numpy() - want_ep)) <= 1e-3 * np.max(np.abs(want_ep))
+    rows = 29
+    preds = g.standard_normal((rows, h)).astype(np.float32)
+    out = gpu.joint(ep[5], torch.from_numpy(preds).cuda())
+    gpu.ctx.check()
+    want = ref.joint(want_ep[5], preds)
+    assert np.max(np.abs(out.cpu().numpy() - want)) <= 1e-3 * np.max(np.abs(want))
+    tokens = g.integers(0, c["vocab"], rows)
+    states = (g.standard_normal((rows, L * 2 * h)) * 0.5).astype(np.float32)
+    st = torch.from_numpy(states).cuda()
+    pr = torch.empty((rows, h), dtype=torch.float32, device="cuda")
+    gpu.predict(tokens, st, pr)
+    gpu.ctx.check()
+    want_st, want_pr = ref.predict(tokens, states)
+    assert np.max(np.abs(st.cpu().numpy() - want_st)) <= 1e-3 * np.max(np.abs(want_st))
+    assert np.max(np.abs(pr.cpu().numpy() - want_pr)) <= 1e-3 * np.max(np.abs(want_pr))
+
+
+def test_predict_rejects_tokens_outside_the_vocabulary(tiny):
+    import torch
+    from telmo_b200 import TelmoError
+    gpu, _ = tiny
+    h, L = gpu.config["pred_hidden"], gpu.config["pred_layers"]
+    st = torch.zeros((2, L * 2 * h), device="cuda")
+    pr = torch.zeros((2, h), device="cuda")
+    with pytest.raises(TelmoError):
+        gpu.predict([0, gpu.config["vocab"]], st, pr)
