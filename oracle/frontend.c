@@ -123,16 +123,14 @@ size_t oracle_granite_rows_for(size_t samples)
     return (samples / HOP + 1) / 2; /* (samples / HOP).div_ceil(2) */
 }
 
-int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float *out)
+void oracle_granite_log_frames(const float *samples, size_t n, size_t len, size_t f0, size_t f1,
+                               size_t n_mels, float *logs)
 {
-    /* GraniteFrontEnd::compute (src/granite_features.rs:161-186). */
-    if (n < 2 * HOP) return -1;
-    size_t rows = oracle_granite_rows_for(n), frames = 2 * rows;
-    size_t len = (frames - 1) * HOP + 1;
-    if (len < n) len = n;
-    /* periodic Hann 400 centered in 512 (src/granite_features.rs:47-52, :209-217). */
+    /* log_frame (src/granite_features.rs:95-133) for frames f0..f1 into logs[(f - f0) * n_mels]:
+     * the n samples zero-padded to len, reflected at both ends. */
     double window[N_FFT];
     memset(window, 0, sizeof window);
+    /* periodic Hann 400 centered in 512 (src/granite_features.rs:47-52, :209-217). */
     float step = (float)(2.0 * M_PI / (double)WIN);
     for (size_t i = 0; i < WIN; i++) {
         float x = (float)i * step;
@@ -140,11 +138,8 @@ int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float
     }
     mel_filter *filters = (mel_filter *)malloc(n_mels * sizeof(mel_filter));
     htk_mel_filters(n_mels, filters);
-    float *logs = (float *)malloc(frames * n_mels * sizeof(float));
     double seg[N_FFT], spec[2 * BINS], power[BINS];
-    for (size_t f = 0; f < frames; f++) {
-        /* log_frame (src/granite_features.rs:95-133): reflect at both ends of the zero-padded
-         * signal of length len. */
+    for (size_t f = f0; f < f1; f++) {
         long start = (long)(f * HOP) - N_FFT / 2;
         for (long i = 0; i < N_FFT; i++) {
             long j = start + i;
@@ -160,15 +155,19 @@ int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float
             for (size_t k = 0; k < filters[m].count; k++)
                 acc += (double)filters[m].w[k] * power[filters[m].first_bin + k];
             float energy = fmaxf((float)acc, 1e-10f);
-            logs[f * n_mels + m] = (float)log10((double)energy);
+            logs[(f - f0) * n_mels + m] = (float)log10((double)energy);
         }
     }
-    float peak = -INFINITY;
-    for (size_t i = 0; i < frames * n_mels; i++) peak = fmaxf(peak, logs[i]);
-    /* stack_rows (src/granite_features.rs:138-158). */
+    free(filters);
+}
+
+void oracle_granite_stack_rows(const float *logs, size_t frames, size_t n_mels, float peak,
+                               size_t first, size_t last, float *out)
+{
+    /* stack_rows (src/granite_features.rs:138-158): rows first..last into out[(row - first)]. */
     float floor_v = peak - 8.0f;
-    for (size_t f = 0; f < frames; f++) {
-        float *row = out + f * 2 * n_mels;
+    for (size_t f = 2 * first; f < 2 * last; f++) {
+        float *row = out + (f - 2 * first) * 2 * n_mels;
         size_t before = f ? f - 1 : 0, after = f + 1 < frames ? f + 1 : frames - 1;
         for (size_t m = 0; m < n_mels; m++) {
             float v = fmaxf(logs[f * n_mels + m], floor_v) / 4.0f + 1.0f;
@@ -178,8 +177,21 @@ int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float
             row[n_mels + m] = (va - vb) / 2.0f;
         }
     }
+}
+
+int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float *out)
+{
+    /* GraniteFrontEnd::compute (src/granite_features.rs:161-186). */
+    if (n < 2 * HOP) return -1;
+    size_t rows = oracle_granite_rows_for(n), frames = 2 * rows;
+    size_t len = (frames - 1) * HOP + 1;
+    if (len < n) len = n;
+    float *logs = (float *)malloc(frames * n_mels * sizeof(float));
+    oracle_granite_log_frames(samples, n, len, 0, frames, n_mels, logs);
+    float peak = -INFINITY;
+    for (size_t i = 0; i < frames * n_mels; i++) peak = fmaxf(peak, logs[i]);
+    oracle_granite_stack_rows(logs, frames, n_mels, peak, 0, rows, out);
     free(logs);
-    free(filters);
     return 0;
 }
 

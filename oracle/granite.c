@@ -310,14 +310,6 @@ static void glu_row(void *p, size_t r)
     oracle_glu(C->big + r * 2 * C->cc, C->big + r * 2 * C->cc + C->cc, C->glu + r * C->cc, C->cc);
 }
 
-static void dwconv_row(void *p, size_t r)
-{
-    const conv_ctx *C = (const conv_ctx *)p;
-    oracle_dwconv1d_frame(C->glu, C->cc, C->m, C->stride * r, C->w, C->kernel, C->bias,
-                          C->dst + r * C->cc);
-    oracle_silu(C->dst + r * C->cc, C->cc);
-}
-
 static void softmax_row(void *p, size_t r)
 {
     const conv_ctx *C = (const conv_ctx *)p;
@@ -381,36 +373,69 @@ static void attention_task(void *ctx, size_t task)
     free(pos);
 }
 
-/* Granite::block_span over a whole utterance (start 0, no left context, src/granite.rs:802-952).
- * x holds t input frames and ends up holding the post-attention states; out gets the outputs. */
-static void block_span(const oracle_granite *g, const block *b, float *x, size_t t, float *out,
-                       scratch *s, int threads)
+/* Granite::block_span (src/granite.rs:795-952): one block over input frames start..end, whose
+ * input x ([end - start, d]) ends up holding their post-attention states, writing outputs from
+ * out_start on (end / 2 of them in all for a strided block, end otherwise) to out. left holds the
+ * post-attention states of frames lo..start, lo = conv_context(b, out_start), which the
+ * convolution reads at the left edge. start begins an attention block. */
+static size_t conv_context(const oracle_granite *g, const block *b, size_t out_start)
+{
+    /* Granite::conv_context (src/granite.rs:955-960). */
+    size_t half = (size_t)g->c.conv_kernel / 2;
+    size_t first = b->strided ? 2 * out_start : out_start;
+    return first > half ? first - half : 0;
+}
+
+typedef struct {
+    const float *glu;
+    float *dst;
+    size_t cc, m, stride, kernel, out_start, lo;
+    const float *w, *bias;
+} span_conv;
+
+static void span_dwconv_row(void *p, size_t r)
+{
+    const span_conv *C = (const span_conv *)p;
+    oracle_dwconv1d_frame(C->glu, C->cc, C->m, C->stride * (C->out_start + r) - C->lo, C->w, C->kernel,
+                          C->bias, C->dst + r * C->cc);
+    oracle_silu(C->dst + r * C->cc, C->cc);
+}
+
+static void block_span(const oracle_granite *g, const block *b, float *x, size_t start, size_t end,
+                       const float *left, size_t out_start, float *out, scratch *s, int threads)
 {
     const oracle_granite_config *c = &g->c;
-    size_t d = (size_t)c->d_model, cc = (size_t)c->conv_channels;
+    size_t d = (size_t)c->d_model, cc = (size_t)c->conv_channels, t = end - start;
     feed_forward(g, &b->ff1, x, t, s, threads);
     layer_norm_rows(&b->norm_att, x, s->h, t, d);
     mat_linear(s->h, d, t, &b->qkv, s->big, 3 * d, NULL, ORACLE_ACT_NONE, 1.0f, 0, threads);
     att_job J = {g, b, s->big, t, (t + (size_t)c->context - 1) / (size_t)c->context, s->att};
     oracle_parallel_for((size_t)c->heads * J.blocks, threads, attention_task, &J);
     linear(s->att, t, &b->out, x, ORACLE_ACT_NONE, 1.0f, 1, threads);
-    /* The convolution module (src/granite.rs:853-944), lo = 0 and m = t. */
-    size_t m = t, stride = b->strided ? 2 : 1, n = b->strided ? t / 2 : t;
-    layer_norm_rows(&b->norm_conv, x, s->h, m, d);
+    /* The convolution module (src/granite.rs:853-944) over the post-attention states of lo..end:
+     * left's rows, then x's. */
+    size_t lo = conv_context(g, b, out_start), m = end - lo;
+    size_t stride = b->strided ? 2 : 1, out_end = b->strided ? end / 2 : end, n = out_end - out_start;
+#define STATE(f) ((f) < start ? left + ((f) - lo) * d : x + ((f) - start) * d)
+    float *states = (float *)malloc((m ? m : 1) * d * sizeof(float));
+    for (size_t f = lo; f < end; f++) memcpy(states + (f - lo) * d, STATE(f), d * sizeof(float));
+    layer_norm_rows(&b->norm_conv, states, s->h, m, d);
     linear(s->h, m, &b->pw1, s->big, ORACLE_ACT_NONE, 1.0f, 0, threads);
-    conv_ctx C = {s->big, s->glu, s->big, cc, m, stride, (size_t)c->conv_kernel, b->dw_w.p,
-                  b->dw_b.p, 0};
-    for_rows(m, 16, threads, glu_row, &C);
-    /* Every output row reads only glu, and rows below n of big are free after the GLU. */
-    for_rows(n, 8, threads, dwconv_row, &C);
+    conv_ctx G = {s->big, s->glu, NULL, cc, m, 1, 0, NULL, NULL, 0};
+    for_rows(m, 16, threads, glu_row, &G);
+    span_conv C = {s->glu, s->big, cc, m, stride, (size_t)c->conv_kernel, out_start, lo, b->dw_w.p, b->dw_b.p};
+    for_rows(n, 8, threads, span_dwconv_row, &C);
     for (size_t r = 0; r < n; r++) {
         float *row = out + r * d;
+        size_t f = stride * (out_start + r);
         if (b->strided) {
-            const float *p = x + 2 * r * d, *q = x + (2 * r + 1) * d;
+            const float *p = STATE(f), *q = STATE(f + 1);
             for (size_t i = 0; i < d; i++) row[i] = (p[i] + q[i]) / 2.0f;
         } else
-            memcpy(row, x + r * d, d * sizeof(float));
+            memcpy(row, STATE(f), d * sizeof(float));
     }
+#undef STATE
+    free(states);
     linear(s->big, n, &b->pw2, out, ORACLE_ACT_NONE, 1.0f, 1, threads);
     feed_forward(g, &b->ff2, out, n, s, threads);
     layer_norm_rows(&b->norm_out, out, s->h, n, d);
@@ -455,7 +480,7 @@ long oracle_granite_encode(const oracle_granite *g, const float *features, size_
     for (int i = 0; i < c->layers; i++) {
         const block *b = &g->blocks[i];
         size_t out_t = b->strided ? t / 2 : t;
-        block_span(g, b, x, t, y, &s, threads);
+        block_span(g, b, x, 0, t, NULL, 0, y, &s, threads);
         float *tmp = x;
         x = y;
         y = tmp;
@@ -501,4 +526,214 @@ void oracle_granite_frame_ids(const oracle_granite *g, const float *encoded, siz
         if (margin) margin[f] = row[best] - second;
     }
     free(logits);
+}
+
+/* ---- GraniteStream (src/granite_stream.rs) ----------------------------------------------------- */
+
+typedef struct {
+    float *states; /* post-attention states at the layer's input rate, [frames, d] */
+    size_t states_rows;
+    float *out; /* outputs at its output rate, the self-conditioning injection added */
+    size_t out_rows;
+} layer_cache;
+
+struct oracle_granite_stream {
+    const oracle_granite *g;
+    float *samples;
+    size_t n, cap;
+    float *logs; /* log10 mel energies of every frame computed, before the floor */
+    size_t log_frames;
+    float peak, floor_peak;
+    int finished;
+    size_t rows;
+    float *features, *input;
+    layer_cache *layers;
+    size_t frozen, lag;
+    uint32_t *ids;
+    size_t n_ids, first_changed;
+};
+
+static void *grow(void *p, size_t bytes) { return realloc(p, bytes ? bytes : 1); }
+
+oracle_granite_stream *oracle_granite_stream_new(const oracle_granite *g)
+{
+    oracle_granite_stream *st = (oracle_granite_stream *)calloc(1, sizeof *st);
+    st->g = g;
+    st->peak = -INFINITY;
+    st->floor_peak = -INFINITY;
+    st->lag = 16; /* DEFAULT_FREEZE_LAG (src/granite_stream.rs:23) */
+    st->layers = (layer_cache *)calloc((size_t)g->c.layers, sizeof(layer_cache));
+    return st;
+}
+
+void oracle_granite_stream_free(oracle_granite_stream *st)
+{
+    if (!st) return;
+    for (int i = 0; i < st->g->c.layers; i++) {
+        free(st->layers[i].states);
+        free(st->layers[i].out);
+    }
+    free(st->layers);
+    free(st->samples);
+    free(st->logs);
+    free(st->features);
+    free(st->input);
+    free(st->ids);
+    free(st);
+}
+
+void oracle_granite_stream_set_freeze_lag(oracle_granite_stream *st, size_t frames) { st->lag = frames; }
+
+int oracle_granite_stream_push(oracle_granite_stream *st, const float *samples, size_t n)
+{
+    if (st->finished) return -1;
+    if (st->n + n > st->cap) {
+        st->cap = (st->n + n) * 2;
+        st->samples = (float *)grow(st->samples, st->cap * sizeof(float));
+    }
+    memcpy(st->samples + st->n, samples, n * sizeof(float));
+    st->n += n;
+    return 0;
+}
+
+/* GraniteStream::update (src/granite_stream.rs:209-361). */
+int oracle_granite_stream_update(oracle_granite_stream *st, int finished, int threads)
+{
+    const oracle_granite *g = st->g;
+    const oracle_granite_config *c = &g->c;
+    if (st->finished) return -1;
+    g_threads = threads < 1 ? 1 : threads;
+    size_t d = (size_t)c->d_model, ctx = (size_t)c->context, n_mels = (size_t)c->n_mels;
+    size_t half = (size_t)c->conv_kernel / 2, width = 4 * n_mels, n = st->n;
+    st->first_changed = st->n_ids;
+    size_t frames, len;
+    if (!finished) {
+        frames = n <= 256 ? 0 : (n - 256) / 160 + 1; /* complete_frames (src/granite_features.rs:84-92) */
+        len = n;
+    } else if (n >= 2 * 160) {
+        frames = 2 * oracle_granite_rows_for(n);
+        len = (frames - 1) * 160 + 1;
+        if (len < n) len = n;
+    } else {
+        frames = st->log_frames;
+        len = n;
+    }
+    st->finished = finished;
+    if (frames > st->log_frames) {
+        st->logs = (float *)grow(st->logs, frames * n_mels * sizeof(float));
+        oracle_granite_log_frames(st->samples, n, len, st->log_frames, frames, n_mels,
+                                  st->logs + st->log_frames * n_mels);
+        for (size_t i = st->log_frames * n_mels; i < frames * n_mels; i++) st->peak = fmaxf(st->peak, st->logs[i]);
+        st->log_frames = frames;
+    }
+    /* A row needs the frame after it for its last delta, until the end repeats the last frame. */
+    size_t rows = finished ? frames / 2 : (frames ? (frames - 1) / 2 : 0);
+    if (rows <= st->rows) return 0;
+
+    size_t first_row = st->rows / ctx * ctx;
+    if (st->peak > st->floor_peak) {
+        size_t row = st->frozen;
+        for (int k = 0; k < c->n_subsample; k++) row = (2 * row > half ? 2 * row - half : 0) / ctx * ctx;
+        if (row < first_row) first_row = row;
+        st->floor_peak = st->peak;
+    }
+    st->features = (float *)grow(st->features, rows * width * sizeof(float));
+    oracle_granite_stack_rows(st->logs, st->log_frames, n_mels, st->peak, first_row, rows,
+                              st->features + first_row * width);
+    st->input = (float *)grow(st->input, rows * d * sizeof(float));
+    linear(st->features + first_row * width, rows - first_row, &g->input, st->input + first_row * d,
+           ORACLE_ACT_NONE, 1.0f, 0, threads);
+    st->rows = rows;
+
+    size_t widest = (size_t)c->ff;
+    if (3 * d > widest) widest = 3 * d;
+    if (2 * (size_t)c->conv_channels > widest) widest = 2 * (size_t)c->conv_channels;
+    scratch s;
+    s.h = (float *)malloc(rows * d * sizeof(float));
+    s.big = (float *)malloc(rows * widest * sizeof(float));
+    s.att = (float *)malloc(rows * d * sizeof(float));
+    s.glu = (float *)malloc(rows * (size_t)c->conv_channels * sizeof(float));
+    size_t changed = first_row, frames_in = rows;
+    int sc_layer = c->layers / 2 - 1, done = 1;
+    for (int i = 0; i < c->layers; i++) {
+        const block *b = &g->blocks[i];
+        layer_cache *L = &st->layers[i];
+        size_t start, out_start, frames_out;
+        if (b->strided) {
+            start = changed / ctx * ctx;
+            /* Outputs before start / 2 whose convolution reaches the changed block. */
+            out_start = ((start > half ? start - half : 0) + 1) / 2;
+            frames_out = frames_in / 2;
+        } else {
+            start = out_start = st->frozen;
+            frames_out = frames_in;
+        }
+        if (start >= frames_in || out_start >= frames_out) { /* too little audio for an output */
+            done = 0;
+            break;
+        }
+        size_t lo = conv_context(g, b, out_start);
+        const float *input = i == 0 ? st->input : st->layers[i - 1].out;
+        float *x = (float *)malloc((frames_in - start) * d * sizeof(float));
+        memcpy(x, input + start * d, (frames_in - start) * d * sizeof(float));
+        float *out = (float *)calloc((frames_out - out_start) * d, sizeof(float));
+        block_span(g, b, x, start, frames_in, L->states + lo * d, out_start, out, &s, threads);
+        if (i == sc_layer) {
+            size_t rows_out = frames_out - out_start;
+            float *inj = (float *)malloc(rows_out * d * sizeof(float));
+            self_conditioning(g, out, rows_out, inj, threads);
+            for (size_t e = 0; e < rows_out * d; e++) out[e] += inj[e];
+            free(inj);
+        }
+        L->states = (float *)grow(L->states, frames_in * d * sizeof(float));
+        memcpy(L->states + start * d, x, (frames_in - start) * d * sizeof(float));
+        L->states_rows = frames_in;
+        L->out = (float *)grow(L->out, frames_out * d * sizeof(float));
+        memcpy(L->out + out_start * d, out, (frames_out - out_start) * d * sizeof(float));
+        L->out_rows = frames_out;
+        free(x);
+        free(out);
+        changed = out_start;
+        frames_in = frames_out;
+    }
+    free(s.h);
+    free(s.big);
+    free(s.att);
+    free(s.glu);
+    if (!done) return 0;
+
+    size_t first = changed;
+    st->ids = (uint32_t *)grow(st->ids, frames_in * sizeof(uint32_t));
+    oracle_granite_frame_ids(g, st->layers[c->layers - 1].out + first * d, frames_in - first, st->ids + first,
+                             NULL, threads);
+    st->n_ids = frames_in;
+    st->first_changed = first;
+    if (frames_in > st->lag) {
+        size_t fz = (frames_in - 1 - st->lag) / ctx * ctx;
+        if (fz > st->frozen) st->frozen = fz;
+    }
+    return 0;
+}
+
+size_t oracle_granite_stream_frames(const oracle_granite_stream *st) { return st->n_ids; }
+size_t oracle_granite_stream_first_changed(const oracle_granite_stream *st) { return st->first_changed; }
+size_t oracle_granite_stream_frozen(const oracle_granite_stream *st) { return st->frozen; }
+size_t oracle_granite_stream_rows(const oracle_granite_stream *st) { return st->rows; }
+
+void oracle_granite_stream_frame_ids(const oracle_granite_stream *st, uint32_t *out)
+{
+    memcpy(out, st->ids, st->n_ids * sizeof(uint32_t));
+}
+
+size_t oracle_granite_stream_layer_output(const oracle_granite_stream *st, int layer, float *out)
+{
+    const layer_cache *L = &st->layers[layer];
+    if (out) memcpy(out, L->out, L->out_rows * (size_t)st->g->c.d_model * sizeof(float));
+    return L->out_rows;
+}
+
+size_t oracle_granite_stream_features(const oracle_granite_stream *st, float *out)
+{
+    if (out) memcpy(out, st->features, st->rows * 4 * (size_t)st->g->c.n_mels * sizeof(float));
+    return st->rows;
 }

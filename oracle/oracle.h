@@ -112,6 +112,13 @@ size_t oracle_granite_rows_for(size_t samples);
 /* GraniteFrontEnd::compute (src/granite_features.rs:161-186): out [rows, 4 * n_mels].
  * Returns 0, or -1 when the audio is too short (fewer than 320 samples). */
 int oracle_granite_features(const float *samples, size_t n, size_t n_mels, float *out);
+/* The pieces of it a stream runs: log_frame (src/granite_features.rs:95-133) for frames f0..f1
+ * of n samples zero-padded to len (logs[(f - f0) * n_mels]), and stack_rows (:138-158) of rows
+ * first..last of frames logs with the given peak (out[(row - first) * 4 * n_mels]). */
+void oracle_granite_log_frames(const float *samples, size_t n, size_t len, size_t f0, size_t f1,
+                               size_t n_mels, float *logs);
+void oracle_granite_stack_rows(const float *logs, size_t frames, size_t n_mels, float peak,
+                               size_t first, size_t last, float *out);
 /* FrontEnd::compute (src/features.rs:101-216) with FrontEndConfig::parakeet: out [n/160, 128].
  * Returns 0, or -1 when the audio is too short. */
 int oracle_parakeet_features(const float *samples, size_t n, float *out);
@@ -153,6 +160,23 @@ void oracle_granite_logits(const oracle_granite *g, const float *encoded, size_t
 
 /* ---- parakeet.rs ----------------------------------------------------------------------------- */
 typedef struct oracle_parakeet oracle_parakeet;
+/* GraniteStream (src/granite_stream.rs): one utterance transcribed while it is spoken. push
+ * appends 16 kHz samples; update encodes what is new (finished: the audio is complete). The
+ * model's strided blocks must come first. */
+typedef struct oracle_granite_stream oracle_granite_stream;
+oracle_granite_stream *oracle_granite_stream_new(const oracle_granite *g);
+void oracle_granite_stream_free(oracle_granite_stream *st);
+void oracle_granite_stream_set_freeze_lag(oracle_granite_stream *st, size_t frames);
+int oracle_granite_stream_push(oracle_granite_stream *st, const float *samples, size_t n);
+int oracle_granite_stream_update(oracle_granite_stream *st, int finished, int threads);
+size_t oracle_granite_stream_frames(const oracle_granite_stream *st);
+size_t oracle_granite_stream_first_changed(const oracle_granite_stream *st);
+size_t oracle_granite_stream_frozen(const oracle_granite_stream *st);
+size_t oracle_granite_stream_rows(const oracle_granite_stream *st);
+void oracle_granite_stream_frame_ids(const oracle_granite_stream *st, uint32_t *out);
+size_t oracle_granite_stream_layer_output(const oracle_granite_stream *st, int layer, float *out);
+size_t oracle_granite_stream_features(const oracle_granite_stream *st, float *out);
+
 typedef struct {
     int d_model, heads, layers, ff, conv_kernel, sub_channels, n_mels, pred_hidden, pred_layers,
         vocab, blank, n_durations, durations[8], max_symbols;

@@ -399,6 +399,86 @@ def ctc_tokens(ids, blank=0):
 
 # ---- the Parakeet TDT model ---------------------------------------------------------------------
 
+def _declare_stream(L):
+    if getattr(L, "_stream_declared", False):
+        return L
+    vp = ctypes.c_void_p
+    L.oracle_granite_stream_new.restype = vp
+    L.oracle_granite_stream_new.argtypes = [vp]
+    L.oracle_granite_stream_free.argtypes = [vp]
+    L.oracle_granite_stream_set_freeze_lag.argtypes = [vp, _sz]
+    L.oracle_granite_stream_push.restype = ctypes.c_int
+    L.oracle_granite_stream_push.argtypes = [vp, _f32p, _sz]
+    L.oracle_granite_stream_update.restype = ctypes.c_int
+    L.oracle_granite_stream_update.argtypes = [vp, ctypes.c_int, ctypes.c_int]
+    for name in ("frames", "first_changed", "frozen", "rows"):
+        f = getattr(L, f"oracle_granite_stream_{name}")
+        f.restype = _sz
+        f.argtypes = [vp]
+    L.oracle_granite_stream_frame_ids.argtypes = [vp, _u32p]
+    L.oracle_granite_stream_layer_output.restype = _sz
+    L.oracle_granite_stream_layer_output.argtypes = [vp, ctypes.c_int, vp]
+    L.oracle_granite_stream_features.restype = _sz
+    L.oracle_granite_stream_features.argtypes = [vp, vp]
+    L._stream_declared = True
+    return L
+
+
+class GraniteStream:
+    """GraniteStream (src/granite_stream.rs) over an oracle Granite model: push 16 kHz samples,
+    update (finished or not), read frame ids, the first changed frame, the frozen frame, and
+    each block's outputs so far."""
+
+    def __init__(self, model: "Granite"):
+        self.model = model
+        self.L = _declare_stream(lib())
+        self._h = self.L.oracle_granite_stream_new(model._h)
+        self.d = model.config["d_model"]
+
+    def __del__(self):
+        try:
+            if self._h:
+                self.L.oracle_granite_stream_free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+    def set_freeze_lag(self, frames):
+        self.L.oracle_granite_stream_set_freeze_lag(self._h, frames)
+
+    def push(self, samples):
+        x = _c(samples, np.float32).reshape(-1)
+        if self.L.oracle_granite_stream_push(self._h, x, x.size) != 0:
+            raise ValueError("audio pushed after the stream finished")
+
+    def update(self, finished=False, threads=1):
+        if self.L.oracle_granite_stream_update(self._h, int(finished), threads) != 0:
+            raise ValueError("the stream already finished")
+
+    def frame_ids(self):
+        out = np.zeros(self.L.oracle_granite_stream_frames(self._h), np.uint32)
+        self.L.oracle_granite_stream_frame_ids(self._h, out)
+        return out
+
+    def first_changed(self):
+        return self.L.oracle_granite_stream_first_changed(self._h)
+
+    def frozen(self):
+        return self.L.oracle_granite_stream_frozen(self._h)
+
+    def layer_output(self, layer):
+        rows = self.L.oracle_granite_stream_layer_output(self._h, layer, None)
+        out = np.zeros((rows, self.d), np.float32)
+        self.L.oracle_granite_stream_layer_output(self._h, layer, out.ctypes.data)
+        return out
+
+    def features(self):
+        rows = self.L.oracle_granite_stream_features(self._h, None)
+        out = np.zeros((rows, 4 * self.model.config["n_mels"]), np.float32)
+        self.L.oracle_granite_stream_features(self._h, out.ctypes.data)
+        return out
+
+
 class ParakeetConfig(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int) for name in (
         "d_model", "heads", "layers", "ff", "conv_kernel", "sub_channels", "n_mels",

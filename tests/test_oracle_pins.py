@@ -484,3 +484,56 @@ def test_tiny_parakeet_is_deterministic_and_decodes_in_order(oracle_lib):
     assert all(i != c["blank"] and i < c["vocab"] for i, _, _ in tokens)
     assert all(d in c["durations"] for _, _, d in tokens)
     assert np.isfinite(margin)
+
+
+# ---- GraniteStream (src/granite_stream.rs) ----------------------------------------------------------
+
+STREAM = dict(d_model=128, heads=2, head_dim=64, layers=4, ff=256, conv_channels=256, conv_kernel=5,
+              context=16, max_relative=32, vocab=33, n_mels=80)
+
+
+def _stream_model(oracle_lib, seed=7):
+    from telmo_b200 import synthetic
+    config = synthetic.granite_config(**STREAM)
+    return config, oracle_lib.Granite(config, synthetic.granite_entries(config, seed=seed,
+                                                                        scales="conditioned"))
+
+
+def test_one_finished_update_is_the_offline_encode(oracle_lib):
+    # The module's promise (src/granite_stream.rs:14-17): a single update over a whole
+    # utterance gives exactly what Granite::encode and frame_ids give.
+    from telmo_b200 import synthetic
+    config, model = _stream_model(oracle_lib)
+    audio = synthetic.audio(3.3, seed=5)
+    st = oracle_lib.GraniteStream(model)
+    st.push(audio)
+    st.update(finished=True)
+    feats = oracle_lib.granite_features(audio)
+    assert np.array_equal(st.features(), feats)
+    enc = model.encode(feats)
+    assert np.array_equal(st.layer_output(config["layers"] - 1), enc)
+    ids, _ = model.frame_ids(enc)
+    assert np.array_equal(st.frame_ids(), ids) and st.first_changed() == 0
+
+
+def test_stream_updates_freeze_and_extend(oracle_lib):
+    # Pieces of 0.37 s: frames only grow, every update reports the first frame it may have
+    # changed, and frames before the frozen block keep their ids from then on.
+    from telmo_b200 import synthetic
+    config, model = _stream_model(oracle_lib)
+    audio = synthetic.audio(4.1, seed=6)
+    st = oracle_lib.GraniteStream(model)
+    st.set_freeze_lag(2)
+    piece, at, before, frozen_ids = 5920, 0, 0, {}
+    while at < audio.size:
+        st.push(audio[at:at + piece])
+        at += piece
+        st.update(finished=at >= audio.size)
+        ids = st.frame_ids()
+        assert ids.size >= before and st.first_changed() <= before
+        for f, v in frozen_ids.items():
+            assert ids[f] == v
+        for f in range(min(st.frozen(), ids.size)):
+            frozen_ids.setdefault(f, ids[f])
+        before = ids.size
+    assert before == model.frames_for(oracle_lib.granite_rows_for(audio.size)) and len(frozen_ids) > 0
