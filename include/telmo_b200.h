@@ -226,6 +226,37 @@ int telmo_granite_profile(telmo_granite *g, int enable);
 int telmo_granite_profile_read(telmo_granite *g, double *ms, long *launches, double *gemm_ops,
                                double *gemm_bytes);
 
+/* ---- streaming (GraniteStream, src/granite_stream.rs) ----------------------------------------- */
+
+/* One utterance transcribed while it is spoken: push appends 16 kHz samples (host), update
+ * encodes what the new audio can change -- the strided blocks over their attention blocks with
+ * new or changed frames, the others from the first frame of their current attention block (the
+ * frozen frame; earlier outputs stay as they were once the next block has freeze_lag frames) --
+ * and refreshes the frame ids from the first frame it may have changed. With finished the audio
+ * is complete and its end is padded as the offline front end pads it; a single finished update
+ * over a whole utterance gives exactly what telmo_granite_encode and telmo_granite_frame_ids
+ * give. The model's strided blocks must come first and it must read 80 mels. A stream uses its
+ * model's work buffers: one stream or batch call of a model at a time. */
+typedef struct telmo_granite_stream telmo_granite_stream;
+int telmo_granite_stream_create(telmo_granite *g, telmo_granite_stream **out);
+void telmo_granite_stream_free(telmo_granite_stream *st);
+/* Encoder frames (80 ms) the next block must have before the one before it freezes (16). */
+int telmo_granite_stream_set_freeze_lag(telmo_granite_stream *st, int frames);
+int telmo_granite_stream_push(telmo_granite_stream *st, const float *samples, size_t n);
+int telmo_granite_stream_update(telmo_granite_stream *st, int finished, void *stream);
+/* Encoder frames so far, the first frame the last update may have changed, the frozen frame. */
+size_t telmo_granite_stream_frames(const telmo_granite_stream *st);
+size_t telmo_granite_stream_first_changed(const telmo_granite_stream *st);
+size_t telmo_granite_stream_frozen(const telmo_granite_stream *st);
+/* The frame ids so far (host, up to cap), the CTC blank included. */
+int telmo_granite_stream_frame_ids(const telmo_granite_stream *st, uint32_t *ids, size_t cap);
+/* Block `layer`'s outputs so far ([rows, d_model], host, up to cap_rows) and the feature rows so
+ * far ([rows, 320], host), for comparing with an offline pass. */
+int telmo_granite_stream_layer_output(const telmo_granite_stream *st, int layer, float *out,
+                                      size_t cap_rows, size_t *rows);
+int telmo_granite_stream_features(const telmo_granite_stream *st, float *out, size_t cap_rows,
+                                  size_t *rows);
+
 /* ctc_tokens (src/granite.rs:1074-1094) on the device for n_utt utterances: utterance u's ids
  * are ids[first[u] .. first[u] + frames[u]) (first, frames: device int arrays); its tokens go to
  * tokens + 3 * first[u] as (id, frame, duration) triples and their number to counts[u]. */

@@ -69,6 +69,17 @@ SIGNATURES = {
     "telmo_granite_transcribe": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_granite_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_granite_launches": (_c.c_long, [_vp]),
+    "telmo_granite_stream_create": (_c.c_int, [_vp, _vp]),
+    "telmo_granite_stream_free": (None, [_vp]),
+    "telmo_granite_stream_set_freeze_lag": (_c.c_int, [_vp, _c.c_int]),
+    "telmo_granite_stream_push": (_c.c_int, [_vp, _vp, _sz]),
+    "telmo_granite_stream_update": (_c.c_int, [_vp, _c.c_int, _vp]),
+    "telmo_granite_stream_frames": (_sz, [_vp]),
+    "telmo_granite_stream_first_changed": (_sz, [_vp]),
+    "telmo_granite_stream_frozen": (_sz, [_vp]),
+    "telmo_granite_stream_frame_ids": (_c.c_int, [_vp, _vp, _sz]),
+    "telmo_granite_stream_layer_output": (_c.c_int, [_vp, _c.c_int, _vp, _sz, _vp]),
+    "telmo_granite_stream_features": (_c.c_int, [_vp, _vp, _sz, _vp]),
     "telmo_granite_profile": (_int, [_vp, _int]),
     "telmo_granite_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "telmo_parakeet_create": (_int, [_vp, _vp, _c.POINTER(_vp)]),

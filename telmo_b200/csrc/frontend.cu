@@ -514,6 +514,70 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
     return ctx->cuda(cudaStreamSynchronize(s), "front end");
 }
 
+// ---- the Granite front end over part of one utterance (GraniteStream) ------------------------
+
+namespace {
+struct StreamMetaHost {
+    int64_t sample_first, sample_count, padded_len;
+    int frame_first, frame_count, row_first;
+};
+}  // namespace
+
+int FrontEnd::stream_meta(const void* host_meta, void* meta_dev, FrontMeta& meta, const int*& row_first,
+                          cudaStream_t s) {
+    const StreamMetaHost& h = *static_cast<const StreamMetaHost*>(host_meta);
+    int64_t longs[3] = {h.sample_first, h.sample_count, h.padded_len};
+    int ints[3] = {h.frame_first, h.frame_count, h.row_first};
+    uint8_t* m = static_cast<uint8_t*>(meta_dev);
+    int64_t* dl = reinterpret_cast<int64_t*>(m);
+    int* di = reinterpret_cast<int*>(m + sizeof longs);
+    if (int rc = ctx->cuda(cudaMemcpyAsync(dl, longs, sizeof longs, cudaMemcpyHostToDevice, s), "stream meta")) return rc;
+    if (int rc = ctx->cuda(cudaMemcpyAsync(di, ints, sizeof ints, cudaMemcpyHostToDevice, s), "stream meta")) return rc;
+    meta.n_utt = 1;
+    meta.frame_first = di;
+    meta.frame_count = di + 1;
+    meta.sample_first = dl;
+    meta.sample_count = dl + 1;
+    meta.padded_len = dl + 2;
+    row_first = di + 2;
+    return TELMO_OK;
+}
+
+int FrontEnd::granite_stream_frames(const float* samples, int64_t n, int64_t len, int f0, int f1, float* logs,
+                                    float* new_peak, void* meta_dev, cudaStream_t s) {
+    // log_frame (src/granite_features.rs:95-133) of frames f0..f1: the kernel's frame f of the
+    // one utterance is local frame f - frame_first = f + f0, written to logs + f * n_mels.
+    if (f1 <= f0) return TELMO_OK;
+    StreamMetaHost h{0, n, len, -f0, f1 - f0, 0};
+    FrontMeta meta;
+    const int* row_first = nullptr;
+    if (int rc = stream_meta(&h, meta_dev, meta, row_first, s)) return rc;
+    float* out = logs + static_cast<int64_t>(f0) * n_mels;
+    granite_logmel_kernel<<<f1 - f0, 256, 0, s>>>(samples, meta, static_cast<const FftTables*>(tables), mel, out);
+    // Their largest value: the same kernel over frames 0..f1 - f0 of the block just written.
+    StreamMetaHost hm{0, n, len, 0, f1 - f0, 0};
+    FrontMeta mm;
+    if (int rc = stream_meta(&hm, static_cast<uint8_t*>(meta_dev) + 64, mm, row_first, s)) return rc;
+    utt_max_kernel<<<1, 256, 0, s>>>(out, mm, n_mels, new_peak);
+    launches += 2;
+    return ctx->cuda(cudaGetLastError(), "stream front end");
+}
+
+int FrontEnd::granite_stream_rows(const float* logs, int frames, const float* peak, int first, int last,
+                                  float* features, void* meta_dev, cudaStream_t s) {
+    // stack_rows (src/granite_features.rs:138-158) of rows first..last over `frames` frames: the
+    // kernel's row r is local row r - row_first = r + first.
+    if (last <= first) return TELMO_OK;
+    StreamMetaHost h{0, 0, 0, 0, frames, -first};
+    FrontMeta meta;
+    const int* row_first = nullptr;
+    if (int rc = stream_meta(&h, static_cast<uint8_t*>(meta_dev) + 128, meta, row_first, s)) return rc;
+    granite_stack_kernel<<<last - first, 160, 0, s>>>(logs, meta, n_mels, peak, row_first,
+                                                      features + static_cast<int64_t>(first) * 4 * n_mels);
+    ++launches;
+    return ctx->cuda(cudaGetLastError(), "stream front end");
+}
+
 }  // namespace telmo
 
 using namespace telmo;

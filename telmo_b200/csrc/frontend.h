@@ -59,6 +59,15 @@ struct FrontEnd {
     // samples_dev: every utterance's samples one after another; features: [sum rows, width].
     int run(const float* samples_dev, const int64_t* lengths, int n_utt, float* features, int* rows_out,
             cudaStream_t s);
+    // The Granite front end over part of one utterance, as a stream runs it: the log10 frames
+    // f0..f1 of its n samples zero-padded to len into logs + f0 * n_mels and their maximum into
+    // *new_peak; rows first..last of `frames` frames floored 8 below *peak into features + first
+    // * 4 * n_mels. meta_dev: 192 bytes of device memory the calls stage their layout in.
+    int granite_stream_frames(const float* samples, int64_t n, int64_t len, int f0, int f1, float* logs,
+                              float* new_peak, void* meta_dev, cudaStream_t s);
+    int granite_stream_rows(const float* logs, int frames, const float* peak, int first, int last, float* features,
+                            void* meta_dev, cudaStream_t s);
+    int stream_meta(const void* host_meta, void* meta_dev, FrontMeta& meta, const int*& row_first, cudaStream_t s);
 };
 
 }  // namespace telmo

@@ -363,6 +363,92 @@ int Granite::feed_forward(const FF& f, float* xb, int m, cudaStream_t s, bool no
     return gemm(q, m, f.down, xb, d, kActNone, 0.5f, 1, s);
 }
 
+int Granite::self_condition(float* xs, int n, cudaStream_t s) {
+    const int d = c.d_model;
+    if (int rc = ctx->cuda(quantize_x2(xs, d, n, d, q, s), "quant")) return rc;
+    ++launches;
+    if (int rc = gemm(q, n, head, big, vocab_ld, kActNone, 1.0f, 0, s)) return rc;
+    if (int rc = ctx->cuda(softmax_quant(big, n, c.vocab, vocab_ld, q, s), "softmax")) return rc;
+    ++launches;
+    return gemm(q, n, mid, xs, d, kActNone, 1.0f, 1, s);
+}
+
+int Granite::span(const Block& b, float* xs, int t, const float* window, int m, int lo, int out_start, int n,
+                  float* out, cudaStream_t s) {
+    const int d = c.d_model, cc = c.conv_channels, ctxn = c.context;
+    const int stride = b.strided ? 2 : 1;
+    // Task words: attention blocks of the span from its first frame (start begins a block), the
+    // convolution's output spans centred on stride * o - lo of the window, the pooled pairs.
+    std::vector<int> host;
+    const int nb = (t + ctxn - 1) / ctxn;
+    for (int k = 0; k < nb; ++k) {
+        host.push_back(k * ctxn);
+        host.push_back(std::min(ctxn, t - k * ctxn));
+    }
+    const int conv_off = static_cast<int>(host.size());
+    int nc = 0;
+    for (int r = 0; r < n; r += 32, ++nc)
+        host.insert(host.end(), {0, m, -out_start, out_start + r, std::min(32, n - r), stride, -lo});
+    const int pool_off = static_cast<int>(host.size());
+    if (b.strided)
+        for (int r = 0; r < n; ++r) host.push_back(2 * (out_start + r) - lo);
+    const int words = static_cast<int>(host.size());
+    if (int rc = ensure(std::max(t, m), (words + 7) / 8 + 1)) return rc;
+    if (int rc = ctx->cuda(cudaMemcpyAsync(tasks_dev, host.data(), sizeof(int) * words, cudaMemcpyHostToDevice, s),
+                           "granite tasks"))
+        return rc;
+    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "granite tasks")) return rc;
+
+    if (int rc = feed_forward(b.ff1, xs, t, s)) return rc;
+    // Attention (src/granite.rs:820-851).
+    if (int rc = ctx->cuda(ln_chain(xs, t, d, b.norm_att.g.p, b.norm_att.b.p, nullptr, nullptr, nullptr, &q, s), "ln"))
+        return rc;
+    ++launches;
+    const bool mma = granite_attention_mma_supported(c.head_dim, ctxn) && b.rel16;
+    if (int rc = gemm_w(q, t, b.qkv, nullptr, big, 3 * d, kActNone, 1.0f, 0, s, mma ? kOutF16Split : kOutF32))
+        return rc;
+    const float scale = static_cast<float>(std::pow(static_cast<double>(c.head_dim), -0.5));
+    const AttnTask* att_tasks = reinterpret_cast<const AttnTask*>(tasks_dev);
+    const cudaError_t ae =
+        mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(t) * 3 * d, c.heads,
+                                    c.head_dim, ctxn, att_tasks, nb, static_cast<const __half*>(b.rel16), b.rel.scales,
+                                    scale, att, s)
+            : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, nb, b.rel.values, b.rel.ld, b.rel.scales,
+                                scale, att, s);
+    if (int rc = ctx->cuda(ae, "attention")) return rc;
+    ++launches;
+    if (int rc = ctx->cuda(quantize_x2(att, d, t, d, q, s), "quant")) return rc;
+    ++launches;
+    if (int rc = gemm(q, t, b.out, xs, d, kActNone, 1.0f, 1, s)) return rc;
+    // Convolution module over the window's m frames (src/granite.rs:853-944).
+    if (int rc = ctx->cuda(ln_chain(window, m, d, b.norm_conv.g.p, b.norm_conv.b.p, nullptr, nullptr, nullptr, &q, s),
+                           "ln"))
+        return rc;
+    ++launches;
+    if (int rc = gemm(q, m, b.pw1, big, 2 * cc, kActNone, 1.0f, 0, s)) return rc;
+    if (int rc = ctx->cuda(glu_dwconv_silu(big, cc, c.conv_kernel, stride,
+                                           reinterpret_cast<const ConvTask*>(tasks_dev + conv_off), nc, b.dw_w.p,
+                                           b.dw_b.p, conv, s),
+                           "dwconv"))
+        return rc;
+    ++launches;
+    if (b.strided) {
+        if (int rc = ctx->cuda(pool_pairs(window, d, tasks_dev + pool_off, n, out, s), "pool")) return rc;
+        ++launches;
+    } else {
+        if (int rc = ctx->cuda(cudaMemcpyAsync(out, window + static_cast<int64_t>(out_start - lo) * d,
+                                               sizeof(float) * static_cast<size_t>(n) * d, cudaMemcpyDeviceToDevice, s),
+                               "span"))
+            return rc;
+    }
+    if (int rc = ctx->cuda(quantize_x2(conv, cc, n, cc, q, s), "quant")) return rc;
+    ++launches;
+    if (int rc = gemm(q, n, b.pw2, out, d, kActNone, 1.0f, 1, s)) return rc;
+    if (int rc = feed_forward(b.ff2, out, n, s)) return rc;
+    ++launches;
+    return ctx->cuda(ln_chain(out, n, d, b.norm_out.g.p, b.norm_out.b.p, out, nullptr, nullptr, nullptr, s), "ln");
+}
+
 int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap,
                     cudaStream_t s) {
     if (!finalized) return ctx->fail(TELMO_ERR_MODEL, "granite: the model is not finalized");
@@ -411,12 +497,12 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
             for (int u = 0; u < n_utt; ++u) {
                 const int n_out = strided ? len[u] / 2 : len[u];
                 for (int r = 0; r < n_out; r += 32) {
-                    host.insert(host.end(), {off, len[u], off_out, r, std::min(32, n_out - r), strided ? 2 : 1});
+                    host.insert(host.end(), {off, len[u], off_out, r, std::min(32, n_out - r), strided ? 2 : 1, 0});
                 }
                 off += len[u];
                 off_out += n_out;
             }
-            p.conv_n = (static_cast<int>(host.size()) - p.conv_off) / 6;
+            p.conv_n = (static_cast<int>(host.size()) - p.conv_off) / 7;
             p.m_out = off_out;
             p.pool_off = static_cast<int>(host.size());
             p.pool_n = 0;

@@ -98,6 +98,15 @@ struct Granite {
     int gemm_w(const QuantAct& a, int m, const DevWeights& w, const float* bias, void* out, int64_t ldc, int act,
                float scale, int acc, cudaStream_t s, int out_kind = kOutF32);
     int feed_forward(const FF& f, float* x, int m, cudaStream_t s, bool normed = false);
+    // Granite::block_span for one stream (src/granite.rs:795-952): block b over input frames
+    // start..end, whose rows x ([t = end - start, d]) end up holding their post-attention
+    // states; `window` holds the post-attention states of frames lo..end ([m, d], x's rows its
+    // last t) that the convolution reads; the outputs of frames out_start .. out_start + n go to
+    // out.
+    int span(const Block& b, float* x, int t, const float* window, int m, int lo, int out_start, int n, float* out,
+             cudaStream_t s);
+    // Self-conditioning (src/granite.rs:1040-1069) of n rows in place: x += mid(softmax(head(x))).
+    int self_condition(float* x, int n, cudaStream_t s);
     int encode(const float* feats, const int* rows, int n_utt, float* out, int* frames_out, int tap, cudaStream_t s);
     int logits(const float* encoded, int frames, float* out, int64_t ld, cudaStream_t s);
     int frame_ids(const float* encoded, int frames, uint32_t* ids, float* margin, cudaStream_t s);

@@ -364,7 +364,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     for (int u = 0; u < n_utt; ++u) {
         const int t = frames_out[u];
         for (int q0 = 0; q0 < t; q0 += q_rows) att.push_back({at, t, q0, tmax - t});
-        for (int r = 0; r < t; r += 32) conv.push_back({at, t, at, r, std::min(32, t - r), 1});
+        for (int r = 0; r < t; r += 32) conv.push_back({at, t, at, r, std::min(32, t - r), 1, 0});
         at += t;
     }
     const int M = static_cast<int>(m), P = 2 * tmax - 1;

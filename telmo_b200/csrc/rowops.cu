@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
     const ConvTask t = tasks[blockIdx.y];
     const int c = blockIdx.x * 128 + threadIdx.x;
     const bool live = c < cc;
-    const int f_lo = S * t.out_first - half;
+    const int f_lo = S * t.out_first + t.shift - half;
     const int nf = S * (t.count - 1) + K;
     const int64_t two_cc = 2 * static_cast<int64_t>(cc);
     for (int i0 = 0; i0 < nf; i0 += 8) {
@@ -284,7 +284,7 @@ __global__ void glu_dwconv_silu_any_kernel(const float* __restrict__ big, int cc
     for (int r = t.out_first; r < t.out_first + t.count; ++r) {
         float acc = __ldg(bias + c);
         for (int j = 0; j < k; ++j) {
-            const int f = t.stride * r + j - half;
+            const int f = t.stride * r + t.shift + j - half;
             if (f >= 0 && f < t.in_len)
                 acc = __fadd_rn(acc, __fmul_rn(__ldg(w + j * cc + c), glu_at(big, t.in_row + f, cc, c)));
         }

@@ -8,10 +8,12 @@
 namespace telmo {
 
 // One span of a depthwise convolution: output frames [out_first, out_first + count) of one
-// utterance whose input frames are rows in_row .. in_row + in_len - 1 and whose output frame r
-// goes to row out_row + r. stride is 1, or 2 for the blocks that halve the frame rate.
+// utterance whose input frames are rows in_row .. in_row + in_len - 1 (zero outside) and whose
+// output frame r goes to row out_row + r. Output frame r is centred on input frame
+// stride * r + shift: shift is 0 for a whole utterance and -lo for a window that starts at input
+// frame lo of a stream. stride is 1, or 2 for the blocks that halve the frame rate.
 struct ConvTask {
-    int in_row, in_len, out_row, out_first, count, stride;
+    int in_row, in_len, out_row, out_first, count, stride, shift;
 };
 
 // One attention block: rows [row, row + len) of one utterance, len <= context.

@@ -235,3 +235,81 @@ def ctc_tokens(ctx, ids, frames: Sequence[int], blank: int = 0, stream=None) -> 
         t = tok[first[u]:first[u] + cnt[u]]
         out.append([Token(int(a), int(b), int(c)) for a, b, c in t])
     return out
+
+
+class GraniteStream:
+    """GraniteStream (src/granite_stream.rs) on the GPU: one utterance transcribed while it is
+    spoken. ``push`` appends 16 kHz samples, ``update`` encodes what they can change; the frame
+    ids so far, the first frame the last update may have changed and the frozen frame follow the
+    reference's."""
+
+    def __init__(self, model: "Granite"):
+        self.model = model
+        self.ctx = model.ctx
+        h = ctypes.c_void_p()
+        check(_lib.load().telmo_granite_stream_create(model.handle, ctypes.byref(h)), self.ctx.handle)
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.load().telmo_granite_stream_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_freeze_lag(self, frames: int):
+        check(_lib.load().telmo_granite_stream_set_freeze_lag(self._h, int(frames)), self.ctx.handle)
+
+    def push(self, samples):
+        x = np.ascontiguousarray(samples, dtype=np.float32).reshape(-1)
+        check(_lib.load().telmo_granite_stream_push(self._h, x.ctypes.data, x.size), self.ctx.handle)
+
+    def update(self, finished: bool = False, stream=None):
+        check(_lib.load().telmo_granite_stream_update(self._h, int(finished), _stream(stream)),
+              self.ctx.handle)
+
+    def frames(self) -> int:
+        return _lib.load().telmo_granite_stream_frames(self._h)
+
+    def first_changed(self) -> int:
+        return _lib.load().telmo_granite_stream_first_changed(self._h)
+
+    def frozen(self) -> int:
+        return _lib.load().telmo_granite_stream_frozen(self._h)
+
+    def frame_ids(self) -> np.ndarray:
+        out = np.zeros(self.frames(), np.uint32)
+        check(_lib.load().telmo_granite_stream_frame_ids(self._h, out.ctypes.data, out.size),
+              self.ctx.handle)
+        return out
+
+    def tokens(self) -> List[Token]:
+        """The frames so far as CTC tokens (repeats collapsed, blanks dropped; ctc_tokens on the
+        GPU)."""
+        import torch
+        ids = self.frame_ids()
+        if ids.size == 0:
+            return []
+        dev = torch.from_numpy(ids.view(np.int32)).cuda()
+        return ctc_tokens(self.ctx, dev, [ids.size], self.model.config["blank"])[0]
+
+    def layer_output(self, layer: int) -> np.ndarray:
+        rows = ctypes.c_size_t(0)
+        L = _lib.load()
+        check(L.telmo_granite_stream_layer_output(self._h, layer, None, 0, ctypes.byref(rows)), self.ctx.handle)
+        out = np.zeros((rows.value, self.model.config["d_model"]), np.float32)
+        check(L.telmo_granite_stream_layer_output(self._h, layer, out.ctypes.data, rows.value, None),
+              self.ctx.handle)
+        return out
+
+    def features(self) -> np.ndarray:
+        rows = ctypes.c_size_t(0)
+        L = _lib.load()
+        check(L.telmo_granite_stream_features(self._h, None, 0, ctypes.byref(rows)), self.ctx.handle)
+        out = np.zeros((rows.value, 4 * self.model.config["n_mels"]), np.float32)
+        check(L.telmo_granite_stream_features(self._h, out.ctypes.data, rows.value, None), self.ctx.handle)
+        return out

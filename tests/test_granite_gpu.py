@@ -190,3 +190,96 @@ def test_full_size_spec_model_tracks_the_reference_until_it_diverges(ctx, oracle
         assert rel_l2(out.cpu().numpy(), ref.encode(f, tap_layer=tap, threads=8)) <= 2e-2
     gpu.ctx.check()
     gpu.close()
+
+
+# ---- streaming (GraniteStream, src/granite_stream.rs) ---------------------------------------------
+
+STREAM = synthetic.granite_config(d_model=128, heads=2, head_dim=64, layers=4, ff=256,
+                                  conv_channels=256, conv_kernel=5, context=16, max_relative=32,
+                                  vocab=33, n_mels=80)
+
+
+@pytest.fixture(scope="module")
+def stream_models(ctx, oracle_lib):
+    return _models(ctx, oracle_lib, STREAM, seed=7)
+
+
+def test_one_finished_stream_update_is_the_offline_pass(stream_models, oracle_lib):
+    # src/granite_stream.rs:14-17: one update over a whole utterance is Granite::encode and
+    # frame_ids -- here, the GPU's own offline front end, encoder and frame ids, bit for bit.
+    import torch
+    from telmo_b200.granite import GraniteStream, logmel
+    from telmo_b200 import _lib
+    gpu, ref = stream_models
+    audio = synthetic.audio(3.3, seed=5)
+    st = GraniteStream(gpu)
+    st.push(audio)
+    st.update(finished=True)
+    feats, rows = logmel(gpu.ctx, _lib.FRONTEND_GRANITE, torch.from_numpy(audio).cuda(), [audio.size])
+    gpu.ctx.check()
+    assert np.array_equal(st.features(), feats.cpu().numpy())
+    enc, frames = gpu.encode(feats, rows)
+    assert np.array_equal(st.layer_output(STREAM["layers"] - 1), enc.cpu().numpy())
+    ids = gpu.frame_ids(enc)
+    assert np.array_equal(st.frame_ids(), ids.cpu().numpy().astype(np.uint32))
+    assert st.first_changed() == 0
+    # And the oracle's stream (the reference's arithmetic) agrees.
+    ost = oracle_lib.GraniteStream(ref)
+    ost.push(audio)
+    ost.update(finished=True)
+    want = ost.layer_output(STREAM["layers"] - 1)
+    assert rel_l2(st.layer_output(STREAM["layers"] - 1), want) <= 2e-3
+
+
+def test_stream_updates_match_the_oracle_stream(stream_models, oracle_lib):
+    # Pieces of 0.37 s (about 4.6 encoder frames), a freeze lag of 2: after every update the
+    # frame count, the first changed frame and the frozen frame equal the oracle stream's, every
+    # block's cached outputs agree, and the ids agree wherever the top-2 logit gap is clear.
+    from telmo_b200.granite import GraniteStream
+    gpu, ref = stream_models
+    audio = synthetic.audio(4.1, seed=6)
+    st, ost = GraniteStream(gpu), oracle_lib.GraniteStream(ref)
+    st.set_freeze_lag(2)
+    ost.set_freeze_lag(2)
+    piece, at, updates = 5920, 0, 0
+    while at < audio.size:
+        st.push(audio[at:at + piece])
+        ost.push(audio[at:at + piece])
+        at += piece
+        done = at >= audio.size
+        st.update(finished=done)
+        ost.update(finished=done)
+        gpu.ctx.check()
+        assert (st.frames(), st.first_changed(), st.frozen()) == \
+            (len(ost.frame_ids()), ost.first_changed(), ost.frozen())
+        for layer in range(STREAM["layers"]):
+            got, want = st.layer_output(layer), ost.layer_output(layer)
+            assert got.shape == want.shape
+            if want.size:
+                assert rel_l2(got, want) <= 2e-3, (updates, layer)
+        last = ost.layer_output(STREAM["layers"] - 1)
+        if last.size:
+            ids, margin = ref.frame_ids(last)
+            clear = margin > 1e-2
+            assert np.array_equal(st.frame_ids()[clear], ids[clear])
+        updates += 1
+    assert updates >= 10 and st.frozen() > 0
+
+
+def test_stream_misuse_is_an_error(stream_models, ctx):
+    from telmo_b200 import TelmoError
+    from telmo_b200.granite import GraniteStream
+    gpu, _ = stream_models
+    st = GraniteStream(gpu)
+    st.push(synthetic.audio(0.5, seed=1))
+    st.update(finished=True)
+    with pytest.raises(TelmoError):
+        st.push(np.zeros(10, np.float32))
+    with pytest.raises(TelmoError):
+        st.update()
+    # A model whose first block is not strided cannot stream.
+    from telmo_b200.granite import Granite
+    bad = dict(STREAM, subsample_layers=[1, 2])
+    g2 = Granite.from_entries(ctx, bad, synthetic.granite_entries(bad, seed=3))
+    with pytest.raises(TelmoError):
+        GraniteStream(g2)
