@@ -30,7 +30,7 @@ struct Grow {
     int ensure(Ctx* ctx, size_t bytes, size_t keep, cudaStream_t s) {
         if (bytes <= cap) return TELMO_OK;
         void* q = nullptr;
-        const size_t want = bytes + bytes / 2 + 4096;
+        const size_t want = std::max<size_t>(2 * bytes, 1 << 20);  // doubling: few reallocations
         if (int rc = ctx->cuda(cudaMalloc(&q, want), "stream buffer")) return rc;
         if (p && keep) {
             if (int rc = ctx->cuda(cudaMemcpyAsync(q, p, std::min(keep, cap), cudaMemcpyDeviceToDevice, s), "stream"))
@@ -126,7 +126,11 @@ int GraniteStream::update(bool fin, cudaStream_t s) {
         return rc;
     // Input projection of the restacked rows (src/granite.rs:724-733).
     if (int rc = input.ensure(ctx, sizeof(float) * new_rows * d, sizeof(float) * rows * d, s)) return rc;
-    if (int rc = g->ensure(new_rows, 1)) return rc;
+    // The model's work buffers in power-of-two steps of rows, so a growing utterance reallocates
+    // them (a device-wide sync) a few times rather than at every update.
+    int reserve = 512;
+    while (reserve < new_rows) reserve *= 2;
+    if (int rc = g->ensure(reserve, 64)) return rc;
     const int m_in = new_rows - first_row;
     if (int rc = ctx->cuda(quantize_x2(features.as<float>() + static_cast<int64_t>(first_row) * width, width, m_in,
                                        width, g->q, s),
