@@ -130,7 +130,7 @@ int GraniteStream::update(bool fin, cudaStream_t s) {
     // them (a device-wide sync) a few times rather than at every update.
     int reserve = 512;
     while (reserve < new_rows) reserve *= 2;
-    if (int rc = g->ensure(reserve, 64)) return rc;
+    if (int rc = g->ensure(reserve, reserve / 4 + 64)) return rc;  // task words of a span: < rows / 6
     const int m_in = new_rows - first_row;
     if (int rc = ctx->cuda(quantize_x2(features.as<float>() + static_cast<int64_t>(first_row) * width, width, m_in,
                                        width, g->q, s),
