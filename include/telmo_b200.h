@@ -363,6 +363,39 @@ int telmo_parakeet_profile(telmo_parakeet *p, int enable);
 int telmo_parakeet_profile_read(telmo_parakeet *p, double *ms, long *launches, double *gemm_ops,
                                 double *gemm_bytes);
 
+/* ---- packs (src/pack.rs) ------------------------------------------------------------------- */
+
+/* The reference's weight file: "TELMOPAK", format version 1, 64-byte aligned entry data, a JSON
+ * index and a "TELMOIDX" trailer, checked as Pack::parse (src/pack.rs:98-259) checks it. Packs
+ * are read on the host (the whole file); the error text of a failed pack call is
+ * telmo_pack_last_error() (per thread). */
+typedef struct telmo_pack telmo_pack;
+#define TELMO_PACK_MATRIX 0
+#define TELMO_PACK_F32 1
+#define TELMO_PACK_BYTES 2
+int telmo_pack_open(const char *path, telmo_pack **out);
+int telmo_pack_from_bytes(const void *data, size_t len, telmo_pack **out);
+void telmo_pack_free(telmo_pack *p);
+const char *telmo_pack_last_error(void);
+/* The model the pack holds ("granite-speech-ctc", "parakeet-tdt"), a metadata value (or null). */
+const char *telmo_pack_model(const telmo_pack *p);
+const char *telmo_pack_meta(const telmo_pack *p, const char *key);
+/* Entry i: its name, kind (TELMO_PACK_*), precision (matrices), n and k (matrices; for f32
+ * tensors the first dimension and the rest's product) and data bytes. */
+size_t telmo_pack_entry_count(const telmo_pack *p);
+int telmo_pack_entry_info(const telmo_pack *p, size_t i, const char **name, int *kind, int *precision,
+                          size_t *n, size_t *k, size_t *bytes);
+/* A bytes entry's data (config.json, tokenizer.json), valid while the pack lives. */
+int telmo_pack_bytes(const telmo_pack *p, const char *name, const void **data, size_t *len);
+/* Config::from_json (src/granite.rs:60-146, src/parakeet.rs:70-141) of a model's config.json. */
+int telmo_granite_config_from_json(const char *json, size_t len, telmo_granite_config *out);
+int telmo_parakeet_config_from_json(const char *json, size_t len, telmo_parakeet_config *out);
+/* Granite::from_pack / Parakeet::from_pack (src/granite.rs:225-231, src/parakeet.rs:691-795) onto
+ * the device: the config from config.json, every entry the model knows uploaded as it is stored
+ * (Int8 or Q8_0 matrices), the model finalized; entries it does not know are ignored. */
+int telmo_granite_load_pack(telmo_ctx *ctx, const telmo_pack *p, telmo_granite **out);
+int telmo_parakeet_load_pack(telmo_ctx *ctx, const telmo_pack *p, telmo_parakeet **out);
+
 #ifdef __cplusplus
 }
 #endif

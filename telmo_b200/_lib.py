@@ -69,6 +69,19 @@ SIGNATURES = {
     "telmo_granite_transcribe": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_granite_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_granite_launches": (_c.c_long, [_vp]),
+    "telmo_pack_open": (_c.c_int, [_c.c_char_p, _vp]),
+    "telmo_pack_from_bytes": (_c.c_int, [_c.c_char_p, _sz, _vp]),
+    "telmo_pack_free": (None, [_vp]),
+    "telmo_pack_last_error": (_c.c_char_p, []),
+    "telmo_pack_model": (_c.c_char_p, [_vp]),
+    "telmo_pack_meta": (_c.c_char_p, [_vp, _c.c_char_p]),
+    "telmo_pack_entry_count": (_sz, [_vp]),
+    "telmo_pack_entry_info": (_c.c_int, [_vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "telmo_pack_bytes": (_c.c_int, [_vp, _c.c_char_p, _vp, _vp]),
+    "telmo_granite_config_from_json": (_c.c_int, [_c.c_char_p, _sz, _vp]),
+    "telmo_parakeet_config_from_json": (_c.c_int, [_c.c_char_p, _sz, _vp]),
+    "telmo_granite_load_pack": (_c.c_int, [_vp, _vp, _vp]),
+    "telmo_parakeet_load_pack": (_c.c_int, [_vp, _vp, _vp]),
     "telmo_granite_stream_create": (_c.c_int, [_vp, _vp]),
     "telmo_granite_stream_free": (None, [_vp]),
     "telmo_granite_stream_set_freeze_lag": (_c.c_int, [_vp, _c.c_int]),

@@ -1,12 +1,16 @@
 // api_internal.h -- the structures behind the C ABI's opaque handles.
 #pragma once
 
+#include <functional>
+#include <string>
+
 #include "kernels.h"
 
 #include <cstdarg>
 #include <string>
 
 struct telmo_ctx;
+struct telmo_pack;
 
 namespace telmo {
 
@@ -41,5 +45,12 @@ void encode_q8_0_panels(const float* rows, size_t n, size_t k, int8_t* values, f
 int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
                    const float* scales, DevWeights* out, const int* col_perm = nullptr);
 void free_weights(DevWeights* w);
+
+// Uploads a pack's matrix and f32 entries whose names `knows` accepts (pack.cu).
+using PackMatrixFn = std::function<int(const char*, int, size_t, size_t, const void*, const float*)>;
+using PackVectorFn = std::function<int(const char*, size_t, const float*)>;
+using PackKnowsFn = std::function<bool(const std::string&)>;
+int pack_load_entries(const telmo_pack* pk, const PackMatrixFn& set_matrix, const PackVectorFn& set_vector,
+                      const PackKnowsFn& knows);
 
 }  // namespace telmo

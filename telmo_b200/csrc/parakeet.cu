@@ -988,6 +988,41 @@ extern "C" int telmo_parakeet_transcribe(telmo_parakeet* pp, const float* sample
     return ctx->cuda(cudaStreamSynchronize(s), "transcribe");
 }
 
+extern "C" int telmo_parakeet_load_pack(telmo_ctx* ctx, const telmo_pack* pk, telmo_parakeet** out) {
+    // Parakeet::from_pack (src/parakeet.rs:691-795) onto the device.
+    if (!ctx || !pk || !out) return TELMO_ERR_ARGUMENT;
+    *out = nullptr;
+    Ctx* c = as_ctx(ctx);
+    const char* model = telmo_pack_model(pk);
+    if (strcmp(model, "parakeet-tdt")) return c->fail(TELMO_ERR_MODEL, "The pack holds %s, not Parakeet TDT.", model);
+    const void* cj = nullptr;
+    size_t cj_len = 0;
+    if (telmo_pack_bytes(pk, "config.json", &cj, &cj_len)) return c->fail(TELMO_ERR_MODEL, "Entry config.json is missing.");
+    telmo_parakeet_config cfg;
+    if (telmo_parakeet_config_from_json(static_cast<const char*>(cj), cj_len, &cfg))
+        return c->fail(TELMO_ERR_MODEL, "%s", telmo_pack_last_error());
+    telmo_parakeet* pp = nullptr;
+    if (int rc = telmo_parakeet_create(ctx, &cfg, &pp)) return rc;
+    Parakeet* p = as_parakeet(pp);
+    int rc = pack_load_entries(
+        pk,
+        [&](const char* name, int precision, size_t n, size_t k, const void* v, const float* s) {
+            return telmo_parakeet_set_matrix(pp, name, precision, n, k, v, s);
+        },
+        [&](const char* name, size_t len, const float* data) { return telmo_parakeet_set_vector(pp, name, len, data); },
+        [&](const std::string& name) {
+            Parakeet::Entry e = p->find(name);
+            return e.mat != nullptr || e.vec != nullptr;
+        });
+    if (!rc) rc = telmo_parakeet_finalize(pp);
+    if (rc) {
+        telmo_parakeet_free(pp);
+        return rc;
+    }
+    *out = pp;
+    return TELMO_OK;
+}
+
 extern "C" int telmo_parakeet_enc_proj(telmo_parakeet* pp, const float* encoded, size_t frames, float* out,
                                        void* stream) {
     Parakeet* p = as_parakeet(pp);

@@ -81,6 +81,19 @@ class Granite:
         check(L.telmo_granite_finalize(g._h), ctx.handle)
         return g
 
+    @staticmethod
+    def from_pack(ctx, pack) -> "Granite":
+        """Granite::from_pack: the config from the pack's config.json, every entry the model knows
+        uploaded as it is stored (src/pack.rs, Model::load)."""
+        from .pack import granite_config_from_json
+        obj = Granite.__new__(Granite)
+        obj.ctx = ctx
+        obj.config = granite_config_from_json(pack.bytes("config.json"))
+        h = ctypes.c_void_p()
+        check(_lib.load().telmo_granite_load_pack(ctx.handle, pack.handle, ctypes.byref(h)), ctx.handle)
+        obj._h = h
+        return obj
+
     @property
     def handle(self):
         return self._h

@@ -75,6 +75,19 @@ class Parakeet:
         check(L.telmo_parakeet_finalize(p._h), ctx.handle)
         return p
 
+    @staticmethod
+    def from_pack(ctx, pack) -> "Parakeet":
+        """Parakeet::from_pack: the config from the pack's config.json, every entry the model knows
+        uploaded as it is stored (src/pack.rs, Model::load)."""
+        from .pack import parakeet_config_from_json
+        obj = Parakeet.__new__(Parakeet)
+        obj.ctx = ctx
+        obj.config = parakeet_config_from_json(pack.bytes("config.json"))
+        h = ctypes.c_void_p()
+        check(_lib.load().telmo_parakeet_load_pack(ctx.handle, pack.handle, ctypes.byref(h)), ctx.handle)
+        obj._h = h
+        return obj
+
     @property
     def handle(self):
         return self._h
