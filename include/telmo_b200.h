@@ -124,6 +124,20 @@ int telmo_linear_noalloc(telmo_ctx *ctx, const float *a, size_t lda, size_t m,
                          const telmo_weights *w, const float *bias, int act, float scale,
                          int accumulate, void *c, int c_dtype, size_t ldc, void *stream);
 
+/* The conformer convolution module's row kernels over one utterance, the reference's Kernels
+ * entries glu, dwconv1d_frame and silu (src/kernels/mod.rs:462-470; scalar arithmetic at
+ * src/kernels/scalar.rs:149-187): row f of `in` (device f32 [frames, 2 * channels], the
+ * pointwise product's output) gives g_f = a / (1 + e^-b) over its halves a | b; output frame r
+ * is SiLU(bias + sum_j w[j] * g_{stride * r + j - kernel / 2}) (taps w device f32
+ * [kernel, channels], frames outside the utterance skipped), written to out (device f32
+ * [out frames, channels]) for r < frames (stride 1) or frames / 2 (stride 2). The tap sum is
+ * the reference's (from the bias, taps in order, each product rounded); the exponentials and
+ * divisions are the fast ones, a few ulp from expf and IEEE division. The task list goes
+ * through the context's workspace, as telmo_linear's operand does. */
+int telmo_conv_module_rows(telmo_ctx *ctx, const float *in, size_t frames, size_t channels,
+                           size_t kernel, size_t stride, const float *w, const float *bias,
+                           float *out, void *stream);
+
 /* telmo_linear on activations that telmo_quantize_x2 already split. */
 int telmo_linear_q(telmo_ctx *ctx, const int8_t *hi, const int8_t *lo, size_t ldq,
                    const float *row_scale, size_t m, const telmo_weights *w, const float *bias,

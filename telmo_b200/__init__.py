@@ -205,6 +205,15 @@ class Kernels:
                                             _ptr(lo), ldq, _ptr(scale), _stream(stream)),
               self.ctx.handle)
 
+    def conv_module_rows(self, x, frames: int, channels: int, kernel: int, stride: int, w, bias,
+                         out, stream=None) -> None:
+        """GLU, depthwise convolution and SiLU over one utterance's rows into `out` (f32), the
+        reference's glu, dwconv1d_frame and silu kernels (src/kernels/mod.rs:462-470)."""
+        check(_lib.load().telmo_conv_module_rows(self.ctx.handle, _ptr(x), frames, channels, kernel,
+                                                 stride, _ptr(w), _ptr(bias), _ptr(out),
+                                                 _stream(stream)),
+              self.ctx.handle)
+
     def linear_q(self, hi, lo, ldq: int, scale, m: int, w: DeviceWeights, c, ldc: int,
                  epi: Epilogue = Epilogue.PLAIN, out_dtype: DType = DType.F32,
                  stream=None) -> None:

@@ -49,6 +49,7 @@ SIGNATURES = {
     "telmo_linear": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _int, _float, _int, _vp, _int, _sz,
                             _vp]),
     "telmo_quantize_x2": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
+    "telmo_conv_module_rows": (_int, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp, _vp]),
     "telmo_linear_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _int, _float, _int, _vp, _int,
                                     _sz, _vp]),
     "telmo_linear_q": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp, _vp, _int, _float, _int, _vp,

@@ -3,9 +3,11 @@
 #include "api_internal.h"
 #include "frontend.h"
 #include "kernels.h"
+#include "rowops.h"
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -329,6 +331,33 @@ extern "C" int telmo_quantize_x2(telmo_ctx* c, const float* a, size_t lda, size_
     return ctx->cuda(quantize_x2(a, static_cast<int64_t>(lda), static_cast<int>(m), static_cast<int>(k), q,
                                  static_cast<cudaStream_t>(stream)),
                      "telmo_quantize_x2");
+}
+
+extern "C" int telmo_conv_module_rows(telmo_ctx* c, const float* in, size_t frames, size_t channels, size_t kernel,
+                                      size_t stride, const float* w, const float* bias, float* out, void* stream) {
+    Ctx* ctx = as_ctx(c);
+    if (!ctx) return TELMO_ERR_ARGUMENT;
+    if (!in || !w || !bias || !out || frames == 0 || frames > (1u << 30) || channels == 0 ||
+        channels > (1u << 20) || kernel == 0 || kernel % 2 == 0 || kernel > 63 || (stride != 1 && stride != 2))
+        return ctx->fail(TELMO_ERR_ARGUMENT,
+                         "telmo_conv_module_rows: bad arguments (frames=%zu channels=%zu kernel=%zu stride=%zu)",
+                         frames, channels, kernel, stride);
+    if (int rc = ctx->use_device()) return rc;
+    const int len = static_cast<int>(frames), st = static_cast<int>(stride);
+    const int n_out = st == 2 ? len / 2 : len;
+    if (n_out == 0) return TELMO_OK;
+    std::vector<ConvTask> tasks;
+    for (int r = 0; r < n_out; r += 32) tasks.push_back({0, len, 0, r, std::min(32, n_out - r), st, 0});
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t bytes = sizeof(ConvTask) * tasks.size();
+    void* dev = ctx->workspace(bytes, s);
+    if (!dev) return ctx->fail(TELMO_ERR_CUDA, "telmo_conv_module_rows: workspace of %zu bytes", bytes);
+    // A pageable source is staged before cudaMemcpyAsync returns, so `tasks` may be freed after.
+    if (int rc = ctx->cuda(cudaMemcpyAsync(dev, tasks.data(), bytes, cudaMemcpyHostToDevice, s), "conv tasks"))
+        return rc;
+    return ctx->cuda(glu_dwconv_silu(in, static_cast<int>(channels), static_cast<int>(kernel), st,
+                                     static_cast<const ConvTask*>(dev), static_cast<int>(tasks.size()), w, bias, out, s),
+                     "telmo_conv_module_rows");
 }
 
 static int run_gemm(Ctx* ctx, const QuantAct& q, size_t m, const Weights* w, const float* bias, int act,

@@ -86,13 +86,14 @@ __device__ __forceinline__ void record_error(uint32_t* error, uint32_t code) {
 // otherwise saturate at two conversions per output): x = h * 65536 + l with l in [0, 65536);
 // h and l convert exactly through the float bit pattern of 2^23 + n, h * 65536 is exact, and
 // the one rounded add yields round-to-nearest-even of x, as __int2float_rn does.
+// The biased patterns are built with one add (h + 32768 < 2^16, so adding 0x4b008000 sets the
+// same bits as the OR) and one byte permute (the low two bytes under 0x4b00), and the product by
+// 65536 being exact, one fused multiply-add rounds the sum exactly once.
 __device__ __forceinline__ float exact_i2f(uint32_t bits) {
-    const int32_t x = static_cast<int32_t>(bits);
-    const int32_t h = x >> 16;  // -32768 .. 32767
-    const uint32_t l = bits & 0xffffu;
-    const float fh = __fsub_rn(__int_as_float(0x4b000000 | static_cast<uint32_t>(h + 32768)), 8421376.0f);
-    const float fl = __fsub_rn(__int_as_float(0x4b000000 | l), 8388608.0f);
-    return __fadd_rn(__fmul_rn(fh, 65536.0f), fl);
+    const int32_t h = static_cast<int32_t>(bits) >> 16;  // -32768 .. 32767
+    const float fh = __fsub_rn(__int_as_float(h + 0x4b008000), 8421376.0f);
+    const float fl = __fsub_rn(__uint_as_float(__byte_perm(bits, 0x4b000000u, 0x7610)), 8388608.0f);
+    return __fmaf_rn(fh, 65536.0f, fl);
 }
 
 // Step for step what oracle_epilogue_x2 computes, with no contraction into FMA. A missing bias
@@ -147,7 +148,7 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&hi)[32], const uint
     }
 }
 
-// The epilogue of a staged chunk, step for step as epilogue_value:
+// The epilogue of a staged chunk, step for step as epilogue_value (except under SiLU, below):
 // v = ((float)hi + (float)lo * (1/254)) * rs * ws [+ bias] [act] [* scale], the chunk's 32 row
 // scales in registers. A bias of 0 and a scale of 1 change no value and are skipped.
 template <int ACT, bool BIAS, bool SCALE>
@@ -155,13 +156,21 @@ __device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[32], const u
                                                const float (&rs)[32], float ws, float bs, float scale,
                                                float (&v)[32]) {
     const float inv254 = 1.0f / 254.0f;
+    const float ws254 = __fmul_rn(ws, inv254);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const float fh = __int2float_rn(static_cast<int32_t>(hi[j]));
         const float fl = ACT == kActSilu ? exact_i2f(lo[j]) : __int2float_rn(static_cast<int32_t>(lo[j]));
-        float x = __fadd_rn(fh, __fmul_rn(fl, inv254));
-        x = __fmul_rn(__fmul_rn(x, rs[j]), ws);
-        if (BIAS) x = __fadd_rn(x, bs);
+        float x;
+        if (ACT == kActSilu) {
+            // SiLU's values already sit a few ulp from the oracle's (fast exponential), so the
+            // scale and bias contract into two fused multiply-adds: fh * rs * ws + fl * rs * ws / 254.
+            x = __fmaf_rn(fl, __fmul_rn(rs[j], ws254), __fmaf_rn(fh, __fmul_rn(rs[j], ws), BIAS ? bs : 0.0f));
+        } else {
+            x = __fadd_rn(fh, __fmul_rn(fl, inv254));
+            x = __fmul_rn(__fmul_rn(x, rs[j]), ws);
+            if (BIAS) x = __fadd_rn(x, bs);
+        }
         if (ACT == kActRelu) x = fmaxf(x, 0.0f);
         if (ACT == kActSilu) x = __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
         if (SCALE) x = __fmul_rn(x, scale);

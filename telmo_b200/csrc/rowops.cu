@@ -226,7 +226,11 @@ __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t r
 // frames' loads in flight at a time -- in a shared column per thread, frames outside the
 // utterance as zeros: adding w * 0 leaves the sum bit for bit as skipping the tap does (the
 // weights are finite), so the taps need no bounds checks. S is the stride of every task.
+// The kernel is bound by instruction issue, not by memory: outputs are made kConvGroup at a
+// time from a register window of the S * (kConvGroup - 1) + K staged values they read, so each
+// staged value is loaded from shared memory once per group rather than once per tap.
 constexpr int kConvSpan = 32;  // output frames per task (set by the host's task list)
+constexpr int kConvGroup = 4;  // outputs per register window (divides kConvSpan)
 
 template <int K, int S>
 __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __restrict__ big, int cc,
@@ -237,21 +241,23 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
     constexpr int half = K / 2;
     constexpr int kFrames = S * (kConvSpan - 1) + K;  // input frames of a span
     __shared__ float glu[kFrames][128];
+    constexpr int kWindow = S * (kConvGroup - 1) + K;
     const ConvTask t = tasks[blockIdx.y];
     const int c = blockIdx.x * 128 + threadIdx.x;
     const bool live = c < cc;
     const int f_lo = S * t.out_first + t.shift - half;
     const int nf = S * (t.count - 1) + K;
     const int64_t two_cc = 2 * static_cast<int64_t>(cc);
+    const float* col = big + (live ? c : 0);
     for (int i0 = 0; i0 < nf; i0 += 8) {
         float a[8], b[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int f = f_lo + i0 + u;
-            const bool ok = live && i0 + u < nf && f >= 0 && f < t.in_len;
-            const int64_t row = static_cast<int64_t>(t.in_row + (ok ? f : 0));
-            a[u] = ok ? big[row * two_cc + c] : 0.0f;
-            b[u] = ok ? big[row * two_cc + cc + c] : 0.0f;
+            const bool ok = live && i0 + u < nf && static_cast<unsigned>(f) < static_cast<unsigned>(t.in_len);
+            const float* p = col + static_cast<int64_t>(t.in_row + (ok ? f : 0)) * two_cc;
+            a[u] = ok ? __ldg(p) : 0.0f;
+            b[u] = ok ? __ldg(p + cc) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
@@ -263,13 +269,22 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
     for (int j = 0; j < K; ++j) wk[j] = __ldg(w + j * cc + c);
     const float bc = __ldg(bias + c);
     float* orow = out + static_cast<int64_t>(t.out_row + t.out_first) * cc + c;
-    for (int r = 0; r < t.count; ++r) {
-        const float* g = &glu[S * r][threadIdx.x];
-        float acc = bc;
+    // The last group may run past the task's count: its window still ends inside the array
+    // (S * 31 + K - 1 < kFrames), and the outputs past count, made from unstaged rows, are not
+    // stored.
+#pragma unroll 1
+    for (int r0 = 0; r0 < t.count; r0 += kConvGroup) {
+        float win[kWindow];
 #pragma unroll
-        for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(wk[j], g[j * 128]));
-        acc = __fdividef(acc, __fadd_rn(1.0f, __expf(-acc)));
-        orow[static_cast<int64_t>(r) * cc] = acc;
+        for (int i = 0; i < kWindow; ++i) win[i] = glu[S * r0 + i][threadIdx.x];
+#pragma unroll
+        for (int g = 0; g < kConvGroup; ++g) {
+            float acc = bc;
+#pragma unroll
+            for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(wk[j], win[S * g + j]));
+            acc = __fdividef(acc, __fadd_rn(1.0f, __expf(-acc)));
+            if (r0 + g < t.count) orow[static_cast<int64_t>(r0 + g) * cc] = acc;
+        }
     }
 }
 
