@@ -405,8 +405,8 @@ cudaError_t txl_attention_mma(const __half* qkv, int64_t plane, const __half* po
                               int npos, const TxlTask* tasks, int n_tasks, int heads, int hd, const float* bias_u,
                               float scale, float* att, cudaStream_t s) {
     if (n_tasks <= 0) return cudaSuccess;
-    if (hd == 128) return launch<128, 32>(qkv, plane, pos, pplane, cpos, npos, tasks, n_tasks, heads, bias_u, scale, att, s);
-    if (hd == 64) return launch<64, 32>(qkv, plane, pos, pplane, cpos, npos, tasks, n_tasks, heads, bias_u, scale, att, s);
+    if (hd == 128) return launch<128, 64>(qkv, plane, pos, pplane, cpos, npos, tasks, n_tasks, heads, bias_u, scale, att, s);
+    if (hd == 64) return launch<64, 64>(qkv, plane, pos, pplane, cpos, npos, tasks, n_tasks, heads, bias_u, scale, att, s);
     return cudaErrorInvalidValue;
 }
 
