@@ -96,23 +96,44 @@ __device__ __forceinline__ float exact_i2f(uint32_t bits) {
     return __fmaf_rn(fh, 65536.0f, fl);
 }
 
-// Step for step what oracle_epilogue_x2 computes, with no contraction into FMA. A missing bias
-// is passed as 0, which leaves every value unchanged (the sums are never -0). SiLU uses the
-// fast exponential and division (a few ulp from v / (1 + expf(-v))). The conversion unit does
-// the two int-to-float conversions, except under SiLU, whose exponential and reciprocal already
-// take two of its slots per value; there the integer path above converts the low sum.
+// 2^x and 1/x as the PTX ISA's single approximate instructions (ex2.approx.ftz.f32, relative
+// error about 2^-22; rcp.approx.ftz.f32, within 1 ulp); SiLU takes e^-x as 2^(-x log2 e).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The SiLU epilogue (both output paths): its values already sit a few ulp from the oracle's
+// (approximate exponential and reciprocal), so the combination contracts:
+// v = (fh + fl / 254) * (rs * ws) + bias, then v / (1 + e^-v).
+__device__ __forceinline__ float silu_value(float fh, float fl, float rs, float ws, float bias) {
+    const float x = __fmaf_rn(__fmaf_rn(fl, 1.0f / 254.0f, fh), __fmul_rn(rs, ws), bias);
+    return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(x, -1.44269504f)))));
+}
+
+// Step for step what oracle_epilogue_x2 computes, with no contraction into FMA, except under
+// SiLU (silu_value above). A missing bias is passed as 0, which leaves every value unchanged (the
+// sums are never -0). The conversion unit does the two int-to-float conversions, except under
+// SiLU, whose exponential and reciprocal already take two of its slots per value; there the
+// integer path above converts the low sum.
 template <int ACT>
 __device__ __forceinline__ float epilogue_value(uint32_t acc_hi, uint32_t acc_lo, float rs, float ws,
                                                 float bias, float scale) {
     const float inv254 = 1.0f / 254.0f;
     const float fh = __int2float_rn(static_cast<int32_t>(acc_hi));
-    const float fl = ACT == kActSilu ? exact_i2f(acc_lo) : __int2float_rn(static_cast<int32_t>(acc_lo));
+    if (ACT == kActSilu) return __fmul_rn(silu_value(fh, exact_i2f(acc_lo), rs, ws, bias), scale);
+    const float fl = __int2float_rn(static_cast<int32_t>(acc_lo));
     float v = __fadd_rn(fh, __fmul_rn(fl, inv254));
     v = __fmul_rn(v, rs);
     v = __fmul_rn(v, ws);
     v = __fadd_rn(v, bias);
     if (ACT == kActRelu) v = fmaxf(v, 0.0f);
-    if (ACT == kActSilu) v = __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
     return __fmul_rn(v, scale);
 }
 
@@ -156,23 +177,19 @@ __device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[32], const u
                                                const float (&rs)[32], float ws, float bs, float scale,
                                                float (&v)[32]) {
     const float inv254 = 1.0f / 254.0f;
-    const float ws254 = __fmul_rn(ws, inv254);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const float fh = __int2float_rn(static_cast<int32_t>(hi[j]));
-        const float fl = ACT == kActSilu ? exact_i2f(lo[j]) : __int2float_rn(static_cast<int32_t>(lo[j]));
         float x;
         if (ACT == kActSilu) {
-            // SiLU's values already sit a few ulp from the oracle's (fast exponential), so the
-            // scale and bias contract into two fused multiply-adds: fh * rs * ws + fl * rs * ws / 254.
-            x = __fmaf_rn(fl, __fmul_rn(rs[j], ws254), __fmaf_rn(fh, __fmul_rn(rs[j], ws), BIAS ? bs : 0.0f));
+            x = silu_value(fh, exact_i2f(lo[j]), rs[j], ws, BIAS ? bs : 0.0f);
         } else {
+            const float fl = __int2float_rn(static_cast<int32_t>(lo[j]));
             x = __fadd_rn(fh, __fmul_rn(fl, inv254));
             x = __fmul_rn(__fmul_rn(x, rs[j]), ws);
             if (BIAS) x = __fadd_rn(x, bs);
         }
         if (ACT == kActRelu) x = fmaxf(x, 0.0f);
-        if (ACT == kActSilu) x = __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
         if (SCALE) x = __fmul_rn(x, scale);
         v[j] = x;
     }

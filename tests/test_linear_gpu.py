@@ -4,8 +4,8 @@ Mirrors the reference's matrix-product tests (src/kernels/mod.rs:962-1128): shap
 edges, every epilogue, accumulate, and the config-1 shape. Three bars:
   * the quantized activations and the two int32 sums are bit-exact against the oracle;
   * the scaled output equals the oracle's step-for-step restatement of the CUDA epilogue bit for
-    bit (act none/relu) or within 1e-5 relative (SiLU, which the epilogue computes with the fast
-    exponential and division);
+    bit (act none/relu) or within 1e-5 relative (SiLU, which the epilogue computes with the
+    approximate exponential and reciprocal and a contracted scale-and-bias step);
   * against the reference's own f32 path (int8 weights widened, f32 activations), each output
     matrix is within 1e-3 max-relative: max|got - ref| / max|ref| <= 1e-3.
 """
