@@ -96,25 +96,12 @@ __device__ __forceinline__ float exact_i2f(uint32_t bits) {
     return __fmaf_rn(fh, 65536.0f, fl);
 }
 
-// 2^x and 1/x as the PTX ISA's single approximate instructions (ex2.approx.ftz.f32, relative
-// error about 2^-22; rcp.approx.ftz.f32, within 1 ulp); SiLU takes e^-x as 2^(-x log2 e).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 // The SiLU epilogue (both output paths): its values already sit a few ulp from the oracle's
 // (approximate exponential and reciprocal), so the combination contracts:
 // v = (fh + fl / 254) * (rs * ws) + bias, then v / (1 + e^-v).
 __device__ __forceinline__ float silu_value(float fh, float fl, float rs, float ws, float bias) {
     const float x = __fmaf_rn(__fmaf_rn(fl, 1.0f / 254.0f, fh), __fmul_rn(rs, ws), bias);
-    return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(x, -1.44269504f)))));
+    return mul_sigmoid(x, x);
 }
 
 // Step for step what oracle_epilogue_x2 computes, with no contraction into FMA, except under

