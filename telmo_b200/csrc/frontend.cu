@@ -37,19 +37,26 @@ __device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a,
 __device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ double dsub(double a, double b) { return __dsub_rn(a, b); }
 
-// One frame's power spectrum from its 512 windowed samples in seg (shared), into power (shared).
-// 256 threads.
-__device__ void power_spectrum(const FftTables* __restrict__ T, const double* seg, double* zr, double* zi,
-                               double* power) {
-    const int tid = threadIdx.x;
-    zr[T->rev[tid]] = seg[2 * tid];
-    zi[T->rev[tid]] = seg[2 * tid + 1];
-    __syncthreads();
-    for (int size = 2; size <= HALF; size *= 2) {
-        const int half = size / 2, step = HALF / size;
-        if (tid < HALF / 2) {
-            const int grp = tid / half, j = tid % half;
-            const int a = grp * size + j, b = a + half;
+// One frame per warp, kFrameWarps frames per CTA: a frame's FFT is 128 butterflies per stage, so
+// a warp (four butterflies per lane, __syncwarp between stages) keeps every lane busy with no
+// block-wide barrier; each warp owns 512 doubles of shared memory.
+constexpr int kFrameWarps = 8;
+
+// One frame's power spectrum, in a warp. On entry z = zr + i zi (zr = buf, zi = buf + 256) holds
+// the packed samples at their bit-reversed positions; on exit power[k] = buf[k], k <= 256. Each
+// butterfly and bin is the reference's arithmetic step for step, whichever lane computes it.
+__device__ void warp_power_spectrum(const FftTables* __restrict__ T, double* buf, int lane) {
+    double* zr = buf;
+    double* zi = buf + HALF;
+#pragma unroll
+    for (int lg = 0; lg < 8; ++lg) {  // sizes 2 .. 256
+        const int half = 1 << lg, step = HALF >> (lg + 1);
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < HALF / 2 / 32; ++q) {
+            const int t = lane + 32 * q;
+            const int grp = t >> lg, j = t & (half - 1);
+            const int a = grp * 2 * half + j, b = a + half;
             const double wr = T->half_re[j * step], wi = T->half_im[j * step];
             const double xr = zr[b], xi = zi[b];
             const double br = dsub(dmul(xr, wr), dmul(xi, wi));
@@ -60,9 +67,13 @@ __device__ void power_spectrum(const FftTables* __restrict__ T, const double* se
             zr[b] = dsub(ar, br);
             zi[b] = dsub(ai, bi);
         }
-        __syncthreads();
     }
-    for (int k = tid; k < BINS; k += blockDim.x) {
+    __syncwarp();
+    double pw[(BINS + 31) / 32];
+#pragma unroll
+    for (int i = 0; i < (BINS + 31) / 32; ++i) {
+        const int k = lane + 32 * i;
+        if (k >= BINS) break;
         const double r = zr[k % HALF], im = zi[k % HALF];
         const double cr = zr[(HALF - k) % HALF], ci = -zi[(HALF - k) % HALF];
         const double er = dmul(dadd(r, cr), 0.5), ei = dmul(dadd(im, ci), 0.5);
@@ -71,9 +82,16 @@ __device__ void power_spectrum(const FftTables* __restrict__ T, const double* se
         const double wr = T->split_re[k], wi = T->split_im[k];
         const double xr = dadd(er, dsub(dmul(wr, orr), dmul(wi, oi)));
         const double xi = dadd(ei, dadd(dmul(wr, oi), dmul(wi, orr)));
-        power[k] = dadd(dmul(xr, xr), dmul(xi, xi));
+        pw[i] = dadd(dmul(xr, xr), dmul(xi, xi));
     }
-    __syncthreads();
+    __syncwarp();  // every lane has read z
+#pragma unroll
+    for (int i = 0; i < (BINS + 31) / 32; ++i) {
+        const int k = lane + 32 * i;
+        if (k >= BINS) break;
+        buf[k] = pw[i];
+    }
+    __syncwarp();
 }
 
 // Which utterance a global frame index belongs to (frame_first is increasing, n entries).
@@ -87,31 +105,44 @@ __device__ __forceinline__ int find_utt(const int* __restrict__ frame_first, int
     return lo;
 }
 
-// Granite log_frame (src/granite_features.rs:95-133) for every frame of the batch.
-__global__ void __launch_bounds__(256) granite_logmel_kernel(const float* __restrict__ samples, const FrontMeta meta,
-                                                            const FftTables* __restrict__ T, const MelTable mel,
-                                                            float* __restrict__ logs) {
-    __shared__ double seg[N_FFT], zr[HALF], zi[HALF], power[BINS];
-    const int f = blockIdx.x;
+// Granite log_frame (src/granite_features.rs:95-133) for frames 0 .. frames - 1 of the batch.
+__global__ void __launch_bounds__(32 * kFrameWarps) granite_logmel_kernel(const float* __restrict__ samples,
+                                                                          const FrontMeta meta, int frames,
+                                                                          const FftTables* __restrict__ T,
+                                                                          const MelTable mel, float* __restrict__ logs) {
+    __shared__ double bufs[kFrameWarps][N_FFT];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int f = blockIdx.x * kFrameWarps + warp;
+    if (f >= frames) return;  // no block-wide barrier follows
+    double* buf = bufs[warp];
     const int u = find_utt(meta.frame_first, meta.n_utt, f);
     const int local = f - meta.frame_first[u];
     const float* x = samples + meta.sample_first[u];
     const long n = meta.sample_count[u];
     const long len = meta.padded_len[u];
     const long start = static_cast<long>(local) * HOP - N_FFT / 2;
-    for (int i = threadIdx.x; i < N_FFT; i += blockDim.x) {
-        long j = start + i;
-        long jj = j < 0 ? -j : (j >= len ? 2 * (len - 1) - j : j);
-        const double s = jj < n ? static_cast<double>(x[jj]) : 0.0;
-        seg[i] = dmul(s, T->window[i]);
+    // The reflect-padded, windowed samples, packed two to a complex value at its bit-reversed slot.
+#pragma unroll
+    for (int q = 0; q < HALF / 32; ++q) {
+        const int m = lane + 32 * q;
+        double v[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int i = 2 * m + e;
+            const long j = start + i;
+            const long jj = j < 0 ? -j : (j >= len ? 2 * (len - 1) - j : j);
+            const double smp = jj < n ? static_cast<double>(x[jj]) : 0.0;
+            v[e] = dmul(smp, T->window[i]);
+        }
+        buf[T->rev[m]] = v[0];
+        buf[HALF + T->rev[m]] = v[1];
     }
-    __syncthreads();
-    power_spectrum(T, seg, zr, zi, power);
-    for (int m = threadIdx.x; m < mel.n_mels; m += blockDim.x) {
+    warp_power_spectrum(T, buf, lane);
+    for (int m = lane; m < mel.n_mels; m += 32) {
         double acc = 0.0;
         const int first = mel.first[m], cnt = mel.count[m];
         const float* w = mel.weights + mel.offset[m];
-        for (int k = 0; k < cnt; ++k) acc = dadd(acc, dmul(static_cast<double>(w[k]), power[first + k]));
+        for (int k = 0; k < cnt; ++k) acc = dadd(acc, dmul(static_cast<double>(w[k]), buf[first + k]));
         const float energy = fmaxf(static_cast<float>(acc), 1e-10f);
         logs[static_cast<long>(f) * mel.n_mels + m] = static_cast<float>(log10(static_cast<double>(energy)));
     }
@@ -167,38 +198,50 @@ __global__ void granite_stack_kernel(const float* __restrict__ logs, const Front
     }
 }
 
-// Parakeet log_mel_frame (src/features.rs:156-173) for every frame: pre-emphasised samples under
-// the 400-sample window (zero outside the utterance), ln(acc + 2^-24) in f64.
-__global__ void __launch_bounds__(256) parakeet_logmel_kernel(const float* __restrict__ samples, const FrontMeta meta,
-                                                             const FftTables* __restrict__ T, const MelTable mel,
-                                                             double* __restrict__ logs) {
-    __shared__ double seg[N_FFT], zr[HALF], zi[HALF], power[BINS];
-    const int f = blockIdx.x;
+// Parakeet log_mel_frame (src/features.rs:156-173) for frames 0 .. frames - 1: pre-emphasised
+// samples under the 400-sample window (zero outside the utterance), ln(acc + 2^-24) in f64.
+__global__ void __launch_bounds__(32 * kFrameWarps) parakeet_logmel_kernel(const float* __restrict__ samples,
+                                                                           const FrontMeta meta, int frames,
+                                                                           const FftTables* __restrict__ T,
+                                                                           const MelTable mel,
+                                                                           double* __restrict__ logs) {
+    __shared__ double bufs[kFrameWarps][N_FFT];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int f = blockIdx.x * kFrameWarps + warp;
+    if (f >= frames) return;  // no block-wide barrier follows
+    double* buf = bufs[warp];
     const int u = find_utt(meta.frame_first, meta.n_utt, f);
     const int local = f - meta.frame_first[u];
     const float* x = samples + meta.sample_first[u];
     const long n = meta.sample_count[u];
     constexpr int offset = (N_FFT - WIN) / 2;
-    for (int i = threadIdx.x; i < N_FFT; i += blockDim.x) {
-        double v = 0.0;
-        if (i >= offset && i < offset + WIN) {
-            // Sample index of window position i: f * hop + i - n_fft / 2.
-            const long j = static_cast<long>(local) * HOP + i - N_FFT / 2;
-            if (j >= 0 && j < n) {
-                const float pe = j == 0 ? x[0] : __fsub_rn(x[j], __fmul_rn(0.97f, x[j - 1]));
-                v = dmul(static_cast<double>(pe), T->window[i]);
+#pragma unroll
+    for (int q = 0; q < HALF / 32; ++q) {
+        const int m = lane + 32 * q;
+        double v[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int i = 2 * m + e;
+            v[e] = 0.0;
+            if (i >= offset && i < offset + WIN) {
+                // Sample index of window position i: f * hop + i - n_fft / 2.
+                const long j = static_cast<long>(local) * HOP + i - N_FFT / 2;
+                if (j >= 0 && j < n) {
+                    const float pe = j == 0 ? x[0] : __fsub_rn(x[j], __fmul_rn(0.97f, x[j - 1]));
+                    v[e] = dmul(static_cast<double>(pe), T->window[i]);
+                }
             }
         }
-        seg[i] = v;
+        buf[T->rev[m]] = v[0];
+        buf[HALF + T->rev[m]] = v[1];
     }
-    __syncthreads();
-    power_spectrum(T, seg, zr, zi, power);
+    warp_power_spectrum(T, buf, lane);
     const double guard = 1.0 / 16777216.0;
-    for (int m = threadIdx.x; m < mel.n_mels; m += blockDim.x) {
+    for (int m = lane; m < mel.n_mels; m += 32) {
         double acc = 0.0;
         const int first = mel.first[m], cnt = mel.count[m];
         const float* w = mel.weights + mel.offset[m];
-        for (int k = 0; k < cnt; ++k) acc = dadd(acc, dmul(static_cast<double>(w[k]), power[first + k]));
+        for (int k = 0; k < cnt; ++k) acc = dadd(acc, dmul(static_cast<double>(w[k]), buf[first + k]));
         logs[static_cast<long>(f) * mel.n_mels + m] = log(dadd(acc, guard));
     }
 }
@@ -498,13 +541,15 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
     const int* row_first = di + 2 * n_utt;
     if (kind == kGranite) {
         float* logs = static_cast<float*>(scratch);
-        granite_logmel_kernel<<<total_frames, 256, 0, s>>>(samples_dev, meta, static_cast<const FftTables*>(tables), mel, logs);
+        granite_logmel_kernel<<<(total_frames + kFrameWarps - 1) / kFrameWarps, 32 * kFrameWarps, 0, s>>>(
+            samples_dev, meta, total_frames, static_cast<const FftTables*>(tables), mel, logs);
         utt_max_kernel<<<n_utt, 256, 0, s>>>(logs, meta, n_mels, peak);
         granite_stack_kernel<<<rf, 160, 0, s>>>(logs, meta, n_mels, peak, row_first, features);
         launches += 3;
     } else {
         double* logs = static_cast<double*>(scratch);
-        parakeet_logmel_kernel<<<total_frames, 256, 0, s>>>(samples_dev, meta, static_cast<const FftTables*>(tables), mel, logs);
+        parakeet_logmel_kernel<<<(total_frames + kFrameWarps - 1) / kFrameWarps, 32 * kFrameWarps, 0, s>>>(
+            samples_dev, meta, total_frames, static_cast<const FftTables*>(tables), mel, logs);
         dim3 grid(n_utt, (n_mels + 31) / 32);
         parakeet_normalize_kernel<<<grid, 256, 0, s>>>(logs, meta, n_mels, features);
         launches += 2;
@@ -553,7 +598,8 @@ int FrontEnd::granite_stream_frames(const float* samples, int64_t n, int64_t len
     const int* row_first = nullptr;
     if (int rc = stream_meta(&h, meta_dev, meta, row_first, s)) return rc;
     float* out = logs + static_cast<int64_t>(f0) * n_mels;
-    granite_logmel_kernel<<<f1 - f0, 256, 0, s>>>(samples, meta, static_cast<const FftTables*>(tables), mel, out);
+    granite_logmel_kernel<<<(f1 - f0 + kFrameWarps - 1) / kFrameWarps, 32 * kFrameWarps, 0, s>>>(
+        samples, meta, f1 - f0, static_cast<const FftTables*>(tables), mel, out);
     // Their largest value: the same kernel over frames 0..f1 - f0 of the block just written.
     StreamMetaHost hm{0, n, len, 0, f1 - f0, 0};
     FrontMeta mm;
