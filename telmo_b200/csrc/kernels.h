@@ -53,15 +53,22 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream);
 #ifdef __CUDACC__
 // One value's split-int8 pair: hi = round(x / d) clamped to [-127, 127], lo = round((x - hi d)
 // * 254 / d) clamped; id = 1 / d and id_lo = 254 / d as the row's quantizer computes them.
+// An integral float in [-127, 127] as int8 without the conversion unit: h + 1.5 * 2^23 is exact
+// and its low byte is h in two's complement.
+__device__ __forceinline__ int8_t small_int_to_i8(float h) {
+    return static_cast<int8_t>(__float_as_int(__fadd_rn(h, 12582912.0f)) & 0xff);
+}
+
 __device__ __forceinline__ void quant_split_one(float x, float d, float id, float id_lo, int8_t& h8, int8_t& l8) {
     float h = roundf(__fmul_rn(x, id));
     h = fminf(fmaxf(h, -127.0f), 127.0f);
     const float e = __fmaf_rn(-h, d, x);
     float l = roundf(__fmul_rn(e, id_lo));
     l = fminf(fmaxf(l, -127.0f), 127.0f);
-    h8 = static_cast<int8_t>(h);
-    l8 = static_cast<int8_t>(l);
+    h8 = small_int_to_i8(h);
+    l8 = small_int_to_i8(l);
 }
+
 
 // 2^x and 1/x as the PTX ISA's single approximate instructions (ex2.approx.ftz.f32, relative
 // error about 2^-22; rcp.approx.ftz.f32, within 1 ulp).

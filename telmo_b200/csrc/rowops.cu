@@ -38,8 +38,8 @@ __device__ __forceinline__ void split(float x, float d, float id, float id_lo, s
     const float e = __fmaf_rn(-h, d, x);
     float l = roundf(__fmul_rn(e, id_lo));
     l = fminf(fmaxf(l, -127.0f), 127.0f);
-    h8 = static_cast<signed char>(h);
-    l8 = static_cast<signed char>(l);
+    h8 = small_int_to_i8(h);
+    l8 = small_int_to_i8(l);
 }
 
 struct Scales {
