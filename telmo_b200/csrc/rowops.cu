@@ -215,7 +215,7 @@ __global__ void softmax_quant_kernel(float* __restrict__ x, int m, int n, int64_
 __device__ __forceinline__ float glu_at(const float* __restrict__ big, int64_t row, int cc, int c) {
     const float a = big[row * 2 * cc + c];
     const float b = big[row * 2 * cc + cc + c];
-    return __fdiv_rn(a, __fadd_rn(1.0f, expf(-b)));
+    return mul_sigmoid(a, b);
 }
 
 // GLU + depthwise convolution (taps in order from the bias, skipping frames outside the
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(128) glu_dwconv_silu_kernel(const float* __res
     }
 }
 
-// The same without a window, for other kernel sizes.
+// The same without a window, for other kernel sizes (the same GLU and SiLU arithmetic).
 __global__ void glu_dwconv_silu_any_kernel(const float* __restrict__ big, int cc, int k,
                                            const ConvTask* __restrict__ tasks, const float* __restrict__ w,
                                            const float* __restrict__ bias, float* __restrict__ out) {
@@ -304,7 +304,7 @@ __global__ void glu_dwconv_silu_any_kernel(const float* __restrict__ big, int cc
             if (f >= 0 && f < t.in_len)
                 acc = __fadd_rn(acc, __fmul_rn(__ldg(w + j * cc + c), glu_at(big, t.in_row + f, cc, c)));
         }
-        acc = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+        acc = mul_sigmoid(acc, acc);
         out[static_cast<int64_t>(t.out_row + r) * cc + c] = acc;
     }
 }
@@ -424,24 +424,29 @@ cudaError_t softmax_quant(float* x, int m, int n, int64_t ld, const QuantAct& q,
 cudaError_t glu_dwconv_silu(const float* big, int cc, int k, int stride, const ConvTask* tasks, int n_tasks,
                             const float* w, const float* bias, float* out, cudaStream_t stream) {
     if (n_tasks <= 0) return cudaSuccess;
-    const int threads = 128;
-    dim3 grid((cc + threads - 1) / threads, n_tasks);
-#define TELMO_CONV_CASE(K)                                                                               \
-    case K:                                                                                              \
-        if (stride == 1) glu_dwconv_silu_kernel<K, 1><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out); \
-        else glu_dwconv_silu_kernel<K, 2><<<grid, threads, 0, stream>>>(big, cc, tasks, w, bias, out);         \
-        break;
     if (stride != 1 && stride != 2) return cudaErrorInvalidValue;
-    switch (k) {
-        TELMO_CONV_CASE(3)
-        TELMO_CONV_CASE(5)
-        TELMO_CONV_CASE(7)
-        TELMO_CONV_CASE(9)
-        TELMO_CONV_CASE(15)
-        default: glu_dwconv_silu_any_kernel<<<grid, threads, 0, stream>>>(big, cc, k, tasks, w, bias, out);
-    }
+    const int threads = 128;
+    constexpr int kMaxTasks = 65535;  // tasks run along gridDim.y
+    for (int t0 = 0; t0 < n_tasks; t0 += kMaxTasks) {
+        const ConvTask* tk = tasks + t0;
+        const dim3 grid((cc + threads - 1) / threads, n_tasks - t0 < kMaxTasks ? n_tasks - t0 : kMaxTasks);
+#define TELMO_CONV_CASE(K)                                                                                   \
+    case K:                                                                                                  \
+        if (stride == 1) glu_dwconv_silu_kernel<K, 1><<<grid, threads, 0, stream>>>(big, cc, tk, w, bias, out); \
+        else glu_dwconv_silu_kernel<K, 2><<<grid, threads, 0, stream>>>(big, cc, tk, w, bias, out);         \
+        break;
+        switch (k) {
+            TELMO_CONV_CASE(3)
+            TELMO_CONV_CASE(5)
+            TELMO_CONV_CASE(7)
+            TELMO_CONV_CASE(9)
+            TELMO_CONV_CASE(15)
+            default: glu_dwconv_silu_any_kernel<<<grid, threads, 0, stream>>>(big, cc, k, tk, w, bias, out);
+        }
 #undef TELMO_CONV_CASE
-    return cudaGetLastError();
+        if (cudaError_t e = cudaGetLastError()) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t pool_pairs(const float* x, int d, const int* src_row, int rows, float* out, cudaStream_t stream) {
