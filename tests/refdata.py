@@ -2,8 +2,8 @@
 
 The reference keeps golden feature tensors for its front ends beside LibriSpeech and FLEURS
 clips (tests/goldens/<model>/ in the telmo source tree). They are read in place when a copy of
-the reference source is present (``TELMO_REFERENCE`` or /root/reference); the clips are never
-copied into this repository.
+the reference source is present (at ``TELMO_REFERENCE``, else at REFERENCE's default below); the
+clips are never copied into this repository.
 """
 
 from __future__ import annotations
