@@ -30,18 +30,6 @@ __device__ __forceinline__ double warp_sum(double v) {
     return v;
 }
 
-// The split-int8 rule (quantize_x2 in quant.cu) for one value.
-__device__ __forceinline__ void split(float x, float d, float id, float id_lo, signed char& h8,
-                                      signed char& l8) {
-    float h = roundf(__fmul_rn(x, id));
-    h = fminf(fmaxf(h, -127.0f), 127.0f);
-    const float e = __fmaf_rn(-h, d, x);
-    float l = roundf(__fmul_rn(e, id_lo));
-    l = fminf(fmaxf(l, -127.0f), 127.0f);
-    h8 = small_int_to_i8(h);
-    l8 = small_int_to_i8(l);
-}
-
 struct Scales {
     float d, id, id_lo;
 };
@@ -130,10 +118,10 @@ __device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int off, int
     for (int c = 0; c < C; ++c) {
         const int i = off + (c * 32 + lane) * 4;
         char4 h, l;
-        split(v[c].x, s.d, s.id, s.id_lo, h.x, l.x);
-        split(v[c].y, s.d, s.id, s.id_lo, h.y, l.y);
-        split(v[c].z, s.d, s.id, s.id_lo, h.z, l.z);
-        split(v[c].w, s.d, s.id, s.id_lo, h.w, l.w);
+        quant_split_one(v[c].x, s.d, s.id, s.id_lo, h.x, l.x);
+        quant_split_one(v[c].y, s.d, s.id, s.id_lo, h.y, l.y);
+        quant_split_one(v[c].z, s.d, s.id, s.id_lo, h.z, l.z);
+        quant_split_one(v[c].w, s.d, s.id, s.id_lo, h.w, l.w);
         *reinterpret_cast<char4*>(hi + i) = h;
         *reinterpret_cast<char4*>(lo + i) = l;
     }
@@ -204,7 +192,7 @@ __global__ void softmax_quant_kernel(float* __restrict__ x, int m, int n, int64_
     int8_t* lr = q.lo + static_cast<int64_t>(row) * q.ld;
     for (int i = lane; i < n; i += 32) {
         signed char h, l;
-        split(xr[i], s.d, s.id, s.id_lo, h, l);
+        quant_split_one(xr[i], s.d, s.id, s.id_lo, h, l);
         hr[i] = h;
         lr[i] = l;
     }
