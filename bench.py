@@ -564,6 +564,9 @@ def run_ours(args, rank, world, local_rank):
             peak = pk["bf16_tflops_sustained"]
             roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                        "traffic_note": "null: achieved averages launches of every product shape; "
+                        "for the FF up-projection alone ncu counts 922 MB of DRAM traffic against "
+                        "980 MB algorithmic (profiles/gemm_i8x2_ff_up_launch.md)",
                         "kernel": "gemm_i8x2_kernel (split-int8 tcgen05 linear)",
                         "ops_per_launch": ops_launch, "avg_launch_us": round(avg * 1e6, 2),
                         "peak_source": pk_src + ": bf16_tflops_sustained; the split-int8 "
