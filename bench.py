@@ -185,15 +185,15 @@ class GraniteWorkload:
         self.dev_tokens = torch.empty(3 * frames + 3, dtype=torch.int32, device="cuda")
         self.dev_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32,
                                       device="cuda")
-        self.host_tokens = torch.empty(3 * frames + 3, dtype=torch.int32).pin_memory()
-        self.host_counts = torch.empty(max(len(b) for b in self.batches) + 1, dtype=torch.int32).pin_memory()
         self.bi = int(packed.nbytes)
         self.bo = 0
-        # End to end: two device audio buffers, so the next batch's host-to-device copy (on its
-        # own stream) runs while the current batch is transcribed.
-        biggest = max(n for _, n in self.offsets)
-        self.e2e_audio = [torch.empty(biggest, dtype=torch.float32, device="cuda") for _ in range(2)]
-        self.copy_stream = torch.cuda.Stream()
+        # End to end: the whole shard in one telmo_granite_transcribe call with host buffers; it
+        # transcribes in groups of batch_seconds (the same cut as self.batches, since self.mine is
+        # length-sorted) and copies each group's audio up while the previous group runs.
+        self.model.set_transcribe_group(self.batch_seconds)
+        self.mine_lengths = np.ascontiguousarray(self.samples[self.mine], dtype=np.int64)
+        all_frames = sum(self.model.frames_for_samples(int(x)) for x in self.mine_lengths)
+        self.host_tokens_all = torch.empty(3 * all_frames + 3, dtype=torch.int32).pin_memory()
 
     def step_gpu(self):
         for b, (at, n) in zip(self.batches, self.offsets):
@@ -201,37 +201,13 @@ class GraniteWorkload:
                                          self.dev_tokens, self.dev_counts)
 
     def step_e2e(self):
-        """Every batch through telmo_granite_transcribe_device with its audio copied from pinned
-        host memory and its tokens and counts copied back; batch i + 1's audio copy overlaps
-        batch i's transcription."""
-        import torch
-        main = torch.cuda.current_stream()
-        copied = [torch.cuda.Event(), torch.cuda.Event()]
-        free = [torch.cuda.Event(), torch.cuda.Event()]
-
-        def copy_in(i):
-            at, n = self.offsets[i]
-            with torch.cuda.stream(self.copy_stream):
-                if i >= 2:
-                    self.copy_stream.wait_event(free[i % 2])
-                self.e2e_audio[i % 2][:n].copy_(self.host_audio[at:at + n], non_blocking=True)
-                copied[i % 2].record(self.copy_stream)
-
-        bo = 0
-        copy_in(0)
-        for i, b in enumerate(self.batches):
-            n = self.offsets[i][1]
-            main.wait_event(copied[i % 2])
-            if i + 1 < len(self.batches):
-                copy_in(i + 1)
-            frames = self.model.transcribe_device(self.e2e_audio[i % 2][:n], self.samples[b],
-                                                  self.dev_tokens, self.dev_counts)
-            free[i % 2].record(main)
-            nt = 3 * int(frames.sum())
-            self.host_tokens[:nt].copy_(self.dev_tokens[:nt], non_blocking=True)
-            self.host_counts[:len(b)].copy_(self.dev_counts[:len(b)], non_blocking=True)
-            bo += 4 * nt + 4 * len(b)
-        self.bo = bo
+        """The shard through telmo_granite_transcribe, the host-buffer entry point: pinned host
+        audio in, host tokens, counts and frames out, every copy inside the call."""
+        if not self.mine:
+            return
+        _, counts, frames = self.model.transcribe_arrays(self.host_audio, self.mine_lengths,
+                                                         tokens_buf=self.host_tokens_all)
+        self.bo = 12 * int(frames.sum()) + 4 * int(counts.size)
 
     def units_per_step(self):
         return self.rank_seconds
@@ -261,17 +237,18 @@ class GraniteWorkload:
     PROFILE = "telmo_granite_profile"
 
     # -- CPU reference ------------------------------------------------------------------------
-    def cpu_sample_utts(self, target_s=24.0):
-        """A bounded sample of the workload for the CPU path: the first utterances of the set
-        (in input order) up to about target_s seconds."""
-        chosen, acc = [], 0.0
-        for u in range(self.n_utt):
-            s = self.samples[u] / SR
-            if acc + s > target_s and chosen:
-                break
-            chosen.append(u)
-            acc += s
-        return chosen, acc
+    CPU_SAMPLE_SECONDS = 240.0
+
+    def cpu_sample_utts(self, target_s=None):
+        """A bounded sample of the workload for the CPU path, spread over its length
+        distribution: with the set's utterances sorted by length, the ones at evenly spaced
+        quantiles (i + 1/2) / n, n chosen so the sample holds about target_s seconds."""
+        target_s = target_s or self.CPU_SAMPLE_SECONDS
+        order = np.argsort(self.samples, kind="stable")
+        mean = float(self.samples.mean()) / SR
+        n = int(min(len(order), max(1, round(target_s / mean))))
+        chosen = [int(order[int((i + 0.5) * len(order) / n)]) for i in range(n)]
+        return chosen, float(self.samples[chosen].sum()) / SR
 
     def cpu_setup(self):
         from oracle import oracle
@@ -296,8 +273,9 @@ class GraniteWorkload:
         t0 = time.perf_counter()
         self.cpu_step(threads)
         dt = time.perf_counter() - t0
-        return self.cpu_seconds / dt, (f"{len(self.cpu_utts)} utterances of the set "
-                                       f"({self.cpu_seconds:.1f} s of audio), features -> tokens")
+        return self.cpu_seconds / dt, (f"{len(self.cpu_utts)} utterances at evenly spaced length "
+                                       f"quantiles of the set ({self.cpu_seconds:.1f} s of audio), "
+                                       f"audio -> tokens")
 
 
 # ---------------------------------------------------------------------------------------------
@@ -309,6 +287,7 @@ class ParakeetWorkload(GraniteWorkload):
               "16 kHz audio -> log-mel -> 8x conv subsampling -> 24-layer FastConformer -> "
               "greedy TDT tokens and durations")
     PROFILE = "telmo_parakeet_profile"
+    CPU_SAMPLE_SECONDS = 150.0
 
     # The whole set (about 4,240 s) fits one batch: every matrix product runs over all frames.
     def __init__(self, rank, world, n_utt=256, batch_seconds=4500.0, precision="int8"):
@@ -448,6 +427,9 @@ class LinearWorkload:
     def between_steps(self):
         self.flush.zero_()
 
+    def algorithmic_bytes(self):
+        return 4 * self.m * self.k + self.n * self.k + 8 * self.n + 4 * self.m * self.n
+
     def units_per_step(self):
         return self.ops / 1e12
 
@@ -485,6 +467,17 @@ def make_workload(args, rank, world):
     return LinearWorkload(rank, world, shape=shape, precision=args.precision)
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import telmo_b200
@@ -510,6 +503,7 @@ def run_ours(args, rank, world, local_rank):
         wl.step_gpu()
         if hasattr(wl, "between_steps"):
             wl.between_steps()
+    wl.step_e2e()  # the host-buffer path's own buffers are allocated before timing
     ctx.check()
     if speech:
         wl.profile_start()
@@ -546,39 +540,55 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     ctx.check()
     e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_start, e_end))
-    t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device="cuda")
-    units = torch.tensor([wl.units_per_step()], dtype=torch.float64, device="cuda")
+    # Every rank's own figures (device busy time of the timed steps, its share of the work), then
+    # the whole job's: its time is the slowest rank's.
+    mine = torch.tensor([step_ms, e2e_ms, wl.units_per_step(),
+                         float(len(getattr(wl, "batches", [None])))], dtype=torch.float64, device="cuda")
     if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(units, op=dist.ReduceOp.SUM)
-    step_ms, e2e_ms = t.tolist()
-    total_units = units.item()
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+    else:
+        every = [mine]
+    every = [t.tolist() for t in every]
+    step_ms = max(r[0] for r in every)
+    e2e_ms = max(r[1] for r in every)
+    total_units = sum(r[2] for r in every)
     if rank == 0:
         pk, pk_src = peaks()
         value = total_units * args.steps / (step_ms / 1e3)
         e2e_value = total_units * args.steps / (e2e_ms / 1e3)
         if speech:
+            own_ms = every[0][0]  # the profile is rank 0's
             avg = prof["gemm_ms"] / max(prof["gemm_n"], 1) / 1e3
             ops_launch = prof["ops"] / max(prof["gemm_n"], 1)
             achieved = ops_launch / avg / 1e12
             peak = pk["bf16_tflops_sustained"]
             roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
-                        "traffic_note": "null: achieved averages launches of every product shape; "
-                        "for the FF up-projection alone ncu counts 922 MB of DRAM traffic against "
-                        "980 MB algorithmic (profiles/gemm_i8x2_ff_up_launch.md)",
+                        "traffic_note": "null: achieved averages launches of every product shape, "
+                        "which no single ncu capture covers; a capture of the feed-forward "
+                        "up-projection alone counts DRAM bytes below its algorithmic bytes",
                         "kernel": "gemm_i8x2_kernel (split-int8 tcgen05 linear)",
                         "ops_per_launch": ops_launch, "avg_launch_us": round(avg * 1e6, 2),
                         "peak_source": pk_src + ": bf16_tflops_sustained; the split-int8 "
                         "product issues two int8 MMAs per multiply-add, so its tensor ceiling "
                         "is the bf16 one",
-                        "time_share": {"gemm": round(prof["gemm_ms"] / step_ms, 3),
-                                       "attention": round(prof["attn_ms"] / step_ms, 3),
-                                       "row_kernels_timed": round(prof["rows_ms"] / step_ms, 3),
-                                       "front_end": round(prof["fe_ms"] / step_ms, 3)}}
+                        "time_share": {"gemm": round(prof["gemm_ms"] / own_ms, 3),
+                                       "attention": round(prof["attn_ms"] / own_ms, 3),
+                                       "row_kernels_timed": round(prof["rows_ms"] / own_ms, 3),
+                                       "front_end": round(prof["fe_ms"] / own_ms, 3)}}
         else:
-            roofline = {"bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                        "frac": None, "traffic": None, "peak_source": pk_src}
+            # One telmo_linear call (split quantization of A, then the tcgen05 product) against
+            # its algorithmic bytes: A f32 read, W int8 read, scales and bias read, C f32 written.
+            per_call_s = (every[0][0] / args.steps) / 1e3
+            alg = wl.algorithmic_bytes()
+            achieved = alg / per_call_s / 1e9
+            roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                        "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                        "algorithmic_bytes": alg, "avg_launch_us": round(per_call_s * 1e6, 2),
+                        "kernel": "telmo_linear: quantize_x2_regs_kernel + gemm_i8x2_kernel, timed "
+                                  "together as one call",
+                        "peak_source": pk_src + ": hbm_gbs"}
         cpu_value, cpu_sample = wl.cpu_sample(os.cpu_count() or 1)
         line = {
             "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
@@ -592,9 +602,14 @@ def run_ours(args, rank, world, local_rank):
                     "h2d_bytes_per_step": int(wl.bi), "d2h_bytes_per_step": int(wl.bo)},
             "roofline": roofline,
             "cpu_baseline": {"value": round(cpu_value, 3), "unit": wl.unit,
-                             "cores": os.cpu_count(), "kind": "port", "sample": cpu_sample},
+                             "cores": os.cpu_count(), "cpu_model": cpu_model(), "kind": "port",
+                             "sample": cpu_sample},
             "clocks": clk,
             "gpu_launches": int(launches),
+            "per_rank": [{"rank": r, "ms_per_step": round(v[0] / args.steps, 3),
+                          "e2e_ms_per_step": round(v[1] / args.steps, 3),
+                          "units_per_step": round(v[2], 3), "batches": int(v[3])}
+                         for r, v in enumerate(every)],
         }
         print(json.dumps(line), flush=True)
     if dist:
@@ -612,8 +627,8 @@ def run_reference(args, rank, world):
         wl.cpu_setup()
         per_step = wl.cpu_seconds
         sample = (f"the oracle's C restatement of telmo's CPU path (reference Rust not "
-                  f"buildable here): {len(wl.cpu_utts)} utterances of the set "
-                  f"({wl.cpu_seconds:.1f} s of audio) per step, features -> tokens")
+                  f"buildable here): {len(wl.cpu_utts)} utterances at evenly spaced length "
+                  f"quantiles of the set ({wl.cpu_seconds:.1f} s of audio) per step, audio -> tokens")
     else:
         per_step = wl.units_per_step()
         sample = "the oracle's C restatement, full config-1 product per step"
@@ -634,7 +649,7 @@ def run_reference(args, rank, world):
         "data": "synthetic (seeded; telmo_b200/synthetic.py), random-init weights",
         "config": wl.config(world),
         "cpu_baseline": {"value": round(value, 3), "unit": wl.unit, "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "cpu_model": cpu_model(), "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": wl.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -221,9 +221,16 @@ size_t telmo_granite_frames_for_samples(const telmo_granite *g, int64_t samples)
  * each utterance's encoder frame count F[u]; tokens (host) receives utterance u's tokens as
  * (id, frame, duration) triples starting at element 3 * (F[0] + ... + F[u-1]) -- size it for
  * 3 * sum of telmo_granite_frames_for_samples(lengths[u]) -- and counts (host, n_utt) their
- * numbers. */
+ * numbers. The utterances run in groups of consecutive utterances with at most the transcribe
+ * group's audio (2048 s unless set below; ceil(total / group) groups of about equal audio, an
+ * utterance longer than a group alone in its own): while one group is transcribed on `stream`,
+ * the next group's samples go up on the model's own copy stream (staged through pinned memory
+ * when `samples` is pageable), and each group's tokens come back behind it. Returns once the
+ * tokens, counts and frames are in host memory. */
 int telmo_granite_transcribe(telmo_granite *g, const float *samples, const int64_t *lengths,
                              int n_utt, uint32_t *tokens, int *counts, int *frames, void *stream);
+/* The audio per group of telmo_granite_transcribe, in seconds (at least 0.02). */
+int telmo_granite_set_transcribe_group(telmo_granite *g, double seconds);
 /* The same with samples, tokens and counts in device memory (lengths and frames on the host). */
 int telmo_granite_transcribe_device(telmo_granite *g, const float *samples,
                                     const int64_t *lengths, int n_utt, uint32_t *tokens,

@@ -204,6 +204,11 @@ long oracle_parakeet_encode(const oracle_parakeet *p, const float *features, siz
  * token or duration choice. Returns the token count. */
 size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, size_t frames,
                               uint32_t *tokens, float *min_margin, int threads);
+/* As oracle_parakeet_decode; sure receives the number of tokens emitted before the first step
+ * whose top-2 gap is at or below threshold (all of them when no step is). */
+size_t oracle_parakeet_decode_sure(const oracle_parakeet *p, const float *encoded, size_t frames,
+                                   uint32_t *tokens, float *min_margin, float threshold,
+                                   size_t *sure, int threads);
 /* The networks the biased beam search reads (src/parakeet.rs:1641-1676): the joint's projection
  * of encoder frames [frames, h]; the joint's outputs [rows, vocab + durations] for prediction
  * rows at one projected frame; predict_rows for one token per row, states [rows][layers][2][h]

@@ -510,6 +510,10 @@ def _parakeet_lib():
     L.oracle_parakeet_decode.restype = _sz
     L.oracle_parakeet_decode.argtypes = [ctypes.c_void_p, _f32p, _sz, _u32p,
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+    L.oracle_parakeet_decode_sure.restype = _sz
+    L.oracle_parakeet_decode_sure.argtypes = [ctypes.c_void_p, _f32p, _sz, _u32p,
+                                              ctypes.POINTER(ctypes.c_float), ctypes.c_float,
+                                              ctypes.POINTER(_sz), ctypes.c_int]
     L.oracle_tdt_step.restype = ctypes.c_int
     L.oracle_tdt_step.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                   ctypes.c_int, ctypes.c_int, ctypes.POINTER(_sz),
@@ -599,6 +603,21 @@ class Parakeet:
         n = _parakeet_lib().oracle_parakeet_decode(self._h, e.reshape(-1), frames, out,
                                                    ctypes.byref(margin), threads)
         return [tuple(int(v) for v in out[3 * i:3 * i + 3]) for i in range(n)], margin.value
+
+    def decode_sure(self, encoded, threshold=1e-2, threads=1):
+        """Greedy TDT: ([(id, frame, duration), ...], sure), where the first ``sure`` tokens were
+        emitted before any joint step whose top-2 logit gap (token or duration) is at or below
+        ``threshold``: the prefix a decoder whose logits are that close must reproduce."""
+        e = _c(encoded, np.float32)
+        frames = e.shape[0]
+        cap = frames * (self.config["max_symbols"] + 1) + 1
+        out = np.zeros(3 * cap, np.uint32)
+        margin = ctypes.c_float()
+        sure = _sz()
+        n = _parakeet_lib().oracle_parakeet_decode_sure(self._h, e.reshape(-1), frames, out,
+                                                        ctypes.byref(margin), threshold,
+                                                        ctypes.byref(sure), threads)
+        return [tuple(int(v) for v in out[3 * i:3 * i + 3]) for i in range(n)], int(sure.value)
 
     # The networks the biased beam search reads (src/parakeet.rs:1641-1676).
     def enc_proj(self, encoded, threads=1):

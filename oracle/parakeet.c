@@ -458,12 +458,16 @@ int oracle_tdt_step(const float *logits, int vocab, int blank, const int *durati
     return 1;
 }
 
-size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, size_t frames,
-                              uint32_t *tokens, float *min_margin, int threads)
+size_t oracle_parakeet_decode_sure(const oracle_parakeet *p, const float *encoded, size_t frames,
+                                   uint32_t *tokens, float *min_margin, float threshold,
+                                   size_t *sure, int threads)
 {
     /* Parakeet::decode / decode_inner greedy TDT (src/parakeet.rs:1285-1296, :1412-1513).
      * min_margin (may be NULL) receives the smallest top-2 logit gap of any joint step's token
-     * or duration choice; returns the number of tokens. */
+     * or duration choice; sure (may be NULL) the number of tokens emitted before the first step
+     * whose gap is at or below threshold (every token when no step is), the prefix that any
+     * decoder whose logits differ by less than the threshold must reproduce; returns the number
+     * of tokens. */
     const oracle_parakeet_config *c = &p->c;
     size_t h = (size_t)c->pred_hidden, d = pp_d(p);
     size_t vocab = (size_t)c->vocab, outputs = vocab + (size_t)c->n_durations;
@@ -479,6 +483,8 @@ size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, si
     size_t t = 0, count = 0;
     int on_frame = 0;
     float worst = INFINITY;
+    int unsure = 0;
+    size_t sure_count = 0;
     while (t < frames) {
         for (size_t j = 0; j < h; j++) z[j] = fmaxf(enc_proj[t * h + j] + pred[j], 0.0f);
         plinear(&p->joint, z, 1, logits, p->joint_b.p, ORACLE_ACT_NONE, 1.0f, 0, threads);
@@ -488,6 +494,10 @@ size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, si
             if (v != token) worst = fminf(worst, logits[token] - logits[v]);
         for (size_t v = 0; v < (size_t)c->n_durations; v++)
             if (v != di) worst = fminf(worst, logits[vocab + di] - logits[vocab + v]);
+        if (!unsure && worst <= threshold) {
+            unsure = 1;
+            sure_count = count;
+        }
         if (oracle_tdt_step(logits, c->vocab, c->blank, c->durations, c->n_durations,
                             c->max_symbols, &t, &on_frame, tokens + 3 * count)) {
             count++;
@@ -495,6 +505,13 @@ size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, si
         }
     }
     if (min_margin) *min_margin = worst;
+    if (sure) *sure = unsure ? sure_count : count;
     free(state); free(pred); free(enc_proj); free(z); free(logits);
     return count;
+}
+
+size_t oracle_parakeet_decode(const oracle_parakeet *p, const float *encoded, size_t frames,
+                              uint32_t *tokens, float *min_margin, int threads)
+{
+    return oracle_parakeet_decode_sure(p, encoded, frames, tokens, min_margin, 0.0f, NULL, threads);
 }

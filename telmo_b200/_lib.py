@@ -18,6 +18,11 @@ TELMO_ERR_DEVICE_TIMEOUT = -3
 TELMO_ERR_UNSUPPORTED = -4
 TELMO_ERR_MODEL = -5
 
+# Output element types of telmo_linear (TELMO_DTYPE_*).
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+DTYPE_I32_PAIR = 2
+
 # Weight precisions (include/telmo_b200.h, telmo's Precision).
 PRECISIONS = {"f32": 0, "f16": 1, "bf16": 2, "int8": 3, "q8_0": 4}
 
@@ -69,6 +74,7 @@ SIGNATURES = {
     "telmo_granite_frames_for_samples": (_sz, [_vp, _c.c_int64]),
     "telmo_granite_transcribe": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "telmo_granite_transcribe_device": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "telmo_granite_set_transcribe_group": (_int, [_vp, _c.c_double]),
     "telmo_granite_launches": (_c.c_long, [_vp]),
     "telmo_pack_open": (_c.c_int, [_c.c_char_p, _vp]),
     "telmo_pack_from_bytes": (_c.c_int, [_c.c_char_p, _sz, _vp]),

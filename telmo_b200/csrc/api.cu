@@ -54,6 +54,40 @@ void* Ctx::workspace(size_t bytes, cudaStream_t stream) {
     return ws;
 }
 
+cudaError_t PinnedRing::upload(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+    if (bytes == 0) return cudaSuccess;
+    Slot& sl = slot[next];
+    next = (next + 1) % kSlots;
+    cudaError_t e = cudaSuccess;
+    if (sl.done) {
+        e = cudaEventSynchronize(sl.done);  // the slot's previous copy has read it
+    } else {
+        e = cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return e;
+    if (bytes > sl.cap) {
+        if (sl.buf) cudaFreeHost(sl.buf);
+        sl.buf = nullptr;
+        sl.cap = 0;
+        const size_t want = std::max<size_t>(bytes + bytes / 4, 64 << 10);
+        if ((e = cudaHostAlloc(&sl.buf, want, cudaHostAllocDefault)) != cudaSuccess) return e;
+        sl.cap = want;
+    }
+    std::memcpy(sl.buf, src, bytes);
+    if ((e = cudaMemcpyAsync(dst, sl.buf, bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess) return e;
+    return cudaEventRecord(sl.done, s);
+}
+
+PinnedRing::~PinnedRing() {
+    for (Slot& sl : slot) {
+        if (sl.done) {
+            cudaEventSynchronize(sl.done);
+            cudaEventDestroy(sl.done);
+        }
+        if (sl.buf) cudaFreeHost(sl.buf);
+    }
+}
+
 }  // namespace telmo
 
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -322,6 +356,12 @@ extern "C" int telmo_quantize_x2(telmo_ctx* c, const float* a, size_t lda, size_
     if (!a || !hi || !lo || !scale || k == 0 || lda < k || ldq < k || ldq % 16 || m > (1u << 30))
         return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_quantize_x2: bad arguments (m=%zu k=%zu lda=%zu ldq=%zu)",
                          m, k, lda, ldq);
+    // The kernels store the levels four bytes at a time and the product reads them through
+    // tensor maps, which need 16-byte aligned rows.
+    const auto misaligned = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) != 0; };
+    if (misaligned(hi, 16) || misaligned(lo, 16) || misaligned(scale, 4) || misaligned(a, 4))
+        return ctx->fail(TELMO_ERR_ARGUMENT,
+                         "telmo_quantize_x2: hi and lo must be 16-byte aligned, a and scale 4-byte aligned");
     if (int rc = ctx->use_device()) return rc;
     QuantAct q;
     q.hi = hi;

@@ -16,6 +16,25 @@ namespace telmo {
 
 struct FrontEnd;
 
+// Pinned host staging for the small host-to-device uploads a call makes (task lists, batch
+// layouts): the copy runs asynchronously from page-locked memory, so the host need not wait for
+// the stream before its source vector goes out of scope. A slot is reused only after the event
+// recorded behind its last copy has completed; with several slots the host can run a few
+// batches ahead of the device.
+struct PinnedRing {
+    static constexpr int kSlots = 8;
+    struct Slot {
+        void* buf = nullptr;
+        size_t cap = 0;
+        cudaEvent_t done = nullptr;
+    } slot[kSlots];
+    int next = 0;
+
+    // Copies `bytes` from host `src` to device `dst` in stream order on `s`.
+    cudaError_t upload(void* dst, const void* src, size_t bytes, cudaStream_t s);
+    ~PinnedRing();
+};
+
 struct Ctx {
     FrontEnd* granite_fe = nullptr;   // created on first use
     FrontEnd* parakeet_fe = nullptr;
@@ -24,6 +43,7 @@ struct Ctx {
     uint32_t* error_word = nullptr;  // device error word the kernels record into
     void* ws = nullptr;              // growable workspace for telmo_linear's quantized operand
     size_t ws_bytes = 0;
+    PinnedRing uploads;              // the calls' small host-to-device uploads
     std::string last_error;
 
     int fail(int code, const char* fmt, ...);

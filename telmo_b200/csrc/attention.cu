@@ -194,14 +194,14 @@ cudaError_t launch_attention(const float* qkv, int heads, int ctx, const AttnTas
                              const int8_t* rel_w, int64_t ld_rel, const float* rel_scale, float scale,
                              float* att, cudaStream_t stream) {
     const int smem = static_cast<int>(sizeof(AttnSmem<HD>));
-    static uint64_t configured = 0;
+    static DeviceOnce configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !(configured >> dev & 1)) {
+    if (!configured.done(dev)) {
         cudaError_t e = cudaFuncSetAttribute(granite_attention_kernel<HD>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev < 64) configured |= uint64_t(1) << dev;
+        configured.mark(dev);
     }
     dim3 grid(n_tasks, heads);
     granite_attention_kernel<HD><<<grid, 256, smem, stream>>>(qkv, heads, ctx, tasks, rel_w, ld_rel, rel_scale,

@@ -248,14 +248,14 @@ template <int HD>
 cudaError_t launch(const __half* qkv, int64_t plane, int heads, int ctx, const AttnTask* tasks, int n_tasks,
                    const __half* rel16, const float* rel_scale, float scale, float* att, cudaStream_t stream) {
     const int smem = static_cast<int>(sizeof(MmaSmem<HD>));
-    static uint64_t configured = 0;
+    static DeviceOnce configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !(configured >> dev & 1)) {
+    if (!configured.done(dev)) {
         cudaError_t e = cudaFuncSetAttribute(granite_attention_mma_kernel<HD>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev < 64) configured |= uint64_t(1) << dev;
+        configured.mark(dev);
     }
     dim3 grid(n_tasks, heads);
     granite_attention_mma_kernel<HD><<<grid, 256, smem, stream>>>(qkv, plane, heads, ctx, tasks, rel16, rel_scale,

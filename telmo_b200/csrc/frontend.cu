@@ -509,6 +509,7 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
     }
     const size_t meta_bytes = sizeof(int64_t) * longs.size() + sizeof(int) * ints.size() + sizeof(float) * n_utt;
     if (meta_bytes > meta_cap) {
+        cudaDeviceSynchronize();  // queued batches may still read the old buffers
         if (meta_dev) cudaFree(meta_dev);
         meta_dev = nullptr;
         meta_cap = 0;
@@ -517,6 +518,7 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
     }
     const size_t log_bytes = static_cast<size_t>(total_frames) * n_mels * (kind == kGranite ? sizeof(float) : sizeof(double));
     if (log_bytes > scratch_cap) {
+        cudaDeviceSynchronize();
         if (scratch) cudaFree(scratch);
         scratch = nullptr;
         scratch_cap = 0;
@@ -527,10 +529,9 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
     int64_t* dl = reinterpret_cast<int64_t*>(m);
     int* di = reinterpret_cast<int*>(m + sizeof(int64_t) * longs.size());
     float* peak = reinterpret_cast<float*>(di + ints.size());
-    if (int rc = ctx->cuda(cudaMemcpyAsync(dl, longs.data(), sizeof(int64_t) * longs.size(), cudaMemcpyHostToDevice, s), "meta"))
-        return rc;
-    if (int rc = ctx->cuda(cudaMemcpyAsync(di, ints.data(), sizeof(int) * ints.size(), cudaMemcpyHostToDevice, s), "meta"))
-        return rc;
+    // Through pinned staging: the copies are asynchronous and the host vectors may go out of scope.
+    if (int rc = ctx->cuda(ctx->uploads.upload(dl, longs.data(), sizeof(int64_t) * longs.size(), s), "meta")) return rc;
+    if (int rc = ctx->cuda(ctx->uploads.upload(di, ints.data(), sizeof(int) * ints.size(), s), "meta")) return rc;
     FrontMeta meta;
     meta.n_utt = n_utt;
     meta.frame_first = di;
@@ -554,9 +555,7 @@ int FrontEnd::run(const float* samples_dev, const int64_t* lengths, int n_utt, f
         parakeet_normalize_kernel<<<grid, 256, 0, s>>>(logs, meta, n_mels, features);
         launches += 2;
     }
-    if (int rc = ctx->cuda(cudaGetLastError(), "front end")) return rc;
-    // The host vectors must outlive the asynchronous copies.
-    return ctx->cuda(cudaStreamSynchronize(s), "front end");
+    return ctx->cuda(cudaGetLastError(), "front end");
 }
 
 // ---- the Granite front end over part of one utterance (GraniteStream) ------------------------

@@ -573,14 +573,16 @@ bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t 
 }  // namespace
 
 int num_sms() {
-    static int sms = 0;
-    if (!sms) {
+    static std::atomic<int> sms{0};
+    int n = sms.load(std::memory_order_relaxed);
+    if (!n) {
         int dev = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+        sms.store(n, std::memory_order_relaxed);
     }
-    return sms;
+    return n;
 }
 
 cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
@@ -594,10 +596,10 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
     const bool two_level = w.lo_values != nullptr;
     if (two_level ? !make_map(&mwl, w.lo_values, w.n, w.k, w.ld) : false) return cudaErrorInvalidValue;
     if (!two_level) mwl = mw;  // not read
-    static uint64_t configured = 0;  // one bit per device
+    static DeviceOnce configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !(configured >> dev & 1)) {
+    if (!configured.done(dev)) {
         cudaError_t e = cudaFuncSetAttribute(gemm_i8x2_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Shape<1>::kSmemBytes);
         if (e == cudaSuccess)
@@ -607,7 +609,7 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream) {
             e = cudaFuncSetAttribute(gemm_i8x2_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Shape<1, true>::kSmemBytes);
         if (e != cudaSuccess) return e;
-        if (dev < 64) configured |= uint64_t(1) << dev;
+        configured.mark(dev);
     }
     // The output goes through TMA when its rows are 16-byte aligned.
     CUtensorMap mo, mo_lo;

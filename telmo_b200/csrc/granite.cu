@@ -46,7 +46,192 @@ Granite::~Granite() {
     }
     release_buffers();
     release_e2e();
+    release_pipeline();
     if (audio_dev) cudaFree(audio_dev);
+}
+
+void Granite::release_pipeline() {
+    if (copy_stream) cudaStreamSynchronize(copy_stream);
+    for (int b = 0; b < 2; ++b) {
+        if (group_audio[b]) cudaFree(group_audio[b]);
+        if (group_pinned[b]) cudaFreeHost(group_pinned[b]);
+        if (group_copied[b]) cudaEventDestroy(group_copied[b]);
+        if (group_read[b]) cudaEventDestroy(group_read[b]);
+        group_audio[b] = group_pinned[b] = nullptr;
+        group_copied[b] = group_read[b] = nullptr;
+    }
+    group_audio_cap = group_pinned_cap = 0;
+    if (tokens_pinned) cudaFreeHost(tokens_pinned);
+    if (counts_pinned) cudaFreeHost(counts_pinned);
+    tokens_pinned = nullptr;
+    counts_pinned = nullptr;
+    tokens_pinned_cap = counts_pinned_cap = 0;
+    if (copy_stream) cudaStreamDestroy(copy_stream);
+    copy_stream = nullptr;
+}
+
+namespace {
+
+bool host_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// Splits utterances 0..n-1, in order, into ceil(total / limit) groups of about equal samples (an
+// utterance longer than the limit alone in its group). Returns the first utterance of each group
+// and, last, n.
+std::vector<int> balanced_groups(const int64_t* lengths, int n, int64_t limit) {
+    int64_t total = 0;
+    for (int u = 0; u < n; ++u) total += lengths[u];
+    const int64_t groups = std::max<int64_t>(1, (total + limit - 1) / limit);
+    std::vector<int> first{0};
+    int64_t acc = 0, in_group = 0, g = 1;
+    for (int u = 0; u < n; ++u) {
+        if (u > first.back() && (in_group + lengths[u] > limit || acc >= g * total / groups)) {
+            first.push_back(u);
+            ++g;
+            in_group = 0;
+        }
+        acc += lengths[u];
+        in_group += lengths[u];
+    }
+    first.push_back(n);
+    return first;
+}
+
+}  // namespace
+
+int Granite::transcribe_host(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
+                             int* frames, cudaStream_t s) {
+    const std::vector<int> first = balanced_groups(lengths, n_utt, group_samples);
+    const int groups = static_cast<int>(first.size()) - 1;
+    std::vector<int64_t> at(groups + 1, 0);  // first sample of each group
+    int64_t biggest = 0, total_frames = 0, most_rows = 0, most_frames = 0;
+    int most_utts = 0;
+    for (int g = 0; g < groups; ++g) {
+        int64_t n = 0, rows = 0, frames_g = 0;
+        for (int u = first[g]; u < first[g + 1]; ++u) {
+            n += lengths[u];
+            const size_t r = telmo_logmel_rows(TELMO_FRONTEND_GRANITE, lengths[u]);
+            rows += static_cast<int64_t>(r);
+            frames_g += static_cast<int64_t>(telmo_granite_frames_for(reinterpret_cast<telmo_granite*>(this), r));
+        }
+        at[g + 1] = at[g] + n;
+        biggest = std::max(biggest, n);
+        most_rows = std::max(most_rows, rows);
+        most_frames = std::max(most_frames, frames_g);
+        most_utts = std::max(most_utts, first[g + 1] - first[g]);
+        total_frames += frames_g;
+    }
+    if (most_rows > (1 << 30)) return ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: group too large");
+    // The device token buffers every group writes must exist before the first group is queued.
+    if (int rc = ensure_e2e(static_cast<int>(most_rows) + 1, static_cast<int>(most_frames) + 1, most_utts)) return rc;
+    const bool pinned_in = host_pinned(samples);
+    const bool pinned_tokens = host_pinned(tokens), pinned_counts = host_pinned(counts);
+    if (!copy_stream && cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return ctx->fail(TELMO_ERR_CUDA, "transcribe: cannot create the copy stream");
+    for (int b = 0; b < 2; ++b) {
+        if (!group_copied[b] && cudaEventCreateWithFlags(&group_copied[b], cudaEventDisableTiming) != cudaSuccess)
+            return ctx->fail(TELMO_ERR_CUDA, "transcribe: cannot create events");
+        if (!group_read[b] && cudaEventCreateWithFlags(&group_read[b], cudaEventDisableTiming) != cudaSuccess)
+            return ctx->fail(TELMO_ERR_CUDA, "transcribe: cannot create events");
+    }
+    const size_t need = static_cast<size_t>(biggest) + 1;
+    if (need > group_audio_cap) {
+        cudaDeviceSynchronize();
+        for (float*& p : group_audio) {
+            if (p) cudaFree(p);
+            p = nullptr;
+        }
+        group_audio_cap = 0;
+        for (float*& p : group_audio)
+            if (int rc = ctx->cuda(cudaMalloc(&p, sizeof(float) * (need + need / 8)), "transcribe")) return rc;
+        group_audio_cap = need + need / 8;
+    }
+    if (!pinned_in && need > group_pinned_cap) {
+        cudaDeviceSynchronize();
+        for (float*& p : group_pinned) {
+            if (p) cudaFreeHost(p);
+            p = nullptr;
+        }
+        group_pinned_cap = 0;
+        for (float*& p : group_pinned)
+            if (int rc = ctx->cuda(cudaHostAlloc(&p, sizeof(float) * (need + need / 8), cudaHostAllocDefault),
+                                   "transcribe"))
+                return rc;
+        group_pinned_cap = need + need / 8;
+    }
+    const size_t tok_need = 3 * static_cast<size_t>(total_frames) + 3;
+    if (!pinned_tokens && tok_need > tokens_pinned_cap) {
+        if (tokens_pinned) cudaFreeHost(tokens_pinned);
+        tokens_pinned = nullptr;
+        tokens_pinned_cap = 0;
+        if (int rc = ctx->cuda(cudaHostAlloc(&tokens_pinned, sizeof(uint32_t) * tok_need, cudaHostAllocDefault),
+                               "transcribe"))
+            return rc;
+        tokens_pinned_cap = tok_need;
+    }
+    if (!pinned_counts && static_cast<size_t>(n_utt) > counts_pinned_cap) {
+        if (counts_pinned) cudaFreeHost(counts_pinned);
+        counts_pinned = nullptr;
+        counts_pinned_cap = 0;
+        if (int rc = ctx->cuda(cudaHostAlloc(&counts_pinned, sizeof(int) * n_utt, cudaHostAllocDefault), "transcribe"))
+            return rc;
+        counts_pinned_cap = static_cast<size_t>(n_utt);
+    }
+    uint32_t* tok_out = pinned_tokens ? tokens : tokens_pinned;
+    int* cnt_out = pinned_counts ? counts : counts_pinned;
+
+    // Group j's audio up into buffer j % 2, once group j - 2 no longer reads it (and, through
+    // pinned memory, once the copy of group j - 2 has left the pinned buffer).
+    auto put = [&](int j) -> int {
+        const int b = j % 2;
+        const size_t bytes = sizeof(float) * static_cast<size_t>(at[j + 1] - at[j]);
+        const float* src = samples + at[j];
+        if (!pinned_in) {
+            if (j >= 2)
+                if (int rc = ctx->cuda(cudaEventSynchronize(group_copied[b]), "transcribe")) return rc;
+            std::memcpy(group_pinned[b], src, bytes);
+            src = group_pinned[b];
+        }
+        if (j >= 2)
+            if (int rc = ctx->cuda(cudaStreamWaitEvent(copy_stream, group_read[b], 0), "transcribe")) return rc;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(group_audio[b], src, bytes, cudaMemcpyHostToDevice, copy_stream),
+                               "transcribe"))
+            return rc;
+        return ctx->cuda(cudaEventRecord(group_copied[b], copy_stream), "transcribe");
+    };
+
+    if (int rc = put(0)) return rc;
+    int64_t tok_at = 0;
+    for (int g = 0; g < groups; ++g) {
+        const int b = g % 2, u0 = first[g], n = first[g + 1] - first[g];
+        if (int rc = ctx->cuda(cudaStreamWaitEvent(s, group_copied[b], 0), "transcribe")) return rc;
+        if (int rc = transcribe_device(group_audio[b], lengths + u0, n, tokens_dev, counts_dev, frames + u0, s))
+            return rc;
+        if (int rc = ctx->cuda(cudaEventRecord(group_read[b], s), "transcribe")) return rc;
+        int64_t f = 0;
+        for (int u = u0; u < u0 + n; ++u) f += frames[u];
+        if (int rc = ctx->cuda(cudaMemcpyAsync(tok_out + 3 * tok_at, tokens_dev, sizeof(uint32_t) * 3 * f,
+                                               cudaMemcpyDeviceToHost, s),
+                               "transcribe"))
+            return rc;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(cnt_out + u0, counts_dev, sizeof(int) * n, cudaMemcpyDeviceToHost, s),
+                               "transcribe"))
+            return rc;
+        tok_at += f;
+        // The next group's audio goes up while this one is transcribed.
+        if (g + 1 < groups)
+            if (int rc = put(g + 1)) return rc;
+    }
+    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "transcribe")) return rc;
+    if (!pinned_tokens) std::memcpy(tokens, tokens_pinned, sizeof(uint32_t) * 3 * tok_at);
+    if (!pinned_counts) std::memcpy(counts, counts_pinned, sizeof(int) * n_utt);
+    return TELMO_OK;
 }
 
 void Granite::release_e2e() {
@@ -114,15 +299,12 @@ int Granite::transcribe_device(const float* samples, const int64_t* lengths, int
         first[n_utt + u] = frames_out[u];
         at += frames_out[u];
     }
-    if (int rc = ctx->cuda(cudaMemcpyAsync(first_dev, first.data(), sizeof(int) * first.size(), cudaMemcpyHostToDevice, s),
-                           "transcribe"))
+    if (int rc = ctx->cuda(ctx->uploads.upload(first_dev, first.data(), sizeof(int) * first.size(), s), "transcribe"))
         return rc;
     ++launches;
-    if (int rc = ctx->cuda(ctc_collapse(ids_dev, first_dev, first_dev + n_utt, n_utt, static_cast<uint32_t>(c.blank),
-                                        tokens, counts, s),
-                           "ctc"))
-        return rc;
-    return ctx->cuda(cudaStreamSynchronize(s), "transcribe");
+    return ctx->cuda(ctc_collapse(ids_dev, first_dev, first_dev + n_utt, n_utt, static_cast<uint32_t>(c.blank),
+                                  tokens, counts, s),
+                     "ctc");
 }
 
 void Granite::release_buffers() {
@@ -394,10 +576,8 @@ int Granite::span(const Block& b, float* xs, int t, const float* window, int m, 
         for (int r = 0; r < n; ++r) host.push_back(2 * (out_start + r) - lo);
     const int words = static_cast<int>(host.size());
     if (int rc = ensure(std::max(t, m), (words + 7) / 8 + 1)) return rc;
-    if (int rc = ctx->cuda(cudaMemcpyAsync(tasks_dev, host.data(), sizeof(int) * words, cudaMemcpyHostToDevice, s),
-                           "granite tasks"))
+    if (int rc = ctx->cuda(ctx->uploads.upload(tasks_dev, host.data(), sizeof(int) * words, s), "granite tasks"))
         return rc;
-    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "granite tasks")) return rc;
 
     if (int rc = feed_forward(b.ff1, xs, t, s)) return rc;
     // Attention (src/granite.rs:820-851).
@@ -524,12 +704,9 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
     }
     const int words = static_cast<int>(host.size());
     if (int rc = ensure(M0, (words + 7) / 8 + 1)) return rc;
-    if (int rc = ctx->cuda(cudaMemcpyAsync(tasks_dev, host.data(), sizeof(int) * words, cudaMemcpyHostToDevice, s),
-                           "granite tasks"))
+    // Through pinned staging: the copy is asynchronous and `host` may go out of scope.
+    if (int rc = ctx->cuda(ctx->uploads.upload(tasks_dev, host.data(), sizeof(int) * words, s), "granite tasks"))
         return rc;
-    // The upload reads `host` asynchronously for pageable memory only after the copy is staged;
-    // wait so the vector may go out of scope.
-    if (int rc = ctx->cuda(cudaStreamSynchronize(s), "granite tasks")) return rc;
 
     // Input projection (src/granite.rs:724-733).
     const int kin = 4 * c.n_mels;
@@ -778,45 +955,21 @@ extern "C" int telmo_granite_transcribe(telmo_granite* gp, const float* samples,
     if (!g) return TELMO_ERR_ARGUMENT;
     if (n_utt <= 0 || !samples || !lengths || !tokens || !counts || !frames)
         return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: bad arguments");
-    if (int rc = g->ctx->use_device()) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int64_t total = 0;
-    for (int u = 0; u < n_utt; ++u) {
+    if (!g->finalized) return g->ctx->fail(TELMO_ERR_MODEL, "granite: the model is not finalized");
+    for (int u = 0; u < n_utt; ++u)
         if (lengths[u] < 0) return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: negative length");
-        total += lengths[u];
-    }
-    if (static_cast<size_t>(total) > g->audio_cap) {
-        cudaStreamSynchronize(s);
-        if (g->audio_dev) cudaFree(g->audio_dev);
-        g->audio_dev = nullptr;
-        g->audio_cap = 0;
-        if (int rc = g->ctx->cuda(cudaMalloc(&g->audio_dev, sizeof(float) * (total + total / 8 + 1)), "transcribe"))
-            return rc;
-        g->audio_cap = static_cast<size_t>(total + total / 8 + 1);
-    }
-    // The device token buffers must exist before transcribe_device checks its arguments.
-    int64_t rows_total = 0, frames_total_est = 0;
-    for (int u = 0; u < n_utt; ++u) {
-        rows_total += static_cast<int64_t>(telmo_logmel_rows(TELMO_FRONTEND_GRANITE, lengths[u]));
-        frames_total_est += static_cast<int64_t>(telmo_granite_frames_for_samples(gp, lengths[u]));
-    }
-    if (rows_total > (1 << 30)) return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_transcribe: batch too large");
-    if (int rc = g->ensure_e2e(static_cast<int>(rows_total) + 1, static_cast<int>(frames_total_est) + 1, n_utt))
-        return rc;
-    if (int rc = g->ctx->cuda(cudaMemcpyAsync(g->audio_dev, samples, sizeof(float) * total, cudaMemcpyHostToDevice, s),
-                              "transcribe"))
-        return rc;
-    if (int rc = g->transcribe_device(g->audio_dev, lengths, n_utt, g->tokens_dev, g->counts_dev, frames, s)) return rc;
-    int64_t frames_total = 0;
-    for (int u = 0; u < n_utt; ++u) frames_total += frames[u];
-    if (int rc = g->ctx->cuda(cudaMemcpyAsync(tokens, g->tokens_dev, sizeof(uint32_t) * 3 * frames_total,
-                                              cudaMemcpyDeviceToHost, s),
-                              "transcribe"))
-        return rc;
-    if (int rc = g->ctx->cuda(cudaMemcpyAsync(counts, g->counts_dev, sizeof(int) * n_utt, cudaMemcpyDeviceToHost, s),
-                              "transcribe"))
-        return rc;
-    return g->ctx->cuda(cudaStreamSynchronize(s), "transcribe");
+    if (int rc = g->ctx->use_device()) return rc;
+    return g->transcribe_host(samples, lengths, n_utt, tokens, counts, frames, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_granite_set_transcribe_group(telmo_granite* gp, double seconds) {
+    Granite* g = as_granite(gp);
+    if (!g) return TELMO_ERR_ARGUMENT;
+    if (!(seconds >= 0.02) || seconds > 1e6)
+        return g->ctx->fail(TELMO_ERR_ARGUMENT, "telmo_granite_set_transcribe_group: %g seconds is out of range",
+                            seconds);
+    g->group_samples = static_cast<int64_t>(seconds * 16000.0);
+    return TELMO_OK;
 }
 
 extern "C" int telmo_granite_profile(telmo_granite* gp, int enable) {

@@ -72,6 +72,21 @@ struct Granite {
     // End-to-end buffers (audio in, tokens out), grown on demand.
     float* audio_dev = nullptr;
     size_t audio_cap = 0;
+    // The host-buffer transcription's pipeline: each group's audio goes up on copy_stream into
+    // one of two device buffers (through one of two pinned buffers when the caller's memory is
+    // pageable) while the previous group is transcribed; tokens come back through pinned memory.
+    int64_t group_samples = int64_t(2048) * 16000;
+    cudaStream_t copy_stream = nullptr;
+    float* group_audio[2] = {nullptr, nullptr};
+    size_t group_audio_cap = 0;
+    float* group_pinned[2] = {nullptr, nullptr};
+    size_t group_pinned_cap = 0;
+    cudaEvent_t group_copied[2] = {nullptr, nullptr};  // the group's audio is on the device
+    cudaEvent_t group_read[2] = {nullptr, nullptr};    // the group's transcription is done with it
+    uint32_t* tokens_pinned = nullptr;
+    size_t tokens_pinned_cap = 0;
+    int* counts_pinned = nullptr;
+    size_t counts_pinned_cap = 0;
     float* feats_dev = nullptr;
     float* enc_dev = nullptr;
     uint32_t* ids_dev = nullptr;
@@ -116,6 +131,10 @@ struct Granite {
                           int* frames_out, cudaStream_t s);
     int ensure_e2e(int rows, int frames, int n_utt);
     void release_e2e();
+    // Host audio -> host tokens in groups of at most group_samples samples, pipelined.
+    int transcribe_host(const float* samples, const int64_t* lengths, int n_utt, uint32_t* tokens, int* counts,
+                        int* frames, cudaStream_t s);
+    void release_pipeline();
 };
 
 }  // namespace telmo

@@ -1,11 +1,22 @@
 // kernels.h -- host-side launchers of the CUDA kernels (internal to libtelmo_b200).
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 namespace telmo {
+
+// One bit per device for set-up done once per device (kernel attributes): safe to test and set
+// from several host threads at once.
+struct DeviceOnce {
+    std::atomic<uint64_t> bits{0};
+    bool done(int dev) const { return dev < 64 && ((bits.load(std::memory_order_acquire) >> dev) & 1); }
+    void mark(int dev) {
+        if (dev < 64) bits.fetch_or(uint64_t(1) << dev, std::memory_order_release);
+    }
+};
 
 // kOutF16Split writes each value v as two fp16 planes, hi = fp16(v) at rows 0..m-1 and
 // lo = fp16(v - hi) at rows m..2m-1 (ldc apart): the operands of the tensor-core attention.

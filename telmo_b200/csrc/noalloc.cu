@@ -28,7 +28,10 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // The device address of the scratch on the current device. In host code g_linear_scratch names
 // a host-side stand-in, not device memory, so the address comes from cudaGetSymbolAddress, once
-// per device, with that device current.
+// per device, with that device current. The cached address belongs to the device's context as
+// it was at that first call: a host program that calls cudaDeviceReset and goes on using the
+// device gets a new context, in which the library's module and its scratch are loaded anew, so
+// it must not call telmo_linear_noalloc again in that process.
 int scratch_address(Ctx* ctx, void** out) {
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     if (ctx->device < 0 || ctx->device >= kMaxDevices)

@@ -199,6 +199,11 @@ class Granite:
         tok = tokens if isinstance(tokens, np.ndarray) else tokens.numpy()
         return tok.reshape(-1), counts, frames
 
+    def set_transcribe_group(self, seconds: float):
+        """The audio per group of the host-buffer transcription (telmo_granite_transcribe), which
+        transcribes one group while the next group's samples are copied to the device."""
+        check(_lib.load().telmo_granite_set_transcribe_group(self._h, float(seconds)), self.ctx.handle)
+
     def transcribe_device(self, samples, lengths, tokens, counts, stream=None):
         """Device-resident variant: samples, tokens [3 * frames] (int32) and counts are CUDA
         tensors; returns the host array of frames per utterance."""

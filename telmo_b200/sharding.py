@@ -34,18 +34,28 @@ def assign(samples: Sequence[int], world: int) -> List[List[int]]:
 
 
 def batches(utts: Sequence[int], samples: Sequence[int], max_seconds: float) -> List[List[int]]:
-    """Length-sorted batches of at most `max_seconds` of audio (a longer utterance gets a batch of
-    its own), so a batch's utterances have similar lengths."""
+    """Length-sorted batches of about equal audio: ceil(total / max_seconds) of them, none above
+    `max_seconds` (a longer utterance gets a batch of its own), so a batch's utterances have
+    similar lengths and the last batch is not a small remainder. The cut rule is the one
+    telmo_granite_transcribe applies to its groups, so the sorted utterances passed to it in one
+    call are transcribed in exactly these batches."""
     samples = np.asarray(samples, dtype=np.int64)
     ordered = sorted(utts, key=lambda u: (int(samples[u]), u))
-    out, cur, acc = [], [], 0.0
+    limit = int(max_seconds * SAMPLE_RATE)
+    total = int(samples[ordered].sum()) if ordered else 0
+    groups = max(1, -(-total // limit))
+    out, cur = [], []
+    acc = in_batch = 0
+    g = 1
     for u in ordered:
-        s = samples[u] / SAMPLE_RATE
-        if cur and acc + s > max_seconds:
+        n = int(samples[u])
+        if cur and (in_batch + n > limit or acc >= g * total // groups):
             out.append(cur)
-            cur, acc = [], 0.0
+            cur, in_batch = [], 0
+            g += 1
         cur.append(u)
-        acc += s
+        acc += n
+        in_batch += n
     if cur:
         out.append(cur)
     return out

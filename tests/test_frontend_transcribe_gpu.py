@@ -71,3 +71,42 @@ def test_transcribe_matches_the_oracle_pipeline(ctx, oracle_lib):
         else:
             assert len(got_t) > 0
     gpu.close()
+
+
+def test_host_transcribe_in_pipelined_groups_equals_one_group(ctx):
+    """telmo_granite_transcribe splits its utterances into groups and copies the next group's
+    audio up while one is transcribed. Each utterance's result does not depend on the others in
+    its batch, so any grouping gives the same tokens, counts and frames bit for bit -- with
+    pageable or pinned host audio and tokens, and for an utterance longer than a group."""
+    import torch
+    from telmo_b200.granite import Granite
+    cfg = synthetic.granite_config(layers=4)
+    entries = synthetic.granite_entries(cfg, seed=1, scales="conditioned")
+    gpu = Granite.from_entries(ctx, cfg, entries)
+    secs = [0.7, 3.3, 1.1, 6.0, 2.5, 0.3, 4.4, 1.9, 2.2, 5.1]
+    audio = [synthetic.audio(s, seed=80 + i) for i, s in enumerate(secs)]
+    lengths = np.array([a.size for a in audio], np.int64)
+    packed = np.concatenate(audio)
+    want = gpu.transcribe_arrays(packed, lengths)
+    for group_s in (4.0, 1.0, 9.0):
+        gpu.set_transcribe_group(group_s)
+        for pinned in (False, True):
+            samples = torch.from_numpy(packed).pin_memory() if pinned else packed
+            cap = 3 * sum(gpu.frames_for_samples(int(x)) for x in lengths)
+            tokens = torch.zeros(cap, dtype=torch.int32).pin_memory() if pinned else None
+            got = gpu.transcribe_arrays(samples, lengths, tokens_buf=tokens)
+            ctx.check()
+            got_tok = (got[0].numpy() if hasattr(got[0], "numpy") else got[0]).view(np.uint32)
+            assert np.array_equal(got[2], want[2]) and np.array_equal(got[1], want[1])
+            # Utterance u's counts[u] triples start at 3 * (frames before it); the rest of its
+            # region is not written.
+            at = 0
+            for f, c in zip(want[2], want[1]):
+                assert np.array_equal(got_tok[3 * at:3 * (at + c)], want[0].view(np.uint32)[3 * at:3 * (at + c)]), \
+                    (group_s, pinned)
+                at += int(f)
+    gpu.set_transcribe_group(2048.0)
+    from telmo_b200 import TelmoError
+    with pytest.raises(TelmoError):
+        gpu.set_transcribe_group(0.0)
+    gpu.close()

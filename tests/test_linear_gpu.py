@@ -244,3 +244,24 @@ def test_bad_arguments_are_errors_not_crashes(ctx):
         kern.linear(None, 4, w, c)                       # null input
     kern.linear(_dev(a), 0, w, c, Epilogue.PLAIN)        # m = 0 is a no-op
     ctx.check()
+
+
+def test_quantize_x2_refuses_unaligned_levels(ctx):
+    # The quantizer stores the levels four bytes at a time and the product reads them through
+    # 16-byte aligned tensor maps: an offset hi or lo pointer is an argument error, found on the
+    # host before anything is launched, and the context stays usable.
+    import torch
+    from telmo_b200 import _lib
+    m, k, ldq = 8, 64, 64
+    a = torch.zeros((m, k), dtype=torch.float32, device="cuda")
+    buf = torch.zeros(2 * m * ldq + 64, dtype=torch.int8, device="cuda")
+    s = torch.zeros(m, dtype=torch.float32, device="cuda")
+    L = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    hi, lo = buf.data_ptr(), buf.data_ptr() + m * ldq
+    for bad_hi, bad_lo in [(hi + 4, lo), (hi, lo + 8), (hi + 1, lo + 1)]:
+        rc = L.telmo_quantize_x2(ctx.handle, a.data_ptr(), k, m, k, bad_hi, bad_lo, ldq, s.data_ptr(), stream)
+        assert rc == _lib.TELMO_ERR_ARGUMENT
+        assert b"aligned" in L.telmo_last_error(ctx.handle)
+    assert L.telmo_quantize_x2(ctx.handle, a.data_ptr(), k, m, k, hi, lo, ldq, s.data_ptr(), stream) == 0
+    ctx.check()

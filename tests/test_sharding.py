@@ -32,6 +32,21 @@ def test_batches_are_length_sorted_and_bounded():
     assert sum(len(x) for x in b) == 6
 
 
+def test_batches_split_the_audio_evenly():
+    # 100 s in batches of at most 40 s: three batches of about a third each, not 40 + 40 + 20.
+    samples = np.full(10, 10 * 16000)
+    b = sharding.batches(range(10), samples, max_seconds=40.0)
+    assert [len(x) for x in b] == [4, 3, 3]
+    secs = synthetic.lengths_log_uniform(4096, 1.0, 30.0, seed=0)
+    samples = (secs * 16000).astype(np.int64)
+    for world in (1, 8):
+        shard = sharding.assign(samples, world)[0]
+        b = sharding.batches(shard, samples, 2048.0)
+        loads = [samples[x].sum() / 16000 for x in b]
+        assert max(loads) <= 2048.0 and len(b) == int(np.ceil(samples[shard].sum() / 16000 / 2048.0))
+        assert min(loads) > 0.9 * max(loads), loads
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
