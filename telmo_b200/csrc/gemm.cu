@@ -25,6 +25,7 @@
 // error word and returns.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "tma.h"
 
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -523,6 +524,8 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
     }
 }
 
+}  // namespace
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -535,6 +538,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     });
     return fn;
 }
+
+bool encode_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
 
 // A 2-D int8 tensor map over rows of `cols` bytes, `ld` bytes apart, boxes of 128 bytes x 128
 // rows with the 128-byte swizzle. Reads past `cols` or `rows` fill zeros.

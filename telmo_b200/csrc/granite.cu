@@ -590,11 +590,14 @@ int Granite::span(const Block& b, float* xs, int t, const float* window, int m, 
     const float scale = static_cast<float>(std::pow(static_cast<double>(c.head_dim), -0.5));
     const AttnTask* att_tasks = reinterpret_cast<const AttnTask*>(tasks_dev);
     const cudaError_t ae =
-        mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(t) * 3 * d, c.heads,
-                                    c.head_dim, ctxn, att_tasks, nb, static_cast<const __half*>(b.rel16), b.rel.scales,
-                                    scale, att, s)
-            : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, nb, b.rel.values, b.rel.ld, b.rel.scales,
-                                scale, att, s);
+        mma && granite_attention_tc_supported(c.head_dim, ctxn)
+            ? granite_attention_tc(reinterpret_cast<const __half*>(big), t, c.heads, c.head_dim, ctxn, att_tasks, nb,
+                                   static_cast<const __half*>(b.rel16), b.rel.scales, scale, att, ctx->error_word, s)
+        : mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(t) * 3 * d, c.heads,
+                                      c.head_dim, ctxn, att_tasks, nb, static_cast<const __half*>(b.rel16),
+                                      b.rel.scales, scale, att, s)
+              : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, nb, b.rel.values, b.rel.ld, b.rel.scales,
+                                  scale, att, s);
     if (int rc = ctx->cuda(ae, "attention")) return rc;
     ++launches;
     if (int rc = ctx->cuda(quantize_x2(att, d, t, d, q, s), "quant")) return rc;
@@ -737,10 +740,14 @@ int Granite::encode(const float* feats, const int* rows, int n_utt, float* out, 
         if (prof.on) prof.begin(kProfAttention, s);
         const AttnTask* att_tasks = reinterpret_cast<const AttnTask*>(tasks_dev + p.att_off);
         const cudaError_t ae =
-            mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(m) * 3 * d, c.heads,
-                                        c.head_dim, ctxn, att_tasks, p.att_n, static_cast<const __half*>(b.rel16),
-                                        b.rel.scales, scale, att, s)
-                : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, p.att_n, b.rel.values, b.rel.ld,
+            mma && granite_attention_tc_supported(c.head_dim, ctxn)
+                ? granite_attention_tc(reinterpret_cast<const __half*>(big), m, c.heads, c.head_dim, ctxn, att_tasks,
+                                       p.att_n, static_cast<const __half*>(b.rel16), b.rel.scales, scale, att,
+                                       ctx->error_word, s)
+            : mma ? granite_attention_mma(reinterpret_cast<const __half*>(big), static_cast<int64_t>(m) * 3 * d, c.heads,
+                                          c.head_dim, ctxn, att_tasks, p.att_n, static_cast<const __half*>(b.rel16),
+                                          b.rel.scales, scale, att, s)
+                  : granite_attention(big, c.heads, c.head_dim, ctxn, att_tasks, p.att_n, b.rel.values, b.rel.ld,
                                     b.rel.scales, scale, att, s);
         if (int rc = ctx->cuda(ae, "attention")) return rc;
         if (prof.on) prof.end(kProfAttention, s);

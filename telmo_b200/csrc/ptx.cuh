@@ -179,6 +179,65 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// D[tmem] (+)= A[smem] * B[smem], fp16 x fp16 -> f32 (kind::f16), one CTA. A and B must both be
+// fp16 (the instruction descriptor below says so).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// The same with A in tensor memory: a_tmem addresses M lanes x K fp16 packed two per column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane from registers (32x32b shape, x32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Instruction descriptor for kind::f16 with fp16 A and B and an f32 accumulator; A K-major, B
+// K-major or (b_mn) MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn) {
+    return (1u << 4) | (b_mn ? (1u << 16) : 0u) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Shared-memory descriptor for an MN-major operand stored with the 128-byte swizzle: rows of 128
+// bytes along MN (64 fp16) for consecutive K, 8-row K groups 1024 bytes apart, and the next 64
+// MN elements `mn_stride` bytes on (the layout of 128-byte-wide SWIZZLE_128B TMA boxes of a
+// row-major [K][MN] matrix, one box per 64 MN elements).
+__device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t mn_stride) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFF) << 16;  // leading byte offset: next MN atom
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;                  // stride byte offset: next 8 K rows
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
 // ---- CTA pairs (clusters of two) for tcgen05 cta_group::2 ---------------------------------
 
 __device__ __forceinline__ uint32_t cluster_rank() {

@@ -61,4 +61,12 @@ cudaError_t granite_attention_mma(const __half* qkv, int64_t plane, int heads, i
                                   int n_tasks, const __half* rel16, const float* rel_scale, float scale, float* att,
                                   cudaStream_t stream);
 
+// The same on the tcgen05 tensor cores (attention_tc.cu), for context 128 and head size 128:
+// the QKV product's fp16 planes of `rows` rows each (the low plane right after the high one);
+// a wait that times out records kErrWaitTimeout in `error`.
+bool granite_attention_tc_supported(int hd, int ctx);
+cudaError_t granite_attention_tc(const __half* qkv, int rows, int heads, int hd, int ctx, const AttnTask* tasks,
+                                 int n_tasks, const __half* rel16, const float* rel_scale, float scale, float* att,
+                                 uint32_t* error, cudaStream_t stream);
+
 }  // namespace telmo
