@@ -28,7 +28,8 @@
 //               memory.
 // TMEM: S in columns 0..127, pos in 128..383 (then P: hi 128..191, lo 192..255), O in 384..511;
 // the next task's S product runs while this task's O is read out. Partial blocks (len < 128)
-// issue only the key and position columns they use. Every wait is bounded; on timeout the
+// issue only the key and position columns they use, and blocks of at most 64 rows load only
+// those rows. Every wait is bounded; on timeout the
 // kernel records kErrWaitTimeout in the error word and returns.
 #include "kernels.h"
 #include "ptx.cuh"
@@ -74,15 +75,18 @@ __device__ __forceinline__ void load_operand(const CUtensorMap* map, uint64_t* b
     tma_load_2d(map, bar, dst + 3 * kBox, x + 64, y_lo);
 }
 
-__device__ __forceinline__ uint32_t pack_half2(__half a, __half b) {
-    return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+// A probability p (0 <= p <= 1) rounded to fp16's 11 significant bits, to nearest even, on the
+// integer pipe -- the value fp16(p) stands for, for p >= 2^-14; below that 0, so the low part
+// carries p. p - f16_high(p) is exact in f32.
+__device__ __forceinline__ float f16_high(float p) {
+    const uint32_t u = __float_as_uint(p);
+    const uint32_t r = (u + 0x0FFFu + ((u >> 13) & 1u)) & ~0x1FFFu;
+    return p >= 6.103515625e-05f ? __uint_as_float(r) : 0.0f;
 }
 
-// 2^x on the PTX ISA's ex2.approx instruction (relative error about 2^-22).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);  // a in the low half
+    return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // The epilogue warps' named barrier (barrier 0 is __syncthreads).
@@ -93,7 +97,8 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n
 __device__ __forceinline__ int win_index(int l, int e) { return l * 64 + ((((e >> 2) ^ l) & 7) | (e >> 2 & 8)) * 4 + (e & 3); }
 
 __global__ void __launch_bounds__(kThreads, 1)
-granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_rel,
+granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_qkv64,
+                            const __grid_constant__ CUtensorMap map_rel,
                             int rows, int heads, const AttnTask* __restrict__ tasks, int n_tasks,
                             const float* __restrict__ rel_scale, int positions, float scale, float* __restrict__ att,
                             uint32_t* error) {
@@ -113,7 +118,8 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
     const int D = heads * HD;
     const int total = n_tasks * heads;
 
-    for (int p = threadIdx.x; p < 256; p += kThreads) rs[p] = p < positions ? __ldg(rel_scale + p) : 0.0f;
+    // Each position's scale times the score scale: the position term of a score is pos * rs[p].
+    for (int p = threadIdx.x; p < 256; p += kThreads) rs[p] = p < positions ? __fmul_rn(__ldg(rel_scale + p), scale) : 0.0f;
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
         mbar_init(&bars->k_full, 1);
@@ -126,6 +132,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&map_qkv);
+        prefetch_tensormap(&map_qkv64);
         prefetch_tensormap(&map_rel);
     }
     if (warp == 1) {
@@ -151,14 +158,20 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 const int h = w % heads;
                 const int y_hi = tk.row, y_lo = rows + tk.row;
                 const uint32_t prev = (it - 1) & 1;
+                // A block of at most 64 rows loads 64-row boxes (the first half of each slot): the
+                // products never read its rows past 64 (S and O stop at 16 * ceil(len / 16) keys;
+                // query rows past len are not stored).
+                const bool short_block = tk.len <= 64;
+                const CUtensorMap* mq = short_block ? &map_qkv64 : &map_qkv;
+                const uint32_t bytes = short_block ? kOperand / 2 : kOperand;
                 // Q: the previous S and position products are done with Q's buffer.
                 if (it > 0 && !mbar_wait(&bars->s_done, prev)) { fail(); break; }
-                mbar_arrive_expect_tx(&bars->q_full, kOperand);
-                load_operand(&map_qkv, &bars->q_full, buf_q, h * HD, y_hi, y_lo);
+                mbar_arrive_expect_tx(&bars->q_full, bytes);
+                load_operand(mq, &bars->q_full, buf_q, h * HD, y_hi, y_lo);
                 // K: the previous softmax is done with its position windows in K's buffer.
                 if (it > 0 && !mbar_wait(&bars->p_full, prev)) { fail(); break; }
-                mbar_arrive_expect_tx(&bars->k_full, kOperand);
-                load_operand(&map_qkv, &bars->k_full, buf_k, D + h * HD, y_hi, y_lo);
+                mbar_arrive_expect_tx(&bars->k_full, bytes);
+                load_operand(mq, &bars->k_full, buf_k, D + h * HD, y_hi, y_lo);
                 // The relative table: the previous O product is done with V in the table's buffer.
                 if (it > 0 && !mbar_wait(&bars->o_done, prev)) { fail(); break; }
                 mbar_arrive_expect_tx(&bars->r_full, 2 * kRelHalf);
@@ -166,8 +179,8 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 tma_load_2d(&map_rel, &bars->r_full, buf_r + kRelHalf, 64, 0);
                 // V: this task's position product is done with the table.
                 if (!mbar_wait(&bars->s_done, it & 1)) { fail(); break; }
-                mbar_arrive_expect_tx(&bars->v_full, kOperand);
-                load_operand(&map_qkv, &bars->v_full, buf_r, 2 * D + h * HD, y_hi, y_lo);
+                mbar_arrive_expect_tx(&bars->v_full, bytes);
+                load_operand(mq, &bars->v_full, buf_r, 2 * D + h * HD, y_hi, y_lo);
             }
         }
     } else if (warp == 1) {
@@ -270,7 +283,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                     const int key = 32 * c + j;
                     const float pos = win[win_index(lane, 31 - lane + j)];
                     const float ps = rs[T - 1 - row + key];
-                    float v = __fadd_rn(__fmul_rn(__uint_as_float(sv[j]), scale), __fmul_rn(__fmul_rn(pos, ps), scale));
+                    float v = __fadd_rn(__fmul_rn(__uint_as_float(sv[j]), scale), __fmul_rn(pos, ps));
                     if (key >= len) v = -INFINITY;
                     lg[32 * cc + j] = v;
                     mx = fmaxf(mx, v);
@@ -281,13 +294,18 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
             epi_sync();
             mx = fmaxf(red_max[row], red_max[T + row]);
             const float mxl = __fmul_rn(mx, kLog2e);
+            // The row sum in f64 (as the reference) over f32 partial sums of 8 exponentials.
             double s0 = 0.0, s1 = 0.0;
 #pragma unroll
-            for (int j = 0; j < 64; j += 2) {
-                lg[j] = ex2_approx(__fmaf_rn(lg[j], kLog2e, -mxl));
-                lg[j + 1] = ex2_approx(__fmaf_rn(lg[j + 1], kLog2e, -mxl));
-                s0 += static_cast<double>(lg[j]);
-                s1 += static_cast<double>(lg[j + 1]);
+            for (int g = 0; g < 8; ++g) {
+                float part = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    lg[8 * g + k] = ex2_approx(__fmaf_rn(lg[8 * g + k], kLog2e, -mxl));
+                    part = __fadd_rn(part, lg[8 * g + k]);
+                }
+                if (g & 1) s1 += static_cast<double>(part);
+                else s0 += static_cast<double>(part);
             }
             red_sum[half * T + row] = s0 + s1;
             epi_sync();
@@ -298,10 +316,9 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
                 const float p0 = __fmul_rn(lg[2 * e], inv), p1 = __fmul_rn(lg[2 * e + 1], inv);
-                const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-                hv[e] = pack_half2(h0, h1);
-                lv[e] = pack_half2(__float2half_rn(__fsub_rn(p0, __half2float(h0))),
-                                   __float2half_rn(__fsub_rn(p1, __half2float(h1))));
+                const float h0 = f16_high(p0), h1 = f16_high(p1);
+                hv[e] = pack2(h0, h1);
+                lv[e] = pack2(__fsub_rn(p0, h0), __fsub_rn(p1, h1));
             }
             tmem_st32(lanes + kColP + 32 * half, hv);
             tmem_st32(lanes + kColP + 64 + 32 * half, lv);
@@ -358,16 +375,19 @@ cudaError_t granite_attention_tc(const __half* qkv, int rows, int heads, int hd,
     }
     const int D = heads * HD;
     // The QKV product's two fp16 planes as one [2 rows, 3 D] tensor: hi rows 0.., lo rows rows...
-    CUtensorMap mq, mr;
+    CUtensorMap mq, mq64, mr;
     if (!encode_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qkv, static_cast<uint64_t>(3 * D),
                        2 * static_cast<uint64_t>(rows), static_cast<uint64_t>(3 * D) * 2, 64, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_map_2d(&mq64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qkv, static_cast<uint64_t>(3 * D),
+                       2 * static_cast<uint64_t>(rows), static_cast<uint64_t>(3 * D) * 2, 64, 64,
                        CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map_2d(&mr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rel16, HD, static_cast<uint64_t>(2 * ctx - 1), HD * 2, 64,
                        256, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     const int total = n_tasks * heads;
     const int grid = std::min(total, num_sms());
-    granite_attention_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mr, rows, heads, tasks, n_tasks, rel_scale,
+    granite_attention_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mq64, mr, rows, heads, tasks, n_tasks, rel_scale,
                                                                        2 * ctx - 1, scale, att, error);
     return cudaGetLastError();
 }

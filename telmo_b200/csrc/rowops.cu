@@ -63,6 +63,23 @@ struct RowReduce {
         ++slot;
         return r;
     }
+    // Two sums reduced together (one exchange, one barrier).
+    __device__ __forceinline__ void sum2(double& a, double& b, int lane) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            a += __shfl_xor_sync(kFull, a, o);
+            b += __shfl_xor_sync(kFull, b, o);
+        }
+        if (P == 1) return;
+        if (lane == 0) {
+            xch[slot * P + part] = a;
+            xch[(slot + 1) * P + part] = b;
+        }
+        sync();
+        a = xch[slot * P] + xch[slot * P + 1];
+        b = xch[(slot + 1) * P] + xch[(slot + 1) * P + 1];
+        slot += 2;
+    }
     __device__ __forceinline__ float max(float v, int lane) {
         v = warp_max(v);
         if (P == 1) return v;
@@ -80,19 +97,20 @@ template <int C, int P>
 __device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, int off, const float* __restrict__ gamma,
                                                 const float* __restrict__ beta, float eps, int lane,
                                                 RowReduce<P>& red) {
-    double s = 0.0;
-#pragma unroll
-    for (int c = 0; c < C; ++c)
-        s += (static_cast<double>(v[c].x) + static_cast<double>(v[c].y)) +
-             (static_cast<double>(v[c].z) + static_cast<double>(v[c].w));
-    const double mean = red.sum(s, lane) / d;
-    double q = 0.0;
+    // Both moments in one pass (f64 sums of the values and of their squares): the variance as
+    // E[x^2] - mean^2 agrees with the reference's two-pass f64 variance to about 1e-16 relative
+    // for the encoder's rows (|mean| within a few standard deviations), and the row is read and
+    // reduced once.
+    double s = 0.0, q = 0.0;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-        const double a = v[c].x - mean, b = v[c].y - mean, e = v[c].z - mean, f = v[c].w - mean;
-        q += (a * a + b * b) + (e * e + f * f);
+        const double a = v[c].x, b = v[c].y, e = v[c].z, f = v[c].w;
+        s += (a + b) + (e + f);
+        q = fma(a, a, fma(b, b, fma(e, e, fma(f, f, q))));
     }
-    const double var = red.sum(q, lane) / d;
+    red.sum2(s, q, lane);
+    const double mean = s / d;
+    const double var = fmax(q / d - mean * mean, 0.0);
     const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
 #pragma unroll
     for (int c = 0; c < C; ++c) {
