@@ -100,8 +100,9 @@ int telmo_linear(telmo_ctx *ctx, const float *a, size_t lda, size_t m, const tel
                  size_t ldc, void *stream);
 
 /* The activation quantization telmo_linear applies, exposed for checking: row r of a (k
- * values) becomes scale[r] * (hi + lo / 254), hi = round(a / scale) as quantize_row_int8
- * (src/quant.rs:190-198) with scale = amax / 127, lo = round((a - hi * scale) * 254 / scale).
+ * values) becomes scale[r] * (hi + lo / 254): scale = amax / 127 as quantize_row_int8
+ * (src/quant.rs:190-198) sets a weight row's, hi = a / scale and lo = (a - hi * scale) * 254 /
+ * scale, each rounded to the nearest integer (halves to even).
  * hi and lo are device int8 [m, ldq], ldq >= k and a multiple of 16; columns k..ldq are zeroed. */
 int telmo_quantize_x2(telmo_ctx *ctx, const float *a, size_t lda, size_t m, size_t k, int8_t *hi,
                       int8_t *lo, size_t ldq, float *scale, void *stream);
@@ -231,7 +232,8 @@ int telmo_granite_transcribe(telmo_granite *g, const float *samples, const int64
                              int n_utt, uint32_t *tokens, int *counts, int *frames, void *stream);
 /* The audio per group of telmo_granite_transcribe, in seconds (at least 0.02). */
 int telmo_granite_set_transcribe_group(telmo_granite *g, double seconds);
-/* The same with samples, tokens and counts in device memory (lengths and frames on the host). */
+/* The same with samples, tokens and counts in device memory (lengths and frames on the host);
+ * returns once the work is queued on `stream` (frames is filled on the host right away). */
 int telmo_granite_transcribe_device(telmo_granite *g, const float *samples,
                                     const int64_t *lengths, int n_utt, uint32_t *tokens,
                                     int *counts, int *frames, void *stream);
@@ -372,6 +374,13 @@ int telmo_parakeet_predict(telmo_parakeet *p, const int *tokens, int rows, float
 int telmo_parakeet_set_decoder(telmo_parakeet *p, int persistent);
 /* Which decoder the last decode ran: 1 persistent, 0 per-phase launches, -1 none yet. */
 int telmo_parakeet_last_decoder(const telmo_parakeet *p);
+/* A test of the persistent decoder's failure path, which has no counterpart in the reference (its
+ * decoder runs on one CPU thread): in the next persistent decode, CTA `cta` does not arrive at
+ * the first grid barrier, so every CTA's bounded wait there runs out after about a second, the
+ * kernel returns without touching the tokens, and the decode returns TELMO_ERR_DEVICE_TIMEOUT.
+ * No copy or tensor-core operation is in flight at that barrier; the context stays usable and
+ * the decode after it runs normally. */
+int telmo_parakeet_test_barrier_timeout(telmo_parakeet *p, int cta);
 /* The persistent decoder's own clock for the last decode run with profiling on: ms[10], per
  * phase kind (start, joint, decide, LSTM products, cells, pred_proj product, prepare; each from
  * one grid barrier to the next), then CTA 0's time inside the products and, of that, waiting

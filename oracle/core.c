@@ -475,10 +475,11 @@ void oracle_quantize_x2(const float *x, size_t m, size_t k, size_t ldx, int8_t *
         float id = d != 0.0f ? 1.0f / d : 0.0f;
         float id_lo = id * 254.0f;
         for (size_t i = 0; i < k; i++) {
-            float h = roundf(row[i] * id);
+            /* Each level rounded to the nearest integer, halves to even (the default mode). */
+            float h = nearbyintf(row[i] * id);
             h = fminf(fmaxf(h, -127.0f), 127.0f);
             float e = fmaf(-h, d, row[i]);
-            float l = roundf(e * id_lo);
+            float l = nearbyintf(e * id_lo);
             l = fminf(fmaxf(l, -127.0f), 127.0f);
             hi[r * ldq + i] = (int8_t)h;
             lo[r * ldq + i] = (int8_t)l;

@@ -67,9 +67,10 @@ void oracle_matmul_rowmajor(const float *a, size_t lda, size_t m, const float *b
 
 /* ---- the split int8 activation rule of the CUDA path (no reference counterpart) ------------
  * Each activation row x (length k) becomes s * (hi + lo / 254) with hi, lo in [-127, 127]:
- * s = amax / 127 and hi = round(x / s) as quantize_row_int8 (src/quant.rs:190-198) computes
- * them, then lo = round((x - hi * s) * 254 / s). The CUDA kernels follow the same f32 steps, so
- * hi, lo and s agree bit for bit. */
+ * s = amax / 127 as quantize_row_int8 (src/quant.rs:190-198) sets a weight row's, hi = x / s
+ * and then lo = (x - hi * s) * 254 / s, each rounded to the nearest integer with halves to even
+ * (the rounding the CUDA kernels get from one add of 1.5 * 2^23). The CUDA kernels follow the
+ * same f32 steps, so hi, lo and s agree bit for bit. */
 void oracle_quantize_x2(const float *x, size_t m, size_t k, size_t ldx, int8_t *hi, int8_t *lo,
                         size_t ldq, float *row_scale);
 /* Exact i32 sums of the two levels against int8 weights in panels: acc_hi[m, n], acc_lo[m, n]. */

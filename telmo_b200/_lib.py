@@ -119,6 +119,7 @@ SIGNATURES = {
     "telmo_parakeet_joint": (_c.c_int, [_vp, _vp, _vp, _c.c_int, _vp, _c.c_size_t, _vp]),
     "telmo_parakeet_predict": (_c.c_int, [_vp, _vp, _c.c_int, _vp, _vp, _vp]),
     "telmo_parakeet_last_decoder": (_c.c_int, [_vp]),
+    "telmo_parakeet_test_barrier_timeout": (_c.c_int, [_vp, _c.c_int]),
     "telmo_parakeet_decoder_profile": (_c.c_int, [_vp, _c.c_void_p, _c.c_void_p]),
     "telmo_parakeet_profile": (_int, [_vp, _int]),
     "telmo_parakeet_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),

@@ -259,9 +259,10 @@ int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* pane
         }
         // Q8_0 (src/quant.rs:8-13): w = q * d[block], exact in f32 (d is an f16 value). The row
         // is re-encoded as s * (hi + lo / 254) with one scale per row, by the rule the
-        // activations use (quant.cu): s = amax / 127, hi = round(w / s), lo = round((w - hi s) *
-        // 254 / s), each clamped to [-127, 127]; the representation is within s / 508 (1/64516 of
-        // the row's largest weight) of w. The GEMM adds hi_a . lo_w to the low-level sum.
+        // activations use (quant.cu): s = amax / 127, hi = w / s and lo = (w - hi s) * 254 / s,
+        // each rounded to the nearest integer (halves to even) and clamped to [-127, 127]; the
+        // representation is within s / 508 (1/64516 of the row's largest weight) of w. The GEMM
+        // adds hi_a . lo_w to the low-level sum.
         float amax = 0.0f;
         for (size_t i = 0; i < k; ++i) {
             const size_t c = col_perm ? static_cast<size_t>(col_perm[i]) : i;
@@ -273,9 +274,9 @@ int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* pane
         const float id_lo = id * 254.0f;
         int8_t* dlo = lo.data() + o * ld;
         for (size_t i = 0; i < k; ++i) {
-            const float h = std::fmin(std::fmax(std::round(w[i] * id), -127.0f), 127.0f);
+            const float h = std::fmin(std::fmax(std::nearbyint(w[i] * id), -127.0f), 127.0f);
             const float e = std::fma(-h, d, w[i]);
-            const float l = std::fmin(std::fmax(std::round(e * id_lo), -127.0f), 127.0f);
+            const float l = std::fmin(std::fmax(std::nearbyint(e * id_lo), -127.0f), 127.0f);
             dst[i] = static_cast<int8_t>(h);
             dlo[i] = static_cast<int8_t>(l);
         }

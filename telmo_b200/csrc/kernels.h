@@ -62,22 +62,19 @@ cudaError_t gemm_i8x2(const GemmArgs& g, cudaStream_t stream);
 
 // x f32 [m, k] (rows ldx floats apart) -> hi, lo, scale (the oracle's quantize_x2 rule).
 #ifdef __CUDACC__
-// One value's split-int8 pair: hi = round(x / d) clamped to [-127, 127], lo = round((x - hi d)
-// * 254 / d) clamped; id = 1 / d and id_lo = 254 / d as the row's quantizer computes them.
-// An integral float in [-127, 127] as int8 without the conversion unit: h + 1.5 * 2^23 is exact
-// and its low byte is h in two's complement.
-__device__ __forceinline__ int8_t small_int_to_i8(float h) {
-    return static_cast<int8_t>(__float_as_int(__fadd_rn(h, 12582912.0f)) & 0xff);
-}
-
+// One value's split-int8 pair: hi = x / d rounded to the nearest integer (halves to even), lo =
+// (x - hi d) * 254 / d rounded the same way; id = 1 / d and id_lo = 254 / d as the row's quantizer
+// computes them. |x id| and |e id_lo| stay below 127.5 for finite rows (|x| <= 127 d to within
+// a few ulp, |e| <= d / 2 likewise), so both levels land in [-127, 127] without a clamp. Adding
+// 1.5 * 2^23 rounds to the nearest integer exactly and leaves it in the low byte of the sum's
+// bits (two's complement), all on the FMA and integer pipes.
 __device__ __forceinline__ void quant_split_one(float x, float d, float id, float id_lo, int8_t& h8, int8_t& l8) {
-    float h = roundf(__fmul_rn(x, id));
-    h = fminf(fmaxf(h, -127.0f), 127.0f);
+    const float uh = __fadd_rn(__fmul_rn(x, id), 12582912.0f);
+    const float h = __fsub_rn(uh, 12582912.0f);
     const float e = __fmaf_rn(-h, d, x);
-    float l = roundf(__fmul_rn(e, id_lo));
-    l = fminf(fmaxf(l, -127.0f), 127.0f);
-    h8 = small_int_to_i8(h);
-    l8 = small_int_to_i8(l);
+    const float ul = __fadd_rn(__fmul_rn(e, id_lo), 12582912.0f);
+    h8 = static_cast<int8_t>(__float_as_int(uh) & 0xff);
+    l8 = static_cast<int8_t>(__float_as_int(ul) & 0xff);
 }
 
 

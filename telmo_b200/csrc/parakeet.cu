@@ -133,6 +133,7 @@ struct Parakeet {
     bool finalized = false;
     int decoder = 1;       // 1: the persistent kernel where the model and device allow it; 0: phases
     int last_decoder = -1;  // which one the last decode ran
+    int withhold_cta = -1;  // the next persistent decode's barrier test (telmo_parakeet_test_barrier_timeout)
     double phase_ms[kTdtClocks] = {};  // the persistent decoder's clock, last profiled decode
     long phase_passes = 0;
     long launches = 0;
@@ -624,6 +625,8 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
         pa.words = pwords;
         pa.max_passes = bound;
         pa.phase_ns = prof.on ? keys + 2 * U : nullptr;
+        pa.withhold_cta = withhold_cta;
+        withhold_cta = -1;
         size_t smem = 0;
         if (L + 2 <= kTdtMaxMats && tdt_persistent_plan(pa, ctx->sms, &smem)) {
             if (int rc = ctx->cuda(cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * (2 * U + kTdtClocks), s), "tdt"))
@@ -643,7 +646,8 @@ int Parakeet::decode(const float* encoded, const int* frames, int n_utt, uint32_
                 return rc;
             if (int rc = ctx->cuda(cudaStreamSynchronize(s), "tdt")) return rc;
             if (host_words[2] == kTdtErrBarrier)
-                return ctx->fail(TELMO_ERR_CUDA, "parakeet_decode: a grid barrier of the decoder timed out");
+                return ctx->fail(TELMO_ERR_DEVICE_TIMEOUT,
+                                 "parakeet_decode: a grid barrier of the decoder timed out; its tokens are invalid");
             if (host_words[2] != 0) return ctx->fail(TELMO_ERR_CUDA, "parakeet_decode: decoding did not finish");
             last_decoder = 1;
             if (total) *total = host_words[1];
@@ -1052,6 +1056,15 @@ extern "C" int telmo_parakeet_set_decoder(telmo_parakeet* pp, int persistent) {
     if (!p) return TELMO_ERR_ARGUMENT;
     if (persistent != 0 && persistent != 1) return p->ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_set_decoder: 0 or 1");
     p->decoder = persistent;
+    return TELMO_OK;
+}
+
+extern "C" int telmo_parakeet_test_barrier_timeout(telmo_parakeet* pp, int cta) {
+    auto* p = reinterpret_cast<Parakeet*>(pp);
+    if (!p) return TELMO_ERR_ARGUMENT;
+    if (cta < 0 || cta >= p->ctx->sms)
+        return p->ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_test_barrier_timeout: no CTA %d", cta);
+    p->withhold_cta = cta;
     return TELMO_OK;
 }
 

@@ -144,6 +144,7 @@ struct TdtPersistentArgs {
     long long max_passes = 0;
     int ring_offset = 0;  // shared memory: the weight units, then the warps' rings
     int chunk = 0;        // k bytes per ring stage: 128 where every k allows, else 64
+    int withhold_cta = -1;  // a test of the timeout path: this CTA never arrives at the first grid barrier
 };
 
 // Assigns every matrix's 8-row units to `sms` CTAs and sizes the shared memory; false if the

@@ -1,9 +1,9 @@
 // quant.cu -- split-int8 quantization of activation rows, the A operand of the int8 GEMM.
 //
-// Each row x of k values becomes s * (hi + lo / 254): s = amax / 127 and hi = round(x / s)
-// clamped to [-127, 127], exactly as quantize_row_int8 computes a weight row
-// (src/quant.rs:190-198), then lo = round((x - hi * s) * 254 / s), the residual at 254 times
-// finer steps. One warp per row; the f32 steps match oracle_quantize_x2 bit for bit.
+// Each row x of k values becomes s * (hi + lo / 254): s = amax / 127 as quantize_row_int8 sets a
+// weight row's (src/quant.rs:190-198), hi = x / s rounded to the nearest integer (halves to
+// even), then lo = (x - hi * s) * 254 / s rounded the same way, the residual at 254 times finer
+// steps. One warp per row; the f32 steps match oracle_quantize_x2 bit for bit.
 #include "kernels.h"
 
 namespace telmo {

@@ -97,30 +97,33 @@ template <int C, int P>
 __device__ __forceinline__ void layer_norm_regs(float4 (&v)[C], int d, int off, const float* __restrict__ gamma,
                                                 const float* __restrict__ beta, float eps, int lane,
                                                 RowReduce<P>& red) {
-    // Both moments in one pass (f64 sums of the values and of their squares): the variance as
-    // E[x^2] - mean^2 agrees with the reference's two-pass f64 variance to about 1e-16 relative
-    // for the encoder's rows (|mean| within a few standard deviations), and the row is read and
-    // reduced once.
-    double s = 0.0, q = 0.0;
+    // Both moments in one pass, reduced in f64 over f32 partial sums of each lane's values (the
+    // reference sums in f64 throughout; the f32 partials of at most 16 values and the one-pass
+    // variance E[x^2] - mean^2 move mean and rstd by about 1e-7 relative for the encoder's rows,
+    // |mean| within a few standard deviations). The normalised value is formed in f32 from the
+    // rounded mean and rstd, within a few ulp of the reference's f64 (x - mean) * rstd rounded to
+    // f32. This keeps the conversion unit, which f64 per-value arithmetic saturates, almost idle.
+    float s32 = 0.0f, q32 = 0.0f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-        const double a = v[c].x, b = v[c].y, e = v[c].z, f = v[c].w;
-        s += (a + b) + (e + f);
-        q = fma(a, a, fma(b, b, fma(e, e, fma(f, f, q))));
+        s32 = __fadd_rn(s32, __fadd_rn(__fadd_rn(v[c].x, v[c].y), __fadd_rn(v[c].z, v[c].w)));
+        q32 = __fmaf_rn(v[c].x, v[c].x, __fmaf_rn(v[c].y, v[c].y, __fmaf_rn(v[c].z, v[c].z, __fmaf_rn(v[c].w, v[c].w, q32))));
     }
+    double s = s32, q = q32;
     red.sum2(s, q, lane);
     const double mean = s / d;
     const double var = fmax(q / d - mean * mean, 0.0);
-    const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
+    const float mf = static_cast<float>(mean);
+    const float rf = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
 #pragma unroll
     for (int c = 0; c < C; ++c) {
         const int i = off + (c * 32 + lane) * 4;
         const float4 g = *reinterpret_cast<const float4*>(gamma + i);
         const float4 b = *reinterpret_cast<const float4*>(beta + i);
-        v[c].x = __fadd_rn(__fmul_rn(static_cast<float>((v[c].x - mean) * rstd), g.x), b.x);
-        v[c].y = __fadd_rn(__fmul_rn(static_cast<float>((v[c].y - mean) * rstd), g.y), b.y);
-        v[c].z = __fadd_rn(__fmul_rn(static_cast<float>((v[c].z - mean) * rstd), g.z), b.z);
-        v[c].w = __fadd_rn(__fmul_rn(static_cast<float>((v[c].w - mean) * rstd), g.w), b.w);
+        v[c].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].x, mf), rf), g.x), b.x);
+        v[c].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].y, mf), rf), g.y), b.y);
+        v[c].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].z, mf), rf), g.z), b.z);
+        v[c].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c].w, mf), rf), g.w), b.w);
     }
 }
 

@@ -161,7 +161,7 @@ __device__ bool grid_sync(const TdtPersistentArgs& a, unsigned& gen) {
         const unsigned target = (gen + 1) * gridDim.x;
         unsigned* count = a.words + kWBarCount;
         __threadfence();
-        atomicAdd(count, 1u);
+        if (gen != 0 || static_cast<int>(blockIdx.x) != a.withhold_cta) atomicAdd(count, 1u);
         const uint64_t t0 = global_ns();
         uint32_t polls = 0;
         int good = 1;

@@ -214,6 +214,12 @@ class Parakeet:
         """1/True: the persistent decoder kernel (the default); 0/False: per-phase launches."""
         check(_lib.load().telmo_parakeet_set_decoder(self._h, int(persistent)), self.ctx.handle)
 
+    def test_barrier_timeout(self, cta: int = 0):
+        """Makes the next persistent decode's first grid barrier run out (CTA `cta` never
+        arrives): that decode raises TelmoError with TELMO_ERR_DEVICE_TIMEOUT after about a
+        second, and the model and context stay usable. A test of the failure path."""
+        check(_lib.load().telmo_parakeet_test_barrier_timeout(self._h, int(cta)), self.ctx.handle)
+
     def last_decoder(self) -> int:
         """1 if the last decode ran the persistent kernel, 0 per-phase launches, -1 none yet."""
         return _lib.load().telmo_parakeet_last_decoder(self._h)

@@ -364,3 +364,35 @@ def test_predict_rejects_tokens_outside_the_vocabulary(tiny):
     pr = torch.zeros((2, h), device="cuda")
     with pytest.raises(TelmoError):
         gpu.predict([0, gpu.config["vocab"]], st, pr)
+
+
+def test_decoder_barrier_timeout_is_reported_and_the_context_recovers(tiny):
+    # The persistent decoder's grid barriers wait at most about a second. One CTA withholds its
+    # arrival at the first barrier (a flag nothing else sets; no copies or MMAs are in flight
+    # there): every CTA's wait runs out, the kernel returns, and the decode reports
+    # TELMO_ERR_DEVICE_TIMEOUT. The same context then checks clean and decodes as before.
+    import time
+    import torch
+    from telmo_b200 import TelmoError
+    from telmo_b200._lib import TELMO_ERR_DEVICE_TIMEOUT
+    gpu, ref = tiny
+    encs = [ref.encode(_features(r, 95 + i)) for i, r in enumerate([203, 57])]
+    frames = [e.shape[0] for e in encs]
+    enc = torch.from_numpy(np.concatenate(encs)).cuda()
+    gpu.set_decoder(True)
+    want = gpu.decode(enc, frames)
+    assert gpu.last_decoder() == 1
+    gpu.test_barrier_timeout(0)
+    t0 = time.perf_counter()
+    with pytest.raises(TelmoError) as e:
+        gpu.decode(enc, frames)
+    assert e.value.status == TELMO_ERR_DEVICE_TIMEOUT and "barrier" in str(e.value)
+    assert 0.5 < time.perf_counter() - t0 < 30.0
+    gpu.ctx.check()
+    got = gpu.decode(enc, frames)
+    gpu.ctx.check()
+    assert gpu.last_decoder() == 1
+    assert [[(t.id, t.frame, t.duration) for t in u] for u in got] == \
+        [[(t.id, t.frame, t.duration) for t in u] for u in want]
+    with pytest.raises(TelmoError):
+        gpu.test_barrier_timeout(-1)
