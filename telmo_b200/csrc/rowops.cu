@@ -153,7 +153,7 @@ __device__ __forceinline__ void quantize_regs(const float4 (&v)[C], int off, int
 // z quantized into q if q.hi given. P warps per row of d = 128 * C values (each holding C / P
 // float4 per lane), 8 warps per block.
 template <int C, int P>
-__global__ void __launch_bounds__(256) ln_chain_kernel(const float* __restrict__ x, int m, int d,
+__global__ void __launch_bounds__(256, 4) ln_chain_kernel(const float* __restrict__ x, int m, int d,
                                                        const float* __restrict__ ga, const float* __restrict__ ba,
                                                        float* __restrict__ y_out, const float* __restrict__ gb,
                                                        const float* __restrict__ bb, QuantAct q, float eps) {
@@ -413,7 +413,7 @@ cudaError_t ln_chain(const float* x, int m, int d, const float* ga, const float*
         TELMO_LN_CASE(1, 1)
         TELMO_LN_CASE(2, 1)
         TELMO_LN_CASE(4, 1)
-        TELMO_LN_CASE(8, 2)
+        TELMO_LN_CASE(8, 1)
         TELMO_LN_CASE(12, 2)
         TELMO_LN_CASE(16, 2)
         default: return cudaErrorInvalidValue;
