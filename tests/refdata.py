@@ -2,8 +2,9 @@
 
 The reference keeps golden feature tensors for its front ends beside LibriSpeech and FLEURS
 clips (tests/goldens/<model>/ in the telmo source tree). They are read in place when a copy of
-the reference source is present (at ``TELMO_REFERENCE``, else at REFERENCE's default below); the
-clips are never copied into this repository.
+the telmo source is present: at the path in ``TELMO_REFERENCE``, else in a checkout named
+``reference`` beside this repository. Without one the tests that need them skip. The clips are
+never copied into this repository.
 """
 
 from __future__ import annotations
@@ -15,7 +16,8 @@ import wave
 
 import numpy as np
 
-REFERENCE = os.environ.get("TELMO_REFERENCE", "/root/reference")
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REFERENCE = os.environ.get("TELMO_REFERENCE") or os.path.join(os.path.dirname(_REPO), "reference")
 GOLDENS = os.path.join(REFERENCE, "tests", "goldens")
 
 _DTYPES = {"F32": np.float32, "F64": np.float64, "I64": np.int64, "I32": np.int32,
