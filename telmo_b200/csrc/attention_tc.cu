@@ -31,6 +31,7 @@
 // issue only the key and position columns they use, and blocks of at most 64 rows load only
 // those rows. Every wait is bounded; on timeout the
 // kernel records kErrWaitTimeout in the error word and returns.
+#include "attention_tc.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 #include "rowops.h"
@@ -48,53 +49,16 @@ constexpr int T = 128;    // query rows and keys per block (Granite's context)
 constexpr int HD = 128;   // head size
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kBox = 128 * 128;              // one 128-row x 64-fp16 box, 128-byte swizzle (16 KB)
-constexpr int kOperand = 4 * kBox;           // hi and lo planes, two 64-column halves each
+using namespace tc_attention;
 constexpr int kRelHalf = 2 * kBox;           // 256 positions x 64 fp16
-constexpr int kWindowBytes = 32 * 64 * 4;    // one warp's position window: 32 rows x 64 f32
 constexpr uint32_t kColS = 0, kColPos = 128, kColP = 128, kColO = 384, kTmemCols = 512;
 constexpr int kSmemBytes = 3 * kOperand + 256 * 4 + 2 * 2 * 128 * 8 + 128 + 1024;
-constexpr float kLog2e = 1.4426950408889634f;
 
 static_assert(kEpiWarps * kWindowBytes <= kOperand, "the position windows live in K's buffer");
 
 struct Bars {
     uint64_t q_full, k_full, r_full, v_full, s_done, p_full, o_done, o_free;
 };
-
-__device__ __forceinline__ void record_error(uint32_t* error, uint32_t code) {
-    if (error) atomicCAS(error, 0u, code);
-}
-
-// The four boxes of one operand (hi, lo planes; two 64-column halves) at column x.
-__device__ __forceinline__ void load_operand(const CUtensorMap* map, uint64_t* bar, uint8_t* dst, int x, int y_hi,
-                                             int y_lo) {
-    tma_load_2d(map, bar, dst, x, y_hi);
-    tma_load_2d(map, bar, dst + kBox, x + 64, y_hi);
-    tma_load_2d(map, bar, dst + 2 * kBox, x, y_lo);
-    tma_load_2d(map, bar, dst + 3 * kBox, x + 64, y_lo);
-}
-
-// A probability p (0 <= p <= 1) rounded to fp16's 11 significant bits, to nearest even, on the
-// integer pipe -- the value fp16(p) stands for, for p >= 2^-14; below that 0, so the low part
-// carries p. p - f16_high(p) is exact in f32.
-__device__ __forceinline__ float f16_high(float p) {
-    const uint32_t u = __float_as_uint(p);
-    const uint32_t r = (u + 0x0FFFu + ((u >> 13) & 1u)) & ~0x1FFFu;
-    return p >= 6.103515625e-05f ? __uint_as_float(r) : 0.0f;
-}
-
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);  // a in the low half
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// The epilogue warps' named barrier (barrier 0 is __syncthreads).
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
-
-// A warp's position window: row l (a lane) holds 64 f32 with 16-byte chunk m at chunk m ^ (l % 8),
-// which keeps both the lanes' row writes and their diagonal reads free of bank conflicts.
-__device__ __forceinline__ int win_index(int l, int e) { return l * 64 + ((((e >> 2) ^ l) & 7) | (e >> 2 & 8)) * 4 + (e & 3); }
 
 __global__ void __launch_bounds__(kThreads, 1)
 granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_qkv64,
@@ -291,7 +255,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 __syncwarp();
             }
             red_max[half * T + row] = mx;
-            epi_sync();
+            epi_sync<32 * kEpiWarps>();
             mx = fmaxf(red_max[row], red_max[T + row]);
             const float mxl = __fmul_rn(mx, kLog2e);
             // The row sum in f64 (as the reference) over f32 partial sums of 8 exponentials.
@@ -308,7 +272,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 else s0 += static_cast<double>(part);
             }
             red_sum[half * T + row] = s0 + s1;
-            epi_sync();
+            epi_sync<32 * kEpiWarps>();
             const float inv = static_cast<float>(1.0 / (red_sum[row] + red_sum[T + row]));
             // P into TMEM (pos's first 128 columns) as the O product's A operand: fp16 pairs of
             // consecutive keys per column, hi plane in columns 0..63, lo plane in 64..127.

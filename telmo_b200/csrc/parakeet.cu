@@ -356,9 +356,10 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     }
     if (r1 * std::max(ch, 1) > (int64_t(1) << 31) || feat_at * f0 > (int64_t(1) << 31))
         return ctx->fail(TELMO_ERR_ARGUMENT, "parakeet_encode: batch too large");
-    // The tensor-core attention takes 64 query rows per task, the other kernel 32.
+    // The tcgen05 attention takes 128 query rows per task, the mma.sync one 64, the other 32.
     const bool mma = txl_attention_mma_supported(hd);
-    const int q_rows = mma ? 64 : 32;
+    const bool tc = txl_attention_tc_supported(hd);
+    const int q_rows = tc ? 128 : mma ? 64 : 32;
     if (!mma && txl_attention_smem(hd, tmax) > 227 * 1024)
         return ctx->fail(TELMO_ERR_UNSUPPORTED, "parakeet_encode: an utterance of %d frames is too long", tmax);
     int at = 0;
@@ -378,7 +379,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
                          quant_bytes(M, std::max(ld_lin, ld_main)) + 3 * piece<float>(static_cast<size_t>(M) * d) +
                          piece<float>(static_cast<size_t>(M) * big_ld) + 2 * piece<float>(static_cast<size_t>(P) * d) +
                          quant_bytes(P, static_cast<int64_t>(round_up(d, 16))) + piece<float>(static_cast<size_t>(P) * c.heads) +
-                         task_bytes;
+                         piece<float>(static_cast<size_t>(M) * c.heads) + task_bytes;
     if (int rc = enc_arena.reserve(ctx, bytes)) return rc;
     Arena& A = enc_arena;
     float* sub_a = A.take<float>(static_cast<size_t>(r1) * ch);
@@ -396,6 +397,7 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
     float* pp = A.take<float>(static_cast<size_t>(P) * d);
     const QuantAct q_pos = quant_piece(A, P, static_cast<int64_t>(round_up(d, 16)));
     float* cpos = A.take<float>(static_cast<size_t>(P) * c.heads);
+    float* ukey = A.take<float>(static_cast<size_t>(M) * c.heads);
     SubTask* front_dev = A.take<SubTask>(front.size());
     SubTask* dw2_dev = A.take<SubTask>(dw2t.size());
     TxlTask* att_dev = A.take<TxlTask>(att.size());
@@ -462,7 +464,12 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
         if (int rc = gemm(q_pos, P, L.pos, nullptr, pp, d, kActNone, 1.0f, 0, s, kind)) return rc;
         const __half* qkv16 = reinterpret_cast<const __half*>(big);
         const __half* pp16 = reinterpret_cast<const __half*>(pp);
-        if (mma) {
+        if (tc) {
+            ++launches;
+            if (int rc = ctx->cuda(txl_bias_terms(pp16, P, qkv16, M, c.heads, L.bias_u.p, L.bias_v.p, cpos, ukey, s),
+                                   "parakeet bias terms"))
+                return rc;
+        } else if (mma) {
             ++launches;
             if (int rc = ctx->cuda(txl_pos_bias(pp16, static_cast<int64_t>(P) * d, P, c.heads, hd, L.bias_u.p,
                                                 L.bias_v.p, cpos, s),
@@ -472,10 +479,12 @@ int Parakeet::encode(const float* feats, const int* rows, int n_utt, float* out,
         if (prof.on) prof.begin(kProfAttention, s);
         ++launches;
         const cudaError_t ae =
-            mma ? txl_attention_mma(qkv16, static_cast<int64_t>(M) * 3 * d, pp16, static_cast<int64_t>(P) * d, cpos, P,
-                                    att_dev, static_cast<int>(att.size()), c.heads, hd, L.bias_u.p, scale, attn, s)
-                : txl_attention(big, pp, att_dev, static_cast<int>(att.size()), c.heads, hd, tmax, L.bias_u.p,
-                                L.bias_v.p, scale, attn, s);
+            tc    ? txl_attention_tc(qkv16, M, pp16, P, cpos, ukey, att_dev, static_cast<int>(att.size()), c.heads, hd,
+                                     scale, attn, ctx->error_word, s)
+            : mma ? txl_attention_mma(qkv16, static_cast<int64_t>(M) * 3 * d, pp16, static_cast<int64_t>(P) * d, cpos,
+                                      P, att_dev, static_cast<int>(att.size()), c.heads, hd, L.bias_u.p, scale, attn, s)
+                  : txl_attention(big, pp, att_dev, static_cast<int>(att.size()), c.heads, hd, tmax, L.bias_u.p,
+                                  L.bias_v.p, scale, attn, s);
         if (int rc = ctx->cuda(ae, "parakeet attention")) return rc;
         if (prof.on) prof.end(kProfAttention, s);
         if (int rc = quant(attn, d, M, d, q, s)) return rc;

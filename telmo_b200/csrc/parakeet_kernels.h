@@ -68,6 +68,19 @@ cudaError_t txl_attention_mma(const __half* qkv, int64_t plane, const __half* po
 cudaError_t txl_pos_bias(const __half* pos, int64_t pplane, int npos, int heads, int hd, const float* bias_u,
                          const float* bias_v, float* cpos, cudaStream_t s);
 
+// The same on the tcgen05 tensor cores (txl_attention_tc.cu), for head size 128, over tasks of
+// 128 query rows: qkv [rows, 3d] and pos [npos, d] as fp16 high/low planes (each low plane right
+// after its high one), cv [heads, npos] and uk [heads, rows] from txl_bias_terms; a wait that times
+// out records kErrWaitTimeout in `error`.
+bool txl_attention_tc_supported(int hd);
+cudaError_t txl_attention_tc(const __half* qkv, int rows, const __half* pos, int npos, const float* cv, const float* uk,
+                             const TxlTask* tasks, int n_tasks, int heads, int hd, float scale, float* att,
+                             uint32_t* error, cudaStream_t s);
+// cv[h][p] = bias_v . pos[p] and uk[h][r] = bias_u . k[r] over head h's columns (the scores' bias
+// parts: (q + u) . k + (q + v) . pos = q . k + uk + q . pos + cv).
+cudaError_t txl_bias_terms(const __half* pos, int npos, const __half* qkv, int rows, int heads, const float* bias_u,
+                           const float* bias_v, float* cv, float* uk, cudaStream_t s);
+
 // One greedy TDT pass is joint_prep -> joint product -> decide_prep -> LSTM product ->
 // cell_prep per layer (the last followed by the pred_proj product). Each prep kernel runs one
 // CTA per utterance and leaves the next product's split-int8 operand rows in q; state is
