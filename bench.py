@@ -16,6 +16,8 @@ Workloads (seeded synthetic data, telmo_b200/synthetic.py):
            sharded and batched as granite.
   linear   config 1: one int8-weight linear, A f32 [1500, 1024] x W int8 [4096, 1024] + bias
            (--shape M,K,N for another product shape with the same distributions).
+  load     the config-5 Granite model loaded from a pack in host memory: the median load time
+           from the reference's panel layout and from a device-layout pack (no host repack).
 
 `--impl reference` times the reference's CPU path for the same workload: the oracle's C
 restatement of telmo's CPU path (the reference is Rust and cannot be built here) on all host
@@ -656,13 +658,66 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_load(args, rank):
+    """Model load time: the config-5 Granite model's pack, held in host memory, to a finalized model
+    on the device -- once from the reference's panel layout (repacked into rows on the host) and
+    once from the device-layout pack (copied as it is). Wall clock around the load call, with the
+    device synchronized on both sides; the median of the timed loads."""
+    if rank != 0:
+        return
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference maps its pack and reads the "
+                          "panels in place on the CPU; it has no device load to time"}), flush=True)
+        return
+    import torch
+    import telmo_b200
+    from telmo_b200 import synthetic
+    from telmo_b200.granite import Granite
+    from telmo_b200.pack import Pack, granite_config_json, write_pack
+    torch.cuda.set_device(0)
+    ctx = telmo_b200.Context(0)
+    cfg = synthetic.granite_config()
+    entries = synthetic.granite_entries(cfg, seed=1, scales="spec", precision=args.precision)
+    panel = Pack(data=write_pack("granite-speech-ctc", dict(entries, **{"config.json": granite_config_json(cfg)})))
+    del entries
+    t0 = time.perf_counter()
+    device = panel.to_device()
+    convert_s = time.perf_counter() - t0
+
+    def load(pack):
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        model = Granite.from_pack(ctx, pack)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t
+        model.close()
+        return dt
+
+    for _ in range(args.warmup):
+        load(panel)
+        load(device)
+    panel_s = statistics.median([load(panel) for _ in range(args.steps)])
+    device_s = statistics.median([load(device) for _ in range(args.steps)])
+    line = {
+        "metric": "model load seconds (pack in host memory -> finalized model on the device)",
+        "value": round(device_s, 4), "unit": "s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(device_s * 1e3, 2), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (random-init weights)",
+        "config": {"workload": "load-config5-granite", "weights": args.precision,
+                   "layout": "device-layout pack"},
+        "panel_pack_s": round(panel_s, 4), "convert_s": round(convert_s, 4), "impl": "ours",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="granite")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["load"], default="granite",
+                    help="load: model load time from a panel pack and from a device-layout pack")
     ap.add_argument("--shape", default="",
                     help="linear: M,K,N of another product (config 1's distributions), e.g. "
                          "53000,1024,4096 for an encoder's feed-forward up-projection")
@@ -676,7 +731,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.workload == "load":
+        run_load(args, rank)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)

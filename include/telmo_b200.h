@@ -403,6 +403,7 @@ typedef struct telmo_pack telmo_pack;
 #define TELMO_PACK_MATRIX 0
 #define TELMO_PACK_F32 1
 #define TELMO_PACK_BYTES 2
+#define TELMO_PACK_DEVICE 3 /* this build's extension: an 8-bit matrix in the device layout */
 int telmo_pack_open(const char *path, telmo_pack **out);
 int telmo_pack_from_bytes(const void *data, size_t len, telmo_pack **out);
 void telmo_pack_free(telmo_pack *p);
@@ -417,12 +418,24 @@ int telmo_pack_entry_info(const telmo_pack *p, size_t i, const char **name, int 
                           size_t *n, size_t *k, size_t *bytes);
 /* A bytes entry's data (config.json, tokenizer.json), valid while the pack lives. */
 int telmo_pack_bytes(const telmo_pack *p, const char *name, const void **data, size_t *len);
+/* A pack whose Int8 and Q8_0 matrices are stored in the device layout (TELMO_PACK_DEVICE; no
+ * counterpart in the reference, which reads its panels on the CPU): n rows of round_up(k, 16) int8
+ * values with one f32 scale per row, and for Q8_0 a second level of rows (w = s (hi + lo / 254)),
+ * the columns in the order the model's kernels read them. Loading such a pack copies each matrix
+ * to the device as it is instead of repacking panels on the host, and gives the same model bit
+ * for bit. Runs on the host (no GPU); the other entries are kept as they are. A device entry is
+ * {"type": "device", "precision", "n", "k", "offset", "bytes", "scales_offset", "scales_bytes"}
+ * plus "lo_offset" and "lo_bytes" for Q8_0. The reference's reader refuses these packs. */
+int telmo_pack_to_device(const telmo_pack *src, telmo_pack **out);
+/* Writes the pack's file to path. */
+int telmo_pack_save(const telmo_pack *p, const char *path);
 /* Config::from_json (src/granite.rs:60-146, src/parakeet.rs:70-141) of a model's config.json. */
 int telmo_granite_config_from_json(const char *json, size_t len, telmo_granite_config *out);
 int telmo_parakeet_config_from_json(const char *json, size_t len, telmo_parakeet_config *out);
 /* Granite::from_pack / Parakeet::from_pack (src/granite.rs:225-231, src/parakeet.rs:691-795) onto
  * the device: the config from config.json, every entry the model knows uploaded as it is stored
- * (Int8 or Q8_0 matrices), the model finalized; entries it does not know are ignored. */
+ * (Int8 or Q8_0 matrices, in panels or in the device layout), the model finalized; entries it
+ * does not know are ignored. */
 int telmo_granite_load_pack(telmo_ctx *ctx, const telmo_pack *p, telmo_granite **out);
 int telmo_parakeet_load_pack(telmo_ctx *ctx, const telmo_pack *p, telmo_parakeet **out);
 

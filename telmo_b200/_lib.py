@@ -85,6 +85,8 @@ SIGNATURES = {
     "telmo_pack_entry_count": (_sz, [_vp]),
     "telmo_pack_entry_info": (_c.c_int, [_vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp]),
     "telmo_pack_bytes": (_c.c_int, [_vp, _c.c_char_p, _vp, _vp]),
+    "telmo_pack_to_device": (_c.c_int, [_vp, _vp]),
+    "telmo_pack_save": (_c.c_int, [_vp, _c.c_char_p]),
     "telmo_granite_config_from_json": (_c.c_int, [_c.c_char_p, _sz, _vp]),
     "telmo_parakeet_config_from_json": (_c.c_int, [_c.c_char_p, _sz, _vp]),
     "telmo_granite_load_pack": (_c.c_int, [_vp, _vp, _vp]),

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 using namespace telmo;
@@ -230,28 +231,22 @@ void encode_q8_0_panels(const float* rows, size_t n, size_t k, int8_t* values, f
     }
 }
 
-int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
-                   const float* scales, DevWeights* out, const int* col_perm) {
-    if (precision != TELMO_PRECISION_INT8 && precision != TELMO_PRECISION_Q8_0)
-        return ctx->fail(TELMO_ERR_UNSUPPORTED,
-                         "precision %d: this build runs int8 weights (TELMO_PRECISION_INT8, "
-                         "TELMO_PRECISION_Q8_0) only",
-                         precision);
-    if (!panel_values || !scales || n == 0 || k == 0 || n > (1u << 30) || k > (1u << 30))
-        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: bad sizes n=%zu k=%zu or null data", n, k);
-    const bool q8 = precision == TELMO_PRECISION_Q8_0;
-    if (q8 && k % 32)
-        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: Q8_0 needs inputs in multiples of 32 (k=%zu)", k);
-    const size_t ld = round_up(k, 16);
-    std::vector<int8_t> rows(n * ld, 0), lo(q8 ? n * ld : 0, 0);
-    std::vector<float> sc(n);
+namespace {
+
+// Round to the nearest integer, halves to even, for |x| < 2^22: adding 1.5 * 2^23 leaves no
+// fraction bits, so the sum is rounded by the addition itself (IEEE round-to-nearest-even).
+inline float round_even(float x) { return (x + 12582912.0f) - 12582912.0f; }
+inline float clamp127(float x) { return x < -127.0f ? -127.0f : (x > 127.0f ? 127.0f : x); }
+
+void encode_device_row_range(bool q8, size_t o0, size_t o1, size_t k, const int8_t* v, const float* scales,
+                             const int* col_perm, int8_t* rows, int8_t* lo, float* sc) {
+    const size_t ld = round_up(k, 16), blocks = k / 32;
     std::vector<float> w(q8 ? k : 0);
-    const int8_t* v = static_cast<const int8_t*>(panel_values);
-    const size_t blocks = k / 32;
-    for (size_t o = 0; o < n; ++o) {
+    for (size_t o = o0; o < o1; ++o) {
         const size_t p = o / 16, j = o % 16;
         const int8_t* src = v + p * k * 16 + j;
-        int8_t* dst = rows.data() + o * ld;
+        int8_t* dst = rows + o * ld;
+        std::fill(dst, dst + ld, int8_t(0));
         if (!q8) {
             for (size_t i = 0; i < k; ++i) dst[i] = src[(col_perm ? col_perm[i] : i) * 16];
             sc[o] = scales[p * 16 + j];
@@ -267,34 +262,91 @@ int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* pane
         for (size_t i = 0; i < k; ++i) {
             const size_t c = col_perm ? static_cast<size_t>(col_perm[i]) : i;
             w[i] = static_cast<float>(src[c * 16]) * scales[(p * blocks + c / 32) * 16 + j];
-            amax = std::fmax(amax, std::fabs(w[i]));
+            const float a = std::fabs(w[i]);
+            amax = a > amax ? a : amax;
         }
         const float d = amax / 127.0f;
         const float id = d != 0.0f ? 1.0f / d : 0.0f;
         const float id_lo = id * 254.0f;
-        int8_t* dlo = lo.data() + o * ld;
+        int8_t* dlo = lo + o * ld;
+        std::fill(dlo, dlo + ld, int8_t(0));
         for (size_t i = 0; i < k; ++i) {
-            const float h = std::fmin(std::fmax(std::nearbyint(w[i] * id), -127.0f), 127.0f);
-            const float e = std::fma(-h, d, w[i]);
-            const float l = std::fmin(std::fmax(std::nearbyint(e * id_lo), -127.0f), 127.0f);
+            const float h = clamp127(round_even(w[i] * id));
+            // w - h s with one rounding: h s (7 by 24 significant bits) and the difference, which
+            // is near 0 against w, are exact in f64.
+            const float e = static_cast<float>(static_cast<double>(w[i]) - static_cast<double>(h) * d);
+            const float l = clamp127(round_even(e * id_lo));
             dst[i] = static_cast<int8_t>(h);
             dlo[i] = static_cast<int8_t>(l);
         }
         sc[o] = d;
     }
+}
+
+}  // namespace
+
+void encode_device_rows(int precision, size_t n, size_t k, const void* panel_values, const float* scales,
+                        const int* col_perm, int8_t* rows, int8_t* lo, float* sc) {
+    // Rows are independent: up to 16 host threads take contiguous ranges of them.
+    const bool q8 = precision == TELMO_PRECISION_Q8_0;
+    const int8_t* v = static_cast<const int8_t*>(panel_values);
+    const size_t work = n * k * (q8 ? 8 : 1);
+    const size_t hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t threads = std::min<size_t>({hw, 16, std::max<size_t>(1, work >> 21), n});
+    if (threads <= 1) {
+        encode_device_row_range(q8, 0, n, k, v, scales, col_perm, rows, lo, sc);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const size_t per = (n + threads - 1) / threads;
+    for (size_t t = 0; t < threads; ++t) {
+        const size_t o0 = t * per, o1 = std::min(n, o0 + per);
+        if (o0 >= o1) break;
+        pool.emplace_back(encode_device_row_range, q8, o0, o1, k, v, scales, col_perm, rows, lo, sc);
+    }
+    for (auto& th : pool) th.join();
+}
+
+int upload_device_rows(Ctx* ctx, int precision, size_t n, size_t k, const int8_t* rows, const int8_t* lo,
+                       const float* sc, DevWeights* out) {
+    const bool q8 = precision == TELMO_PRECISION_Q8_0;
+    const size_t ld = round_up(k, 16);
     out->n = static_cast<int>(n);
     out->k = static_cast<int>(k);
     out->ld = static_cast<int64_t>(ld);
-    if (int rc = ctx->cuda(cudaMalloc(&out->values, rows.size()), "weights")) return rc;
+    if (int rc = ctx->cuda(cudaMalloc(&out->values, n * ld), "weights")) return rc;
     if (int rc = ctx->cuda(cudaMalloc(&out->scales, n * sizeof(float)), "weights")) return rc;
-    if (int rc = ctx->cuda(cudaMemcpy(out->values, rows.data(), rows.size(), cudaMemcpyHostToDevice), "weights"))
-        return rc;
+    if (int rc = ctx->cuda(cudaMemcpy(out->values, rows, n * ld, cudaMemcpyHostToDevice), "weights")) return rc;
     if (q8) {
-        if (int rc = ctx->cuda(cudaMalloc(&out->lo_values, lo.size()), "weights")) return rc;
-        if (int rc = ctx->cuda(cudaMemcpy(out->lo_values, lo.data(), lo.size(), cudaMemcpyHostToDevice), "weights"))
-            return rc;
+        if (int rc = ctx->cuda(cudaMalloc(&out->lo_values, n * ld), "weights")) return rc;
+        if (int rc = ctx->cuda(cudaMemcpy(out->lo_values, lo, n * ld, cudaMemcpyHostToDevice), "weights")) return rc;
     }
-    return ctx->cuda(cudaMemcpy(out->scales, sc.data(), n * sizeof(float), cudaMemcpyHostToDevice), "weights");
+    return ctx->cuda(cudaMemcpy(out->scales, sc, n * sizeof(float), cudaMemcpyHostToDevice), "weights");
+}
+
+int check_weight_shape(Ctx* ctx, int precision, size_t n, size_t k) {
+    if (precision != TELMO_PRECISION_INT8 && precision != TELMO_PRECISION_Q8_0)
+        return ctx->fail(TELMO_ERR_UNSUPPORTED,
+                         "precision %d: this build runs int8 weights (TELMO_PRECISION_INT8, "
+                         "TELMO_PRECISION_Q8_0) only",
+                         precision);
+    if (n == 0 || k == 0 || n > (1u << 30) || k > (1u << 30))
+        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: bad sizes n=%zu k=%zu", n, k);
+    if (precision == TELMO_PRECISION_Q8_0 && k % 32)
+        return ctx->fail(TELMO_ERR_ARGUMENT, "weights: Q8_0 needs inputs in multiples of 32 (k=%zu)", k);
+    return TELMO_OK;
+}
+
+int upload_weights(Ctx* ctx, int precision, size_t n, size_t k, const void* panel_values,
+                   const float* scales, DevWeights* out, const int* col_perm) {
+    if (int rc = check_weight_shape(ctx, precision, n, k)) return rc;
+    if (!panel_values || !scales) return ctx->fail(TELMO_ERR_ARGUMENT, "weights: null data");
+    const bool q8 = precision == TELMO_PRECISION_Q8_0;
+    const size_t ld = round_up(k, 16);
+    std::vector<int8_t> rows(n * ld), lo(q8 ? n * ld : 0);
+    std::vector<float> sc(n);
+    encode_device_rows(precision, n, k, panel_values, scales, col_perm, rows.data(), lo.data(), sc.data());
+    return upload_device_rows(ctx, precision, n, k, rows.data(), q8 ? lo.data() : nullptr, sc.data(), out);
 }
 
 void free_weights(DevWeights* w) {

@@ -850,9 +850,11 @@ extern "C" int telmo_granite_create(telmo_ctx* cp, const telmo_granite_config* c
 
 extern "C" void telmo_granite_free(telmo_granite* g) { delete as_granite(g); }
 
-extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int precision, size_t n, size_t k,
-                                        const void* panel_values, const float* scales) {
-    Granite* g = as_granite(gp);
+namespace {
+
+// The checks both matrix setters share: the name, the shape, and exact integers for the relative
+// tables (they feed the attention kernels). On success the old matrix is freed.
+int granite_prepare_matrix(Granite* g, const char* name, int precision, size_t n, size_t k, Granite::Entry* out) {
     if (!g || !name) return TELMO_ERR_ARGUMENT;
     Granite::Entry e = g->find(name);
     if (!e.mat) return g->ctx->fail(TELMO_ERR_MODEL, "granite: no matrix named %s", name);
@@ -867,24 +869,55 @@ extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int
                                 name);
     free_weights(e.mat);
     g->finalized = false;
-    if (int rc = upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat)) return rc;
-    // The relative tables also get an fp16 copy for the tensor-core attention (int8 values are
-    // exact in fp16); the per-position scales stay in the weights' scale vector.
+    *out = e;
+    return TELMO_OK;
+}
+
+// The relative tables also get an fp16 copy for the tensor-core attention (int8 values are exact
+// in fp16); the per-position scales stay in the weights' scale vector. value(o, i) is the table's
+// int8 value at position o, dimension i.
+template <class Value>
+int granite_upload_rel16(Granite* g, const DevWeights* mat, size_t n, size_t k, Value value) {
     for (auto& b : g->blocks) {
-        if (e.mat != &b.rel) continue;
+        if (mat != &b.rel) continue;
         if (b.rel16) cudaFree(b.rel16);
         b.rel16 = nullptr;
         std::vector<__half> rel16(n * k);
-        const int8_t* v = static_cast<const int8_t*>(panel_values);
         for (size_t o = 0; o < n; ++o)
-            for (size_t i = 0; i < k; ++i)
-                rel16[o * k + i] = __float2half(static_cast<float>(v[((o / 16) * k + i) * 16 + o % 16]));
+            for (size_t i = 0; i < k; ++i) rel16[o * k + i] = __float2half(static_cast<float>(value(o, i)));
         if (int rc = g->ctx->cuda(cudaMalloc(&b.rel16, sizeof(__half) * n * k), "granite rel")) return rc;
         return g->ctx->cuda(cudaMemcpy(b.rel16, rel16.data(), sizeof(__half) * n * k, cudaMemcpyHostToDevice),
                             "granite rel");
     }
     return TELMO_OK;
 }
+
+}  // namespace
+
+extern "C" int telmo_granite_set_matrix(telmo_granite* gp, const char* name, int precision, size_t n, size_t k,
+                                        const void* panel_values, const float* scales) {
+    Granite* g = as_granite(gp);
+    Granite::Entry e;
+    if (int rc = granite_prepare_matrix(g, name, precision, n, k, &e)) return rc;
+    if (int rc = upload_weights(g->ctx, precision, n, k, panel_values, scales, e.mat)) return rc;
+    const int8_t* v = static_cast<const int8_t*>(panel_values);
+    return granite_upload_rel16(g, e.mat, n, k, [&](size_t o, size_t i) { return v[((o / 16) * k + i) * 16 + o % 16]; });
+}
+
+namespace telmo {
+
+int granite_set_device_matrix(telmo_granite* gp, const char* name, int precision, size_t n, size_t k,
+                              const int8_t* rows, const int8_t* lo, const float* scales) {
+    Granite* g = as_granite(gp);
+    Granite::Entry e;
+    if (int rc = granite_prepare_matrix(g, name, precision, n, k, &e)) return rc;
+    if (int rc = check_weight_shape(g->ctx, precision, n, k)) return rc;
+    if (int rc = upload_device_rows(g->ctx, precision, n, k, rows, lo, scales, e.mat)) return rc;
+    const size_t ld = round_up(k, 16);
+    return granite_upload_rel16(g, e.mat, n, k, [&](size_t o, size_t i) { return rows[o * ld + i]; });
+}
+
+}  // namespace telmo
 
 extern "C" int telmo_granite_set_vector(telmo_granite* gp, const char* name, size_t len, const float* data) {
     Granite* g = as_granite(gp);

@@ -250,6 +250,8 @@ bool parse_json(const char* data, size_t len, Json& out) {
 constexpr size_t kPrefix = 16, kTrailer = 24, kAlign = 64;
 constexpr uint64_t kMaxIndex = 64ull << 20;
 
+size_t round_up_64(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
 int precision_of(const std::string& name) {
     if (name == "f32") return TELMO_PRECISION_F32;
     if (name == "f16") return TELMO_PRECISION_F16;
@@ -279,6 +281,7 @@ struct PackEntry {
     size_t n = 0, k = 0;
     std::vector<size_t> shape;
     size_t offset = 0, bytes = 0, scales_offset = 0, scales_bytes = 0;
+    size_t lo_offset = 0, lo_bytes = 0;  // a device entry's low level (Q8_0)
 };
 
 }  // namespace telmo
@@ -375,6 +378,21 @@ int parse_pack(telmo_pack& pk) {
                 if (v && expected > SIZE_MAX / v) return fail_pack("Entry " + e.name + " has the wrong size.");
                 expected *= static_cast<size_t>(v);
             }
+        } else if (t == "device") {
+            // This build's extension (the reference has no such kind): an 8-bit matrix already in
+            // the device layout -- n rows of round_up(k, 16) values, n row scales, and for Q8_0 a
+            // low level of rows -- so loading it copies instead of repacking panels.
+            e.kind = TELMO_PACK_DEVICE;
+            const Json* pr = item.get("precision");
+            e.precision = pr && pr->type == Json::kString ? precision_of(pr->text) : -1;
+            if (e.precision != TELMO_PRECISION_INT8 && e.precision != TELMO_PRECISION_Q8_0)
+                return fail_pack("Entry " + e.name + " has a precision the device layout doesn't hold.");
+            if (int rc = num("n", e.n)) return rc;
+            if (int rc = num("k", e.k)) return rc;
+            if (e.n == 0 || e.k == 0 || e.n > (1u << 24) || e.k > (1u << 24) ||
+                (e.precision == TELMO_PRECISION_Q8_0 && e.k % 32))
+                return fail_pack("Entry " + e.name + " has an impossible shape.");
+            expected = e.n * ((e.k + 15) / 16 * 16);
         } else if (t == "bytes") {
             e.kind = TELMO_PACK_BYTES;
         } else {
@@ -396,6 +414,18 @@ int parse_pack(telmo_pack& pk) {
                 return fail_pack("Entry " + e.name + " has the wrong number of scales.");
             if (int rc = num("scales_offset", e.scales_offset)) return rc;
             if (int rc = check_range(e.scales_offset, e.scales_bytes)) return rc;
+        }
+        if (e.kind == TELMO_PACK_DEVICE) {
+            if (int rc = num("scales_bytes", e.scales_bytes)) return rc;
+            if (e.scales_bytes != e.n * 4) return fail_pack("Entry " + e.name + " has the wrong number of scales.");
+            if (int rc = num("scales_offset", e.scales_offset)) return rc;
+            if (int rc = check_range(e.scales_offset, e.scales_bytes)) return rc;
+            if (e.precision == TELMO_PRECISION_Q8_0) {
+                if (int rc = num("lo_bytes", e.lo_bytes)) return rc;
+                if (e.lo_bytes != e.bytes) return fail_pack("Entry " + e.name + " has the wrong size.");
+                if (int rc = num("lo_offset", e.lo_offset)) return rc;
+                if (int rc = check_range(e.lo_offset, e.lo_bytes)) return rc;
+            }
         }
         if (pk.by_name.count(e.name)) return fail_pack("Two entries are named " + e.name + ".");
         pk.by_name[e.name] = pk.entries.size();
@@ -555,6 +585,37 @@ int parakeet_config_from_json(const char* text, size_t len, telmo_parakeet_confi
 
 const uint8_t* entry_data(const telmo_pack* pk, size_t off) { return pk->data.data() + off; }
 
+// ---- writing packs ------------------------------------------------------------------------------
+
+const char* precision_name(int precision) {
+    switch (precision) {
+        case TELMO_PRECISION_F32: return "f32";
+        case TELMO_PRECISION_F16: return "f16";
+        case TELMO_PRECISION_BF16: return "bf16";
+        case TELMO_PRECISION_INT8: return "int8";
+        default: return "q8_0";
+    }
+}
+
+// A JSON string (RFC 8259 section 7): quotes, backslashes and control characters escaped; other
+// bytes (UTF-8) as they are.
+std::string json_string(const std::string& v) {
+    std::string out = "\"";
+    for (unsigned char ch : v) {
+        if (ch == '"' || ch == '\\') {
+            out += '\\';
+            out += static_cast<char>(ch);
+        } else if (ch < 0x20) {
+            char buf[8];
+            snprintf(buf, sizeof buf, "\\u%04x", ch);
+            out += buf;
+        } else {
+            out += static_cast<char>(ch);
+        }
+    }
+    return out + "\"";
+}
+
 }  // namespace
 
 extern "C" int telmo_pack_from_bytes(const void* data, size_t len, telmo_pack** out) {
@@ -619,6 +680,134 @@ extern "C" int telmo_pack_bytes(const telmo_pack* pk, const char* name, const vo
     return TELMO_OK;
 }
 
+extern "C" int telmo_pack_to_device(const telmo_pack* src, telmo_pack** out) {
+    // Every Int8 and Q8_0 matrix re-encoded by the upload's own host routine (encode_device_rows),
+    // so a model loaded from the result holds the same device bytes as one loaded from src. The
+    // file is laid out first and written in place, in one allocation.
+    if (!src || !out) return TELMO_ERR_ARGUMENT;
+    *out = nullptr;
+    std::vector<int> linear_perm;
+    if (src->model == "parakeet-tdt") {
+        const PackEntry* cj = src->find("config.json");
+        if (!cj) return fail_pack("Entry config.json is missing.");
+        telmo_parakeet_config cfg;
+        if (int rc = parakeet_config_from_json(reinterpret_cast<const char*>(entry_data(src, cj->offset)), cj->bytes, &cfg))
+            return rc;
+        linear_perm = parakeet_linear_perm(cfg.sub_channels, cfg.n_mels);
+    }
+    // Layout: each entry's blobs (values; then scales; then a device entry's low level) at the
+    // next 64-byte boundaries, and the index text that names them.
+    struct Placed {
+        int kind = TELMO_PACK_BYTES;
+        size_t at = 0, bytes = 0, s_at = 0, s_bytes = 0, l_at = 0, l_bytes = 0;
+    };
+    std::vector<Placed> placed(src->entries.size());
+    size_t end = kPrefix;
+    auto place = [&](size_t bytes) {
+        const size_t at = round_up_64(end);
+        end = at + bytes;
+        return at;
+    };
+    std::string index = "{\"model\":" + json_string(src->model) + ",\"metadata\":{";
+    for (size_t i = 0; i < src->metadata.size(); ++i)
+        index += (i ? "," : "") + json_string(src->metadata[i].first) + ":" + json_string(src->metadata[i].second);
+    index += "},\"entries\":[";
+    char buf[320];
+    for (size_t i = 0; i < src->entries.size(); ++i) {
+        const PackEntry& e = src->entries[i];
+        Placed& pl = placed[i];
+        index += (i ? ",{" : "{") + std::string("\"name\":") + json_string(e.name);
+        const bool device = e.kind == TELMO_PACK_DEVICE ||
+                            (e.kind == TELMO_PACK_MATRIX &&
+                             (e.precision == TELMO_PRECISION_INT8 || e.precision == TELMO_PRECISION_Q8_0));
+        if (device) {
+            if (e.kind == TELMO_PACK_MATRIX && !linear_perm.empty() && e.name == "sub.linear" && linear_perm.size() != e.k)
+                return fail_pack("Entry sub.linear doesn't fit config.json.");
+            const size_t plane = e.n * ((e.k + 15) / 16 * 16);
+            pl.kind = TELMO_PACK_DEVICE;
+            pl.bytes = plane;
+            pl.at = place(plane);
+            pl.s_bytes = e.n * 4;
+            pl.s_at = place(pl.s_bytes);
+            snprintf(buf, sizeof buf,
+                     ",\"type\":\"device\",\"precision\":\"%s\",\"n\":%zu,\"k\":%zu,\"offset\":%zu,\"bytes\":%zu,"
+                     "\"scales_offset\":%zu,\"scales_bytes\":%zu",
+                     precision_name(e.precision), e.n, e.k, pl.at, pl.bytes, pl.s_at, pl.s_bytes);
+            index += buf;
+            if (e.precision == TELMO_PRECISION_Q8_0) {
+                pl.l_bytes = plane;
+                pl.l_at = place(plane);
+                snprintf(buf, sizeof buf, ",\"lo_offset\":%zu,\"lo_bytes\":%zu", pl.l_at, pl.l_bytes);
+                index += buf;
+            }
+        } else if (e.kind == TELMO_PACK_MATRIX) {
+            pl.kind = TELMO_PACK_MATRIX;
+            pl.bytes = e.bytes;
+            pl.at = place(e.bytes);
+            snprintf(buf, sizeof buf, ",\"type\":\"matrix\",\"precision\":\"%s\",\"n\":%zu,\"k\":%zu,\"offset\":%zu,\"bytes\":%zu",
+                     precision_name(e.precision), e.n, e.k, pl.at, pl.bytes);
+            index += buf;
+            if (e.scales_bytes) {
+                pl.s_bytes = e.scales_bytes;
+                pl.s_at = place(pl.s_bytes);
+                snprintf(buf, sizeof buf, ",\"scales_offset\":%zu,\"scales_bytes\":%zu", pl.s_at, pl.s_bytes);
+                index += buf;
+            }
+        } else if (e.kind == TELMO_PACK_F32) {
+            pl.kind = TELMO_PACK_F32;
+            pl.bytes = e.bytes;
+            pl.at = place(e.bytes);
+            index += ",\"type\":\"f32\",\"shape\":[";
+            for (size_t d = 0; d < e.shape.size(); ++d) index += (d ? "," : "") + std::to_string(e.shape[d]);
+            snprintf(buf, sizeof buf, "],\"offset\":%zu,\"bytes\":%zu", pl.at, pl.bytes);
+            index += buf;
+        } else {
+            pl.bytes = e.bytes;
+            pl.at = place(e.bytes);
+            snprintf(buf, sizeof buf, ",\"type\":\"bytes\",\"offset\":%zu,\"bytes\":%zu", pl.at, pl.bytes);
+            index += buf;
+        }
+        index += "}";
+    }
+    index += "]}";
+    const uint64_t index_at = end, index_len = index.size();
+    std::vector<uint8_t> data(end + index.size() + kTrailer, 0);
+    memcpy(data.data(), "TELMOPAK", 8);
+    const uint32_t version = 1;
+    memcpy(data.data() + 8, &version, 4);
+    uint8_t* d = data.data();
+    for (size_t i = 0; i < src->entries.size(); ++i) {
+        const PackEntry& e = src->entries[i];
+        const Placed& pl = placed[i];
+        if (pl.kind == TELMO_PACK_DEVICE && e.kind == TELMO_PACK_MATRIX) {
+            const int* perm = !linear_perm.empty() && e.name == "sub.linear" ? linear_perm.data() : nullptr;
+            encode_device_rows(e.precision, e.n, e.k, entry_data(src, e.offset),
+                               reinterpret_cast<const float*>(entry_data(src, e.scales_offset)), perm,
+                               reinterpret_cast<int8_t*>(d + pl.at), reinterpret_cast<int8_t*>(d + pl.l_at),
+                               reinterpret_cast<float*>(d + pl.s_at));
+            continue;
+        }
+        memcpy(d + pl.at, entry_data(src, e.offset), pl.bytes);
+        if (pl.s_bytes) memcpy(d + pl.s_at, entry_data(src, e.scales_offset), pl.s_bytes);
+        if (pl.l_bytes) memcpy(d + pl.l_at, entry_data(src, e.lo_offset), pl.l_bytes);
+    }
+    memcpy(d + index_at, index.data(), index.size());
+    uint8_t* trailer = d + index_at + index_len;
+    memcpy(trailer, &index_at, 8);
+    memcpy(trailer + 8, &index_len, 8);
+    memcpy(trailer + 16, "TELMOIDX", 8);
+    return make_pack(std::move(data), out);
+}
+
+extern "C" int telmo_pack_save(const telmo_pack* pk, const char* path) {
+    if (!pk || !path) return TELMO_ERR_ARGUMENT;
+    FILE* f = fopen(path, "wb");
+    if (!f) return fail_pack(std::string("Cannot create ") + path + ".");
+    const bool ok = fwrite(pk->data.data(), 1, pk->data.size(), f) == pk->data.size();
+    if (fclose(f) != 0 || !ok) return fail_pack(std::string("Cannot write ") + path + ".");
+    return TELMO_OK;
+}
+
 extern "C" int telmo_granite_config_from_json(const char* json, size_t len, telmo_granite_config* out) {
     if (!json || !out) return TELMO_ERR_ARGUMENT;
     return granite_config_from_json(json, len, out);
@@ -631,13 +820,19 @@ extern "C" int telmo_parakeet_config_from_json(const char* json, size_t len, tel
 
 namespace telmo {
 
-int pack_load_entries(const telmo_pack* pk, const PackMatrixFn& set_matrix, const PackVectorFn& set_vector,
-                      const PackKnowsFn& knows) {
+int pack_load_entries(const telmo_pack* pk, const PackMatrixFn& set_matrix, const PackDeviceFn& set_device,
+                      const PackVectorFn& set_vector, const PackKnowsFn& knows) {
     for (const PackEntry& e : pk->entries) {
         if (e.kind == TELMO_PACK_BYTES || !knows(e.name)) continue;
         if (e.kind == TELMO_PACK_MATRIX) {
             const float* scales = e.scales_bytes ? reinterpret_cast<const float*>(entry_data(pk, e.scales_offset)) : nullptr;
             if (int rc = set_matrix(e.name.c_str(), e.precision, e.n, e.k, entry_data(pk, e.offset), scales)) return rc;
+        } else if (e.kind == TELMO_PACK_DEVICE) {
+            const int8_t* lo = e.lo_bytes ? reinterpret_cast<const int8_t*>(entry_data(pk, e.lo_offset)) : nullptr;
+            if (int rc = set_device(e.name.c_str(), e.precision, e.n, e.k,
+                                    reinterpret_cast<const int8_t*>(entry_data(pk, e.offset)), lo,
+                                    reinterpret_cast<const float*>(entry_data(pk, e.scales_offset))))
+                return rc;
         } else {
             if (int rc = set_vector(e.name.c_str(), e.bytes / 4, reinterpret_cast<const float*>(entry_data(pk, e.offset))))
                 return rc;
@@ -667,6 +862,9 @@ extern "C" int telmo_granite_load_pack(telmo_ctx* ctx, const telmo_pack* pk, tel
         pk,
         [&](const char* name, int precision, size_t n, size_t k, const void* v, const float* s) {
             return telmo_granite_set_matrix(g, name, precision, n, k, v, s);
+        },
+        [&](const char* name, int precision, size_t n, size_t k, const int8_t* v, const int8_t* lo, const float* s) {
+            return granite_set_device_matrix(g, name, precision, n, k, v, lo, s);
         },
         [&](const char* name, size_t len, const float* data) { return telmo_granite_set_vector(g, name, len, data); },
         [&](const std::string& name) {

@@ -875,9 +875,22 @@ extern "C" int telmo_parakeet_create(telmo_ctx* cp, const telmo_parakeet_config*
 
 extern "C" void telmo_parakeet_free(telmo_parakeet* p) { delete as_parakeet(p); }
 
-extern "C" int telmo_parakeet_set_matrix(telmo_parakeet* pp, const char* name, int precision, size_t n, size_t k,
-                                         const void* panel_values, const float* scales) {
-    Parakeet* p = as_parakeet(pp);
+namespace telmo {
+
+std::vector<int> parakeet_linear_perm(int sub_channels, int n_mels) {
+    // Column f * ch + c of the device matrix is the pack's column c * freqs + f.
+    const int ch = sub_channels, freqs = n_mels / 8;
+    std::vector<int> perm(static_cast<size_t>(ch) * freqs);
+    for (int f = 0; f < freqs; ++f)
+        for (int cc = 0; cc < ch; ++cc) perm[static_cast<size_t>(f) * ch + cc] = cc * freqs + f;
+    return perm;
+}
+
+}  // namespace telmo
+
+namespace {
+
+int parakeet_prepare_matrix(Parakeet* p, const char* name, size_t n, size_t k, Parakeet::Entry* out) {
     if (!p || !name) return TELMO_ERR_ARGUMENT;
     Parakeet::Entry e = p->find(name);
     if (!e.mat) return p->ctx->fail(TELMO_ERR_MODEL, "parakeet: no matrix named %s", name);
@@ -886,17 +899,39 @@ extern "C" int telmo_parakeet_set_matrix(telmo_parakeet* pp, const char* name, i
     if (int rc = p->ctx->use_device()) return rc;
     free_weights(e.mat);
     p->finalized = false;
+    *out = e;
+    return TELMO_OK;
+}
+
+}  // namespace
+
+extern "C" int telmo_parakeet_set_matrix(telmo_parakeet* pp, const char* name, int precision, size_t n, size_t k,
+                                         const void* panel_values, const float* scales) {
+    Parakeet* p = as_parakeet(pp);
+    Parakeet::Entry e;
+    if (int rc = parakeet_prepare_matrix(p, name, n, k, &e)) return rc;
     if (e.mat == &p->linear) {
-        // Column f * ch + c of the uploaded matrix is the pack's column c * freqs + f (a Q8_0
-        // row is re-encoded with one row scale, which no column order changes).
-        const int ch = p->c.sub_channels, freqs = p->c.n_mels / 8;
-        std::vector<int> perm(k);
-        for (int f = 0; f < freqs; ++f)
-            for (int cc = 0; cc < ch; ++cc) perm[static_cast<size_t>(f) * ch + cc] = cc * freqs + f;
+        // The subsampling output takes its inputs frequency-major on the device (a Q8_0 row is
+        // re-encoded with one row scale, which no column order changes).
+        const std::vector<int> perm = parakeet_linear_perm(p->c.sub_channels, p->c.n_mels);
         return upload_weights(p->ctx, precision, n, k, panel_values, scales, e.mat, perm.data());
     }
     return upload_weights(p->ctx, precision, n, k, panel_values, scales, e.mat);
 }
+
+namespace telmo {
+
+int parakeet_set_device_matrix(telmo_parakeet* pp, const char* name, int precision, size_t n, size_t k,
+                               const int8_t* rows, const int8_t* lo, const float* scales) {
+    // Device rows are stored with the columns already in the device's order.
+    Parakeet* p = as_parakeet(pp);
+    Parakeet::Entry e;
+    if (int rc = parakeet_prepare_matrix(p, name, n, k, &e)) return rc;
+    if (int rc = check_weight_shape(p->ctx, precision, n, k)) return rc;
+    return upload_device_rows(p->ctx, precision, n, k, rows, lo, scales, e.mat);
+}
+
+}  // namespace telmo
 
 extern "C" int telmo_parakeet_set_vector(telmo_parakeet* pp, const char* name, size_t len, const float* data) {
     Parakeet* p = as_parakeet(pp);
@@ -1021,6 +1056,9 @@ extern "C" int telmo_parakeet_load_pack(telmo_ctx* ctx, const telmo_pack* pk, te
         pk,
         [&](const char* name, int precision, size_t n, size_t k, const void* v, const float* s) {
             return telmo_parakeet_set_matrix(pp, name, precision, n, k, v, s);
+        },
+        [&](const char* name, int precision, size_t n, size_t k, const int8_t* v, const int8_t* lo, const float* s) {
+            return parakeet_set_device_matrix(pp, name, precision, n, k, v, lo, s);
         },
         [&](const char* name, size_t len, const float* data) { return telmo_parakeet_set_vector(pp, name, len, data); },
         [&](const std::string& name) {

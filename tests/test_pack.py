@@ -9,7 +9,7 @@ import pytest
 
 from telmo_b200 import synthetic
 
-from packs import granite_config_json, parakeet_config_json, write_pack
+from telmo_b200.pack import granite_config_json, parakeet_config_json, write_pack
 
 
 def _sample():
@@ -85,6 +85,138 @@ def test_damaged_packs_are_refused():
             Pack(data=with_index(change))
 
 
+# ---- device-layout packs (this build's extension; host only) ------------------------------------
+
+def _panel_rows(values, n, k):
+    """The panel layout's [n, k] int8 values (output o in panel o // 16, lane o % 16)."""
+    p = (n + 15) // 16
+    return np.asarray(values, np.int8).reshape(p, k, 16).transpose(0, 2, 1).reshape(p * 16, k)[:n]
+
+
+def _device_planes(values, scales, n, k, precision, perm=None):
+    """The device layout restated: rows of round_up(k, 16) values, one scale per row; Q8_0 rows
+    re-encoded as s (hi + lo / 254) with s = amax / 127, each level rounded half to even."""
+    ld = (k + 15) // 16 * 16
+    q = _panel_rows(values, n, k).astype(np.int32)
+    perm = np.arange(k) if perm is None else np.asarray(perm)
+    hi = np.zeros((n, ld), np.int8)
+    lo = np.zeros((n, ld), np.int8)
+    if precision == "int8":
+        hi[:, :k] = q[:, perm]
+        sc = np.asarray(scales, np.float32).reshape(-1)[:n]
+        return hi, None, sc
+    blocks = k // 32
+    d = np.asarray(scales, np.float32).reshape(-1, blocks, 16).transpose(0, 2, 1).reshape(-1, blocks)[:n]
+    w = (q.astype(np.float32) * np.repeat(d, 32, axis=1))[:, perm]
+    amax = np.abs(w).max(axis=1)
+    s = (amax / np.float32(127)).astype(np.float32)
+    inv = np.where(s != 0, np.float32(1) / np.where(s != 0, s, 1), 0).astype(np.float32)
+    h = np.clip(np.rint(w * inv[:, None]), -127, 127).astype(np.float32)
+    e = (w.astype(np.float64) - h.astype(np.float64) * s[:, None].astype(np.float64)).astype(np.float32)
+    l = np.clip(np.rint(e * (inv * np.float32(254))[:, None]), -127, 127)
+    hi[:, :k] = h.astype(np.int8)
+    lo[:, :k] = l.astype(np.int8)
+    return hi, lo, s
+
+
+def _read_index(data):
+    at, n = struct.unpack("<QQ", data[-24:-8])
+    return json.loads(data[at:at + n])
+
+
+def test_device_layout_pack(tmp_path):
+    # The converted pack holds each 8-bit matrix as the upload would build it on the host, keeps
+    # the other entries, reads back through the same checks, and converts again to itself.
+    from telmo_b200.pack import Pack
+    sample = _sample()
+    src = Pack(data=write_pack("test", sample, {"source": "x"}))
+    dev = src.to_device()
+    assert dev.model == "test" and dev.meta("source") == "x"
+    got = {e["name"]: e for e in dev.entries()}
+    assert got["w8"]["kind"] == "device" and got["w8"]["precision"] == "int8"
+    assert (got["w8"]["n"], got["w8"]["k"], got["w8"]["bytes"]) == (40, 64, 40 * 64)
+    assert got["wq"]["kind"] == "device" and got["wq"]["precision"] == "q8_0"
+    assert got["bias"]["kind"] == "f32" and dev.bytes("config.json") == b'{"a":1}'
+    dev.save(tmp_path / "dev.pack")
+    data = (tmp_path / "dev.pack").read_bytes()
+    index = {e["name"]: e for e in _read_index(data)["entries"]}
+    assert np.array_equal(np.frombuffer(data, np.float32, 6, index["bias"]["offset"]), sample["bias"].reshape(-1))
+    for name, prec in (("w8", "int8"), ("wq", "q8_0")):
+        values, scales, n, k = sample[name][:4]
+        hi, lo, sc = _device_planes(values, scales, n, k, prec)
+        e = index[name]
+        assert e["type"] == "device" and all(e[f] % 64 == 0 for f in e if f.endswith("offset"))
+        assert np.array_equal(np.frombuffer(data, np.int8, e["bytes"], e["offset"]).reshape(n, -1), hi)
+        assert np.array_equal(np.frombuffer(data, np.float32, n, e["scales_offset"]), sc)
+        if lo is not None:
+            assert np.array_equal(np.frombuffer(data, np.int8, e["lo_bytes"], e["lo_offset"]).reshape(n, -1), lo)
+        else:
+            assert "lo_offset" not in e
+    again = Pack(path=tmp_path / "dev.pack").to_device()
+    again.save(tmp_path / "again.pack")
+    assert (tmp_path / "again.pack").read_bytes() == data
+
+
+@pytest.mark.parametrize("precision", ["int8", "q8_0"])
+def test_device_layout_pack_orders_parakeet_columns(tmp_path, precision):
+    # Parakeet's subsampling output matrix is stored with its columns in the kernels' order
+    # (frequency-major); every other matrix keeps the pack's order.
+    from telmo_b200.pack import Pack
+    pc = synthetic.parakeet_config(layers=1, d_model=64, heads=2, ff=128, sub_channels=32, pred_hidden=32,
+                                   vocab=17, blank=16)
+    pe = synthetic.parakeet_entries(pc, seed=3, precision=precision)
+    Pack(data=write_pack("parakeet-tdt", dict(pe, **{"config.json": parakeet_config_json(pc)}))).to_device().save(
+        tmp_path / "p.pack")
+    data = (tmp_path / "p.pack").read_bytes()
+    index = {e["name"]: e for e in _read_index(data)["entries"]}
+    ch, freqs = pc["sub_channels"], pc["n_mels"] // 8
+    perm = [c * freqs + f for f in range(freqs) for c in range(ch)]
+    for name, order in (("sub.linear", perm), ("sub.pw1", None)):
+        values, scales, n, k = pe[name][:4]
+        hi, lo, sc = _device_planes(values, scales, n, k, precision, order)
+        e = index[name]
+        assert np.array_equal(np.frombuffer(data, np.int8, e["bytes"], e["offset"]).reshape(n, -1), hi)
+        assert np.array_equal(np.frombuffer(data, np.float32, n, e["scales_offset"]), sc)
+        if lo is not None:
+            assert np.array_equal(np.frombuffer(data, np.int8, e["lo_bytes"], e["lo_offset"]).reshape(n, -1), lo)
+    # A Parakeet pack without its config cannot be converted (the column order depends on it).
+    from telmo_b200 import TelmoError
+    with pytest.raises(TelmoError, match="config.json"):
+        Pack(data=write_pack("parakeet-tdt", pe)).to_device()
+
+
+def test_damaged_device_entries_are_refused(tmp_path):
+    from telmo_b200 import TelmoError
+    from telmo_b200.pack import Pack
+    Pack(data=write_pack("test", _sample())).to_device().save(tmp_path / "d.pack")
+    good = (tmp_path / "d.pack").read_bytes()
+    idx_at, idx_len = struct.unpack("<QQ", good[-24:-8])
+    index = json.loads(good[idx_at:idx_at + idx_len])
+
+    def with_index(change):
+        ix = json.loads(json.dumps(index))
+        change(ix)
+        blob = json.dumps(ix).encode()
+        return good[:idx_at] + blob + struct.pack("<QQ", idx_at, len(blob)) + b"TELMOIDX"
+
+    def entry(ix, name):
+        return next(e for e in ix["entries"] if e["name"] == name)
+
+    Pack(data=with_index(lambda ix: None))
+    cases = [
+        lambda ix: entry(ix, "w8").update(precision="f32"),
+        lambda ix: entry(ix, "w8").update(bytes=40 * 48),
+        lambda ix: entry(ix, "w8").update(scales_bytes=4),
+        lambda ix: entry(ix, "wq").pop("lo_offset"),
+        lambda ix: entry(ix, "wq").update(lo_bytes=64),
+        lambda ix: entry(ix, "wq").update(lo_offset=entry(ix, "wq")["offset"]),
+        lambda ix: entry(ix, "wq").update(k=48),
+    ]
+    for change in cases:
+        with pytest.raises(TelmoError):
+            Pack(data=with_index(change))
+
+
 def test_config_json_round_trips():
     from telmo_b200.pack import granite_config_from_json, parakeet_config_from_json
     g = synthetic.granite_config()
@@ -141,14 +273,19 @@ def test_models_load_from_packs(ctx, precision):
                                 dict(ge, **{"config.json": granite_config_json(gc), "extra": np.ones(3, np.float32)})))
     a, b = Granite.from_entries(ctx, gc, ge), Granite.from_pack(ctx, pack)
     feats = torch.from_numpy(synthetic.rng(4).standard_normal((61, 32)).astype(np.float32)).cuda()
-    assert np.array_equal(a.encode(feats, [61])[0].cpu().numpy(), b.encode(feats, [61])[0].cpu().numpy())
+    want = a.encode(feats, [61])[0].cpu().numpy()
+    assert np.array_equal(want, b.encode(feats, [61])[0].cpu().numpy())
+    # The device-layout pack (matrices copied, not repacked) loads into the same model.
+    assert np.array_equal(want, Granite.from_pack(ctx, pack.to_device()).encode(feats, [61])[0].cpu().numpy())
     pc = synthetic.parakeet_config(layers=2, d_model=128, heads=2, ff=256, sub_channels=32, pred_hidden=64,
                                    vocab=65, blank=64)
     pe = synthetic.parakeet_entries(pc, seed=5, scales="conditioned", precision=precision)
     pack = Pack(data=write_pack("parakeet-tdt", dict(pe, **{"config.json": parakeet_config_json(pc)})))
     a, b = Parakeet.from_entries(ctx, pc, pe), Parakeet.from_pack(ctx, pack)
     f = torch.from_numpy(synthetic.rng(6).standard_normal((203, 128)).astype(np.float32)).cuda()
-    assert np.array_equal(a.encode(f, [203])[0].cpu().numpy(), b.encode(f, [203])[0].cpu().numpy())
+    want = a.encode(f, [203])[0].cpu().numpy()
+    assert np.array_equal(want, b.encode(f, [203])[0].cpu().numpy())
+    assert np.array_equal(want, Parakeet.from_pack(ctx, pack.to_device()).encode(f, [203])[0].cpu().numpy())
     gone = {k: v for k, v in pe.items() if k != "layers.1.pos"}
     pack = Pack(data=write_pack("parakeet-tdt", dict(gone, **{"config.json": parakeet_config_json(pc)})))
     with pytest.raises(TelmoError, match="layers.1.pos"):
