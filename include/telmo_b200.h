@@ -393,6 +393,95 @@ int telmo_parakeet_profile(telmo_parakeet *p, int enable);
 int telmo_parakeet_profile_read(telmo_parakeet *p, double *ms, long *launches, double *gemm_ops,
                                 double *gemm_bytes);
 
+/* ---- decoding that favours special words (src/biasing.rs, src/biasing/) -------------------- */
+
+/* Boost (src/biasing.rs:40-150): Parakeet's bonus per token of a special word and its beam;
+ * Granite's spotting bonus per token, the margin a spotted word must beat the greedy words by,
+ * and the extra margin per letter a word has below five. Bonuses 0-10, margins 0-50, beam 1-16. */
+typedef struct {
+    float bonus;
+    int beam;
+    float spotting_bonus;
+    float spotting_margin;
+    float short_word_margin;
+} telmo_boost;
+/* The reference's defaults: 1.5, 4, 4.0, 2.0, 3.0. */
+void telmo_boost_default(telmo_boost *b);
+
+/* Special words ready for decoding (Compiled, src/biasing.rs:740-870), built on the host from
+ * their spellings already split into the model's tokens -- this library has no tokenizer. Form i
+ * is form_lengths[i] (1-32) tokens of form_tokens, in order, and form_letters[i] letters and
+ * digits in its spelling (a word of fewer than five needs a larger spotting margin). A caller
+ * passes each spelling Compiled::new favours (the word and its capitalized form, a spoken form's
+ * capitalizations); repeated token sequences count once. boundary[t] says whether a word may end
+ * just before vocabulary token t (Tokenizer::is_word_boundary: it starts a word or holds no letter
+ * or digit), wordlike[t] whether it holds a letter or digit. Failures are TELMO_ERR_ARGUMENT with
+ * the reason in telmo_words_last_error() (per thread). Host only. */
+typedef struct telmo_words telmo_words;
+int telmo_words_create(size_t vocab, const uint8_t *boundary, const uint8_t *wordlike,
+                       const uint32_t *form_tokens, const size_t *form_lengths,
+                       const size_t *form_letters, size_t n_forms, const telmo_boost *boost,
+                       telmo_words **out);
+void telmo_words_free(telmo_words *w);
+const char *telmo_words_last_error(void);
+/* Distinct forms, and the sorted distinct tokens of all forms (Compiled::tokens: columns 2.. of
+ * the score rows); returns their number, writing up to cap. */
+size_t telmo_words_forms(const telmo_words *w);
+size_t telmo_words_columns(const telmo_words *w, uint32_t *tokens, size_t cap);
+/* The matcher (src/biasing.rs:653-679) on a state of three words (node, covered, half; all zero
+ * at the start): the state after a token and the change in bonus, and the change when the audio
+ * ends. For tests and for callers that run their own search. */
+int telmo_words_step(const telmo_words *w, const uint64_t *state, uint32_t token, uint64_t *next,
+                     float *delta);
+int telmo_words_finish(const telmo_words *w, const uint64_t *state, float *delta);
+
+/* spot (src/biasing/spotting.rs:95-245): replaces greedy CTC tokens by special words where an
+ * alignment of the word plus its bonus beats the greedy path over the same frames by the margin.
+ * greedy: n_greedy (id, frame, duration) triples of frames first..; scores: score rows of every
+ * frame from 0, [frames, 2 + columns] (a frame's best logit, the blank's, then the columns'). Writes
+ * the tokens (triples, up to cap; *n_tokens is the number, TELMO_ERR_ARGUMENT when it exceeds cap)
+ * and for each spotted word the [begin, end) pair of output tokens it holds (ranges may be NULL).
+ * Host only. */
+int telmo_spot(const telmo_words *w, const uint32_t *greedy, size_t n_greedy, const float *scores,
+               size_t frames, size_t first, uint32_t *tokens, size_t cap, size_t *n_tokens,
+               size_t *ranges, size_t ranges_cap, size_t *n_ranges);
+/* Granite::decode_biased (src/granite.rs:584-604) up to the text rewrites: the CTC head and
+ * greedy ids on the device, the score rows gathered there (score_row, src/biasing/spotting.rs:
+ * 10-15) so only [frames, 2 + columns] floats come back, then ctc_tokens and spot on the host.
+ * encoded: device [frames, d_model]; tokens: host triples, up to cap. Spoken forms, symbols and
+ * fillers (text rewrites) are outside this library. Synchronizes the stream. */
+int telmo_granite_decode_biased(telmo_granite *g, const float *encoded, size_t frames,
+                                const telmo_words *w, uint32_t *tokens, size_t cap,
+                                size_t *n_tokens, void *stream);
+
+/* tdt_beam::beam_search (src/biasing/tdt_beam.rs:141-401) over a caller's networks
+ * (tdt_beam::TdtNetwork): joint(user, frame, preds [rows, pred_width], rows, out [rows, vocab +
+ * n_durations]) and predict(user, tokens [rows], rows, states [rows, state_width] updated,
+ * preds [rows, pred_width] written), each returning 0 or a status that ends the search. The search
+ * decodes frames start_frame..frames from the given decoder state and writes the best hypothesis's
+ * tokens as triples (up to cap). Host only. */
+typedef int (*telmo_tdt_joint_fn)(void *user, size_t frame, const float *preds, size_t rows, float *out);
+typedef int (*telmo_tdt_predict_fn)(void *user, const int *tokens, size_t rows, float *states,
+                                    float *preds);
+int telmo_tdt_beam_search(int vocab, int blank, const int *durations, int n_durations, int max_symbols,
+                          size_t state_width, size_t pred_width, telmo_tdt_joint_fn joint,
+                          telmo_tdt_predict_fn predict, void *user, size_t frames, size_t start_frame,
+                          size_t start_on_frame, const float *start_state, const float *start_pred,
+                          const telmo_words *w, uint32_t *tokens, size_t cap, size_t *n_tokens);
+/* Parakeet::beam_search (src/parakeet.rs:1360-1410) over this model's device networks: the
+ * joint's projection of encoded frames offset.. once (device), then per search step one batched
+ * joint over the hypotheses at the step's frame and one batched prediction over those that
+ * emitted. encoded: device [frames, d_model], the utterance's frames from `offset`; state and pred
+ * (host, pred_layers * 2 * pred_hidden and pred_hidden floats) with frame and on_frame give the
+ * decoder state to continue from, or NULL for the state before any token (initial_decoder_state,
+ * :1321-1335, frame 0). Token frames count from the utterance's start. With no special words the
+ * search returns no tokens, as the reference's does (decode greedily instead). Synchronizes the
+ * stream. */
+int telmo_parakeet_beam_search(telmo_parakeet *p, const float *encoded, size_t frames, size_t offset,
+                               const float *state, const float *pred, size_t frame, size_t on_frame,
+                               const telmo_words *w, uint32_t *tokens, size_t cap, size_t *n_tokens,
+                               void *stream);
+
 /* ---- packs (src/pack.rs) ------------------------------------------------------------------- */
 
 /* The reference's weight file: "TELMOPAK", format version 1, 64-byte aligned entry data, a JSON

@@ -39,6 +39,17 @@ _sz = _c.c_size_t
 _int = _c.c_int
 _float = _c.c_float
 
+# The caller's networks of telmo_tdt_beam_search (telmo_tdt_joint_fn, telmo_tdt_predict_fn).
+TDT_JOINT_FN = _c.CFUNCTYPE(_int, _vp, _sz, _c.POINTER(_float), _sz, _c.POINTER(_float))
+TDT_PREDICT_FN = _c.CFUNCTYPE(_int, _vp, _c.POINTER(_int), _sz, _c.POINTER(_float), _c.POINTER(_float))
+
+
+class Boost(ctypes.Structure):
+    """telmo_boost (include/telmo_b200.h)."""
+    _fields_ = [("bonus", ctypes.c_float), ("beam", ctypes.c_int), ("spotting_bonus", ctypes.c_float),
+                ("spotting_margin", ctypes.c_float), ("short_word_margin", ctypes.c_float)]
+
+
 # name -> (restype, argtypes); every function include/telmo_b200.h declares.
 SIGNATURES = {
     "telmo_ctx_create": (_int, [_int, _c.POINTER(_vp)]),
@@ -125,6 +136,19 @@ SIGNATURES = {
     "telmo_parakeet_decoder_profile": (_c.c_int, [_vp, _c.c_void_p, _c.c_void_p]),
     "telmo_parakeet_profile": (_int, [_vp, _int]),
     "telmo_parakeet_profile_read": (_int, [_vp, _vp, _vp, _vp, _vp]),
+    "telmo_boost_default": (None, [_vp]),
+    "telmo_words_create": (_int, [_sz, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "telmo_words_free": (None, [_vp]),
+    "telmo_words_last_error": (_c.c_char_p, []),
+    "telmo_words_forms": (_sz, [_vp]),
+    "telmo_words_columns": (_sz, [_vp, _vp, _sz]),
+    "telmo_words_step": (_int, [_vp, _vp, _c.c_uint32, _vp, _vp]),
+    "telmo_words_finish": (_int, [_vp, _vp, _vp]),
+    "telmo_spot": (_int, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _sz, _vp]),
+    "telmo_granite_decode_biased": (_int, [_vp, _vp, _sz, _vp, _vp, _sz, _vp, _vp]),
+    "telmo_tdt_beam_search": (_int, [_int, _int, _vp, _int, _int, _sz, _sz, TDT_JOINT_FN, TDT_PREDICT_FN, _vp,
+                                     _sz, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "telmo_parakeet_beam_search": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _sz, _vp, _vp]),
 }
 
 FRONTEND_GRANITE = 0

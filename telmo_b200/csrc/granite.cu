@@ -7,6 +7,7 @@
 // edges) and the stride-2 pooling see utterance boundaries, through task lists built here.
 #include "../../include/telmo_b200.h"
 #include "api_internal.h"
+#include "biasing.h"
 #include "frontend.h"
 #include "granite_internal.h"
 #include "kernels.h"
@@ -975,6 +976,47 @@ extern "C" int telmo_granite_frame_ids(telmo_granite* gp, const float* encoded, 
     if (!g || !encoded || !ids) return TELMO_ERR_ARGUMENT;
     if (int rc = g->ctx->use_device()) return rc;
     return g->frame_ids(encoded, static_cast<int>(frames), ids, margin, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int telmo_granite_decode_biased(telmo_granite* gp, const float* encoded, size_t frames, const telmo_words* w,
+                                           uint32_t* tokens, size_t cap, size_t* n_tokens, void* stream) {
+    // Granite::decode_biased (src/granite.rs:584-604) up to the text rewrites: frame_scores with
+    // the words' columns (:690-716) on the device, then ctc_tokens and spot on the host.
+    Granite* g = as_granite(gp);
+    if (!g || !w || !n_tokens || (cap && !tokens) || (frames && !encoded)) return TELMO_ERR_ARGUMENT;
+    *n_tokens = 0;
+    if (frames == 0) return TELMO_OK;
+    if (frames > (1u << 24)) return g->ctx->fail(TELMO_ERR_ARGUMENT, "decode_biased: too many frames");
+    if (int rc = g->ctx->use_device()) return rc;
+    if (!g->finalized) return g->ctx->fail(TELMO_ERR_MODEL, "granite: the model is not finalized");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const biasing::Words& words = words_of(w);
+    const size_t width = 2 + words.tokens.size();
+    uint32_t* ids_dev = nullptr;
+    float* scores_dev = nullptr;
+    std::vector<uint32_t> ids(frames);
+    std::vector<float> scores(words.forms.empty() ? 0 : frames * width);
+    int rc = g->ctx->cuda(cudaMalloc(&ids_dev, frames * sizeof(uint32_t)), "decode_biased");
+    if (!rc && !scores.empty()) rc = g->ctx->cuda(cudaMalloc(&scores_dev, scores.size() * sizeof(float)), "decode_biased");
+    // The logits stay in the model's scratch after the ids; the score rows are gathered from them.
+    if (!rc) rc = g->frame_ids(encoded, static_cast<int>(frames), ids_dev, nullptr, s);
+    if (!rc && scores_dev)
+        rc = words_score_rows(w, g->big, static_cast<int64_t>(frames), g->c.vocab, g->vocab_ld, g->c.blank, scores_dev, s);
+    if (!rc)
+        rc = g->ctx->cuda(cudaMemcpyAsync(ids.data(), ids_dev, frames * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+                          "decode_biased");
+    if (!rc && scores_dev)
+        rc = g->ctx->cuda(cudaMemcpyAsync(scores.data(), scores_dev, scores.size() * sizeof(float), cudaMemcpyDeviceToHost, s),
+                          "decode_biased");
+    if (!rc) rc = g->ctx->cuda(cudaStreamSynchronize(s), "decode_biased");
+    if (ids_dev) cudaFree(ids_dev);
+    if (scores_dev) cudaFree(scores_dev);
+    if (rc) return rc;
+    const std::vector<biasing::Token> greedy = biasing::ctc_tokens(ids.data(), frames, static_cast<uint32_t>(g->c.blank));
+    std::vector<biasing::Token> out;
+    std::vector<std::pair<size_t, size_t>> ranges;
+    biasing::spot(words, greedy, scores.data(), frames, 0, &out, &ranges);
+    return words_tokens_out(out, tokens, cap, n_tokens);
 }
 
 extern "C" size_t telmo_granite_frames_for_samples(const telmo_granite* g, int64_t samples) {

@@ -21,6 +21,7 @@
 // nothing of it).
 #include "../../include/telmo_b200.h"
 #include "api_internal.h"
+#include "biasing.h"
 #include "frontend.h"
 #include "granite_internal.h"
 #include "kernels.h"
@@ -1096,6 +1097,120 @@ extern "C" int telmo_parakeet_predict(telmo_parakeet* pp, const int* tokens, int
     if (!p) return TELMO_ERR_ARGUMENT;
     if (int rc = p->ctx->use_device()) return rc;
     return p->predict_rows(tokens, rows, states, preds, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+// Parakeet's joint and prediction networks as the biased beam search reads them (Networks,
+// src/parakeet.rs:1634-1676), on the device: the encoder frames from `first` on are projected for
+// the joint once; each call stages the hypotheses' rows to the device, runs the batched product
+// and brings the outputs back (the search itself is host logic).
+class DeviceTdtNetwork : public biasing::TdtNetwork {
+public:
+    DeviceTdtNetwork(Parakeet* p, const float* enc_proj, size_t first, float* stage, cudaStream_t s)
+        : p_(p), enc_proj_(enc_proj), first_(first), stage_(stage), s_(s) {}
+    size_t state_width() const override { return static_cast<size_t>(p_->c.pred_layers) * 2 * p_->c.pred_hidden; }
+    size_t pred_width() const override { return static_cast<size_t>(p_->c.pred_hidden); }
+    // Rows at most biasing::kMaxBeam, so the staging buffers hold any group.
+    int joint(size_t frame, const float* preds, size_t rows, float* out) override {
+        const size_t h = pred_width(), outputs = static_cast<size_t>(p_->c.vocab + p_->c.n_durations);
+        float* preds_dev = stage_;
+        float* out_dev = stage_ + biasing::kMaxBeam * h;
+        Ctx* ctx = p_->ctx;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(preds_dev, preds, rows * h * 4, cudaMemcpyHostToDevice, s_), "beam joint"))
+            return rc;
+        if (int rc = p_->joint_rows(enc_proj_ + (frame - first_) * h, preds_dev, static_cast<int>(rows), out_dev,
+                                    static_cast<int64_t>(outputs), s_))
+            return rc;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(out, out_dev, rows * outputs * 4, cudaMemcpyDeviceToHost, s_), "beam joint"))
+            return rc;
+        return ctx->cuda(cudaStreamSynchronize(s_), "beam joint");
+    }
+    int predict(const int* tokens, size_t rows, float* states, float* preds) override {
+        const size_t h = pred_width(), sw = state_width();
+        const size_t outputs = static_cast<size_t>(p_->c.vocab + p_->c.n_durations);
+        float* states_dev = stage_ + biasing::kMaxBeam * (h + outputs);
+        float* preds_dev = states_dev + biasing::kMaxBeam * sw;
+        Ctx* ctx = p_->ctx;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(states_dev, states, rows * sw * 4, cudaMemcpyHostToDevice, s_), "beam predict"))
+            return rc;
+        if (int rc = p_->predict_rows(tokens, static_cast<int>(rows), states_dev, preds_dev, s_)) return rc;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(states, states_dev, rows * sw * 4, cudaMemcpyDeviceToHost, s_), "beam predict"))
+            return rc;
+        if (int rc = ctx->cuda(cudaMemcpyAsync(preds, preds_dev, rows * h * 4, cudaMemcpyDeviceToHost, s_), "beam predict"))
+            return rc;
+        return ctx->cuda(cudaStreamSynchronize(s_), "beam predict");
+    }
+    // Floats of staging: preds and joint outputs, states and predictions, for kMaxBeam rows.
+    static size_t stage_floats(const Parakeet* p) {
+        const size_t h = static_cast<size_t>(p->c.pred_hidden);
+        const size_t outputs = static_cast<size_t>(p->c.vocab + p->c.n_durations);
+        const size_t sw = static_cast<size_t>(p->c.pred_layers) * 2 * h;
+        return biasing::kMaxBeam * (h + outputs + sw + h);
+    }
+
+private:
+    Parakeet* p_;
+    const float* enc_proj_;
+    size_t first_;
+    float* stage_;
+    cudaStream_t s_;
+};
+
+}  // namespace
+
+extern "C" int telmo_parakeet_beam_search(telmo_parakeet* pp, const float* encoded, size_t frames, size_t offset,
+                                          const float* state, const float* pred, size_t frame, size_t on_frame,
+                                          const telmo_words* w, uint32_t* tokens, size_t cap, size_t* n_tokens,
+                                          void* stream) {
+    // Parakeet::beam_search (src/parakeet.rs:1360-1410), from initial_decoder_state (:1321-1335)
+    // when no state is given.
+    Parakeet* p = as_parakeet(pp);
+    if (!p || !w || !n_tokens || (cap && !tokens) || (frames && !encoded) || (!state) != (!pred))
+        return TELMO_ERR_ARGUMENT;
+    *n_tokens = 0;
+    if (int rc = p->ctx->use_device()) return rc;
+    if (!p->finalized) return p->ctx->fail(TELMO_ERR_MODEL, "parakeet: the model is not finalized");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto& c = p->c;
+    const size_t h = static_cast<size_t>(c.pred_hidden), sw = static_cast<size_t>(c.pred_layers) * 2 * h;
+    biasing::TdtShape shape;
+    if (int rc = words_tdt_shape(c.vocab, c.blank, c.durations, c.n_durations, c.max_symbols, &shape)) return rc;
+    biasing::TdtStart start;
+    if (state) {
+        start.state.assign(state, state + sw);
+        start.pred.assign(pred, pred + h);
+        start.frame = frame;
+        start.on_frame = on_frame;
+    }
+    const size_t first = start.frame > offset ? start.frame - offset : 0;
+    const biasing::Words& words = words_of(w);
+    if (first >= frames || words.forms.empty()) return TELMO_OK;
+    const size_t rows = frames - first;
+    float* enc_proj = nullptr;
+    float* stage = nullptr;
+    int rc = p->ctx->cuda(cudaMalloc(&enc_proj, rows * h * sizeof(float)), "beam search");
+    if (!rc) rc = p->ctx->cuda(cudaMalloc(&stage, DeviceTdtNetwork::stage_floats(p) * sizeof(float)), "beam search");
+    if (!rc) rc = p->enc_proj_rows(encoded + first * static_cast<size_t>(c.d_model), static_cast<int64_t>(rows), enc_proj, s);
+    DeviceTdtNetwork net(p, enc_proj, first, stage, s);
+    if (!rc && !state) {
+        // The decoder's state before any token: the blank's prediction from zero LSTM states.
+        start.state.assign(sw, 0.0f);
+        start.pred.assign(h, 0.0f);
+        const int blank = c.blank;
+        rc = net.predict(&blank, 1, start.state.data(), start.pred.data());
+    }
+    std::vector<biasing::Token> out;
+    if (!rc) {
+        // Frames are counted from `first` inside the search, as the projected rows are.
+        start.frame = first;
+        rc = biasing::beam_search(net, shape, frames, std::move(start), words, &out);
+    }
+    if (enc_proj) cudaFree(enc_proj);
+    if (stage) cudaFree(stage);
+    if (rc) return rc;
+    for (auto& t : out) t.frame += static_cast<uint32_t>(offset);
+    return words_tokens_out(out, tokens, cap, n_tokens);
 }
 
 extern "C" int telmo_parakeet_set_decoder(telmo_parakeet* pp, int persistent) {

@@ -159,6 +159,19 @@ class Granite:
         """ctc_tokens (src/granite.rs:1074-1094) for every utterance of a batch, on the GPU."""
         return ctc_tokens(self.ctx, ids, frames, self.config["blank"], stream)
 
+    def decode_biased(self, encoded, words, stream=None) -> np.ndarray:
+        """Granite::decode_biased (src/granite.rs:584-604) up to the text rewrites: greedy CTC
+        tokens of one utterance's CUDA encoder output [frames, d_model] with special words
+        spotted in (telmo_b200.biasing.Words). Returns (id, frame, duration) tokens [n, 3]."""
+        frames = int(encoded.shape[0])
+        cap = frames + 16
+        out = np.zeros((cap, 3), np.uint32)
+        n = ctypes.c_size_t()
+        check(_lib.load().telmo_granite_decode_biased(self._h, encoded.data_ptr(), frames, words.handle,
+                                                      out.ctypes.data, cap, ctypes.byref(n), _stream(stream)),
+              self.ctx.handle)
+        return out[:n.value].copy()
+
     def frames_for_samples(self, samples: int) -> int:
         return _lib.load().telmo_granite_frames_for_samples(self._h, int(samples))
 

@@ -210,6 +210,29 @@ class Parakeet:
         check(_lib.load().telmo_parakeet_predict(self._h, t.ctypes.data, t.size, states.data_ptr(),
                                                  preds.data_ptr(), _stream(stream)), self.ctx.handle)
 
+    def beam_search(self, encoded, words, offset: int = 0, state=None, stream=None) -> np.ndarray:
+        """Parakeet::beam_search (src/parakeet.rs:1360-1410) on the GPU networks: the TDT beam
+        search that favours special words (telmo_b200.biasing.Words) over one utterance's CUDA
+        encoder frames [frames, d_model] (its frames from `offset`). state: None for the decoder
+        state before any token, else (lstm, pred, frame, on_frame) with host arrays. Returns (id,
+        frame, duration) tokens [n, 3], frames counted from the utterance's start."""
+        frames = int(encoded.shape[0])
+        cap = frames * int(self.config["max_symbols"]) + 16
+        out = np.zeros((cap, 3), np.uint32)
+        n = ctypes.c_size_t()
+        if state is None:
+            lstm = pred = None
+            frame = on_frame = 0
+        else:
+            lstm = np.ascontiguousarray(state[0], np.float32)
+            pred = np.ascontiguousarray(state[1], np.float32)
+            frame, on_frame = int(state[2]), int(state[3])
+        check(_lib.load().telmo_parakeet_beam_search(
+            self._h, encoded.data_ptr(), frames, offset, None if lstm is None else lstm.ctypes.data,
+            None if pred is None else pred.ctypes.data, frame, on_frame, words.handle, out.ctypes.data, cap,
+            ctypes.byref(n), _stream(stream)), self.ctx.handle)
+        return out[:n.value].copy()
+
     def set_decoder(self, persistent: bool):
         """1/True: the persistent decoder kernel (the default); 0/False: per-phase launches."""
         check(_lib.load().telmo_parakeet_set_decoder(self._h, int(persistent)), self.ctx.handle)
