@@ -18,8 +18,10 @@
 // Structure: a persistent, warp-specialised kernel, one CTA per SM.
 //   warp 0      TMA producer: 128 x 128-byte boxes of W, A_hi and A_lo per stage (128B swizzle)
 //   warp 1      MMA issuer: 4 x tcgen05.mma kind::i8 per 128-byte K step
-//   warps 2-9   epilogue: tcgen05.ld, fused scale/bias/act/residual, TMA stores (two warps per
-//               TMEM lane quarter, each on half of the tile's activation rows)
+//   warps 2-17  epilogue: tcgen05.ld of 16 columns at a time, fused scale/bias/act/residual, TMA
+//               stores (four warps per TMEM lane quarter, each on a quarter of the tile's
+//               activation rows: at k = 1024 the epilogue of a tile takes about as long as its
+//               main loop, and with two warps per scheduler it was bound by their latencies)
 // TMEM holds two tiles (2 x 256 columns), so the epilogue of one tile overlaps the main loop of
 // the next. Every mbarrier wait is bounded; on timeout the kernel records kErrWaitTimeout in the
 // error word and returns.
@@ -42,11 +44,12 @@ constexpr int BN = 128;  // output features per tile (MMA M)
 constexpr int BM = 128;  // activation rows per tile (MMA N = 2 * BM)
 constexpr int BK = 128;  // bytes = int8 elements per stage along K (one 128-byte swizzle row)
 constexpr int UMMA_K = 32;
-constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each on half the columns
+constexpr int kEpiWarps = 16;                // four per TMEM lane quarter, each on a quarter of the columns
+constexpr int kRows = 16;                    // activation rows (TMEM columns) per epilogue chunk
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileBytes = 128 * BK;  // one 128-row operand box
 constexpr int kTmemCols = 2 * 2 * BM;  // 2 buffers x (hi, lo) x BM columns
-constexpr int kStageOutBytes = 32 * 32 * 4;   // one 32 x 32 f32 output chunk
+constexpr int kStageOutBytes = kRows * 32 * 4;  // one 16-row x 32-feature f32 output chunk
 constexpr int kOutStaging = kEpiWarps * kStageOutBytes;  // one buffer per epilogue warp
 
 // Pipeline shape per variant: CG = 1, one CTA per 128-feature tile, stages of W + A_hi + A_lo
@@ -125,30 +128,30 @@ __device__ __forceinline__ float epilogue_value(uint32_t acc_hi, uint32_t acc_lo
     return __fmul_rn(v, scale);
 }
 
-// One 32-row chunk of one thread's output column: 32 values computed branch-free, then stored
-// (rows_valid of them, each warp store covering 32 consecutive features of one row).
+// One chunk of one thread's output column (kRows rows): the values computed branch-free, then
+// stored (rows_valid of them, each warp store covering 32 consecutive features of one row).
 template <int ACT, bool ACC, typename OutT>
-__device__ __forceinline__ void store_chunk(const uint32_t (&hi)[32], const uint32_t (&lo)[32], float my_rs,
+__device__ __forceinline__ void store_chunk(const uint32_t (&hi)[kRows], const uint32_t (&lo)[kRows], float my_rs,
                                             float ws, float bs, float scale, OutT* o, int64_t ldc,
                                             int rows_valid, bool n_ok) {
-    float v[32];
+    float v[kRows];
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < kRows; ++j)
         v[j] = epilogue_value<ACT>(hi[j], lo[j], __shfl_sync(0xffffffffu, my_rs, j), ws, bs, scale);
     if (!n_ok) return;
-    if (rows_valid == 32) {
+    if (rows_valid == kRows) {
         if (ACC) {
-            float old[32];
+            float old[kRows];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) old[j] = static_cast<float>(o[j * ldc]);
+            for (int j = 0; j < kRows; ++j) old[j] = static_cast<float>(o[j * ldc]);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(old[j], v[j]);
+            for (int j = 0; j < kRows; ++j) v[j] = __fadd_rn(old[j], v[j]);
         }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j * ldc] = static_cast<OutT>(v[j]);
+        for (int j = 0; j < kRows; ++j) o[j * ldc] = static_cast<OutT>(v[j]);
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
+        for (int j = 0; j < kRows; ++j)
             if (j < rows_valid) {
                 float x = v[j];
                 if (ACC) x = __fadd_rn(static_cast<float>(o[j * ldc]), x);
@@ -158,15 +161,15 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&hi)[32], const uint
 }
 
 // The epilogue of a staged chunk, step for step as epilogue_value (except under SiLU, below):
-// v = ((float)hi + (float)lo * (1/254)) * rs * ws [+ bias] [act] [* scale], the chunk's 32 row
-// scales in registers. A bias of 0 and a scale of 1 change no value and are skipped.
+// v = ((float)hi + (float)lo * (1/254)) * rs * ws [+ bias] [act] [* scale], the chunk's kRows
+// row scales in registers. A bias of 0 and a scale of 1 change no value and are skipped.
 template <int ACT, bool BIAS, bool SCALE>
-__device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[32], const uint32_t (&lo)[32],
-                                               const float (&rs)[32], float ws, float bs, float scale,
-                                               float (&v)[32]) {
+__device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[kRows], const uint32_t (&lo)[kRows],
+                                               const float (&rs)[kRows], float ws, float bs, float scale,
+                                               float (&v)[kRows]) {
     const float inv254 = 1.0f / 254.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < kRows; ++j) {
         const float fh = __int2float_rn(static_cast<int32_t>(hi[j]));
         float x;
         if (ACT == kActSilu) {
@@ -184,9 +187,9 @@ __device__ __forceinline__ void compute_chunk2(const uint32_t (&hi)[32], const u
 }
 
 template <int ACT>
-__device__ __forceinline__ void compute_chunk_act(bool bias, bool scale_on, const uint32_t (&hi)[32],
-                                                  const uint32_t (&lo)[32], const float (&rs)[32], float ws,
-                                                  float bs, float scale, float (&v)[32]) {
+__device__ __forceinline__ void compute_chunk_act(bool bias, bool scale_on, const uint32_t (&hi)[kRows],
+                                                  const uint32_t (&lo)[kRows], const float (&rs)[kRows], float ws,
+                                                  float bs, float scale, float (&v)[kRows]) {
     if (bias) {
         if (scale_on) compute_chunk2<ACT, true, true>(hi, lo, rs, ws, bs, scale, v);
         else compute_chunk2<ACT, true, false>(hi, lo, rs, ws, bs, scale, v);
@@ -196,17 +199,17 @@ __device__ __forceinline__ void compute_chunk_act(bool bias, bool scale_on, cons
     }
 }
 
-__device__ __forceinline__ void compute_chunk_any(int act, bool bias, bool scale_on, const uint32_t (&hi)[32],
-                                                  const uint32_t (&lo)[32], const float (&rs)[32], float ws,
-                                                  float bs, float scale, float (&v)[32]) {
+__device__ __forceinline__ void compute_chunk_any(int act, bool bias, bool scale_on, const uint32_t (&hi)[kRows],
+                                                  const uint32_t (&lo)[kRows], const float (&rs)[kRows], float ws,
+                                                  float bs, float scale, float (&v)[kRows]) {
     if (act == kActNone) compute_chunk_act<kActNone>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
     else if (act == kActRelu) compute_chunk_act<kActRelu>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
     else compute_chunk_act<kActSilu>(bias, scale_on, hi, lo, rs, ws, bs, scale, v);
 }
 
 template <typename OutT>
-__device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_t (&hi)[32],
-                                                const uint32_t (&lo)[32], float my_rs, float ws, float bs,
+__device__ __forceinline__ void store_chunk_any(int act, bool acc, const uint32_t (&hi)[kRows],
+                                                const uint32_t (&lo)[kRows], float my_rs, float ws, float bs,
                                                 float scale, OutT* o, int64_t ldc, int rows_valid, bool n_ok) {
     if (act == kActNone) {
         if (acc) store_chunk<kActNone, true>(hi, lo, my_rs, ws, bs, scale, o, ldc, rows_valid, n_ok);
@@ -382,8 +385,10 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
             __syncwarp();
         }
     } else {
-        // ---- epilogue (warps 2..9): thread = one output feature, 32 rows per TMEM load; the two
-        // warps of a TMEM lane quarter take the tile's first and second 64 activation rows ----
+        // ---- epilogue (warps 2..17): thread = one output feature, kRows rows per TMEM load; the
+        // four warps of a TMEM lane quarter take a quarter of the tile's activation rows each, so
+        // four warps per scheduler hide one another's TMEM, load and store latencies ----
+        constexpr int kChunks = BM / (4 * kRows);  // chunks per warp per tile
         const int quad = warp & 3;  // TMEM lanes this warp may access: 32 * quad ..
         const int part = (warp - 2) / 4;
         const bool has_bias = p.bias != nullptr;
@@ -400,6 +405,13 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
             const bool n_ok = n < p.n;
             const float ws = n_ok ? __ldg(p.w_scale + n) : 0.0f;
             const float bs = (has_bias && n_ok) ? __ldg(p.bias + n) : 0.0f;
+            // The row scales of this warp's rows into L1 while the tile's products finish (the
+            // first and last row of each chunk, in case the scales are not 128-byte aligned), so
+            // the loads below hit L1 instead of waiting on L2 after the TMEM load.
+            if (lane < 2 * kChunks) {
+                const int mc = m0 + (part * kChunks + lane / 2) * kRows + (lane & 1) * (kRows - 1);
+                if (mc < p.m) prefetch_l1(p.row_scale + mc);
+            }
             if (!mbar_wait(&tmem_full[buf], use & 1)) {
                 record_error(p.error, kErrWaitTimeout);
                 *abort_flag = 1;
@@ -409,22 +421,22 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(buf * 2 * BM);
 #pragma unroll 1
-            for (int c = part * (BM / 64); c < (part + 1) * (BM / 64); ++c) {
-                uint32_t hi[32], lo[32];
-                tmem_ld32(taddr + c * 32, hi);
-                tmem_ld32(taddr + BM + c * 32, lo);
+            for (int c = part * kChunks; c < (part + 1) * kChunks; ++c) {
+                uint32_t hi[kRows], lo[kRows];
+                tmem_ld16(taddr + c * kRows, hi);
+                tmem_ld16(taddr + BM + c * kRows, lo);
                 tmem_ld_wait();
-                const int mc = m0 + c * 32;
+                const int mc = m0 + c * kRows;
                 if (mc >= p.m) continue;
-                const float my_rs = (mc + lane < p.m) ? __ldg(p.row_scale + mc + lane) : 0.0f;
-                const int rows_valid = p.m - mc < 32 ? p.m - mc : 32;
-                // The chunk's 32 row scales in registers: broadcast 16-byte loads for a full,
-                // aligned chunk, else shuffles of the lanes' own loads.
-                float rs[32];
-                if (rows_valid == 32 && rs_vec) {
+                const float my_rs = (lane < kRows && mc + lane < p.m) ? __ldg(p.row_scale + mc + lane) : 0.0f;
+                const int rows_valid = p.m - mc < kRows ? p.m - mc : kRows;
+                // The chunk's row scales in registers: broadcast 16-byte loads for a full, aligned
+                // chunk, else shuffles of the lanes' own loads.
+                float rs[kRows];
+                if (rows_valid == kRows && rs_vec) {
                     const float4* r4 = reinterpret_cast<const float4*>(p.row_scale + mc);
 #pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
+                    for (int q4 = 0; q4 < kRows / 4; ++q4) {
                         const float4 t4 = __ldg(r4 + q4);
                         rs[4 * q4] = t4.x;
                         rs[4 * q4 + 1] = t4.y;
@@ -433,26 +445,26 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) rs[j] = __shfl_sync(0xffffffffu, my_rs, j);
+                    for (int j = 0; j < kRows; ++j) rs[j] = __shfl_sync(0xffffffffu, my_rs, j);
                 }
                 const int64_t off = static_cast<int64_t>(mc) * p.ldc + n;
                 if (p.out_path != kDirect) {
-                    // Stage the 32 x 32 chunk (row = activation row, column = feature) and let one
-                    // lane hand it to TMA; the previous chunk's store has read the buffer by the
-                    // time this chunk's values are computed, almost always.
-                    float v[32];
+                    // Stage the kRows x 32 chunk (row = activation row, column = feature) and let
+                    // one lane hand it to TMA; the previous chunk's store has read the buffer by
+                    // the time this chunk's values are computed, almost always.
+                    float v[kRows];
                     compute_chunk_any(p.act, has_bias, scale_on, hi, lo, rs, ws, bs, p.scale, v);
                     if (lane == 0) bulk_wait_read<0>();
                     __syncwarp();
                     if (p.out_kind == kOutF32) {
                         float* sf = reinterpret_cast<float*>(sbuf);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) sf[j * 32 + lane] = v[j];
+                        for (int j = 0; j < kRows; ++j) sf[j * 32 + lane] = v[j];
                     } else if (p.out_kind == kOutF16Split) {
                         __half* sh = reinterpret_cast<__half*>(sbuf);
-                        __half* sl = sh + 32 * 32;
+                        __half* sl = sh + kRows * 32;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
+                        for (int j = 0; j < kRows; ++j) {
                             const __half h = __float2half_rn(v[j]);
                             sh[j * 32 + lane] = h;
                             sl[j * 32 + lane] = __float2half_rn(__fsub_rn(v[j], __half2float(h)));
@@ -460,7 +472,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     } else {
                         __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(sbuf);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) sb[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+                        for (int j = 0; j < kRows; ++j) sb[j * 32 + lane] = __float2bfloat16_rn(v[j]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -468,16 +480,16 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     if (lane == 0 && x0 < p.n) {
                         if (p.out_path == kTmaReduce) tma_reduce_add_2d(&map_out, sbuf, x0, mc);
                         else tma_store_2d(&map_out, sbuf, x0, mc);
-                        if (p.out_kind == kOutF16Split) tma_store_2d(&map_out_lo, sbuf + 32 * 32 * 2, x0, mc);
+                        if (p.out_kind == kOutF16Split) tma_store_2d(&map_out_lo, sbuf + kRows * 32 * 2, x0, mc);
                         bulk_commit();
                     }
                 } else if (p.out_kind == kOutF16Split) {
-                    float v[32];
+                    float v[kRows];
                     compute_chunk_any(p.act, has_bias, scale_on, hi, lo, rs, ws, bs, p.scale, v);
                     __half* oh = static_cast<__half*>(p.out) + off;
                     __half* ol = oh + static_cast<int64_t>(p.m) * p.ldc;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < kRows; ++j)
                         if (j < rows_valid && n_ok) {
                             const __half h = __float2half_rn(v[j]);
                             oh[j * p.ldc] = h;
@@ -493,7 +505,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
                     int32_t* o_hi = static_cast<int32_t*>(p.out) + static_cast<int64_t>(mc) * p.ldc + n;
                     int32_t* o_lo = o_hi + static_cast<int64_t>(p.m) * p.ldc;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < kRows; ++j) {
                         if (mc + j < p.m && n_ok) {
                             o_hi[j * p.ldc] = static_cast<int32_t>(hi[j]);
                             o_lo[j * p.ldc] = static_cast<int32_t>(lo[j]);
@@ -568,7 +580,8 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
     return r == CUDA_SUCCESS;
 }
 
-// The output tensor map: m rows of n elements, ldc apart, 32 x 32 boxes without swizzle. Each
+// The output tensor map: m rows of n elements, ldc apart, boxes of 32 elements x kRows rows
+// without swizzle. Each
 // plane of the split output gets its own map, so TMA drops the rows of a partial chunk past m
 // instead of writing them into the other plane.
 bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t ldc) {
@@ -577,7 +590,7 @@ bool make_out_map(CUtensorMap* map, void* base, int kind, int m, int n, int64_t 
     const bool two = kind == kOutBF16 || kind == kOutF16Split;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * (two ? 2 : 4)};
-    cuuint32_t box[2] = {32, 32};
+    cuuint32_t box[2] = {32, static_cast<cuuint32_t>(kRows)};
     cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType type = kind == kOutBF16        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : kind == kOutF16Split ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
