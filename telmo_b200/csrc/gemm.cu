@@ -20,8 +20,8 @@
 //   warp 1      MMA issuer: 4 x tcgen05.mma kind::i8 per 128-byte K step
 //   warps 2-17  epilogue: tcgen05.ld of 16 columns at a time, fused scale/bias/act/residual, TMA
 //               stores (four warps per TMEM lane quarter, each on a quarter of the tile's
-//               activation rows: at k = 1024 the epilogue of a tile takes about as long as its
-//               main loop, and with two warps per scheduler it was bound by their latencies)
+//               activation rows, so four warps per scheduler overlap one another's TMEM loads,
+//               scale loads and stores)
 // TMEM holds two tiles (2 x 256 columns), so the epilogue of one tile overlaps the main loop of
 // the next. Every mbarrier wait is bounded; on timeout the kernel records kErrWaitTimeout in the
 // error word and returns.
@@ -386,8 +386,7 @@ gemm_i8x2_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constan
         }
     } else {
         // ---- epilogue (warps 2..17): thread = one output feature, kRows rows per TMEM load; the
-        // four warps of a TMEM lane quarter take a quarter of the tile's activation rows each, so
-        // four warps per scheduler hide one another's TMEM, load and store latencies ----
+        // four warps of a TMEM lane quarter take a quarter of the tile's activation rows each ----
         constexpr int kChunks = BM / (4 * kRows);  // chunks per warp per tile
         const int quad = warp & 3;  // TMEM lanes this warp may access: 32 * quad ..
         const int part = (warp - 2) / 4;
