@@ -23,11 +23,11 @@ __device__ __forceinline__ float madd(float acc, float w, float v) { return __fa
 }  // namespace
 
 // Fused conv0 + ReLU + depthwise conv1 (Parakeet::subsample's first two convolutions,
-// src/parakeet.rs:937-941). One CTA per (span of kSubRows output time steps t2, block of kSubCh
-// channels): it stages the feature rows the span reads, computes conv0 + ReLU for the t1 rows the
-// span needs into shared memory (2 x kSubRows + 1 rows, so about 1/8 of conv0 is computed twice
-// across neighbouring spans), then the depthwise conv from there. Thread = (channel, group of
-// positions); each thread keeps its channel's 9 taps in registers.
+// src/parakeet.rs:937-941). One CTA per span of kSubRows output time steps t2: it stages the
+// feature rows the span reads once, then for each block of kSubCh channels computes conv0 + ReLU
+// for the t1 rows the span needs into shared memory (2 x kSubRows + 1 rows, so about 1/8 of conv0
+// is computed twice across neighbouring spans) and the depthwise conv from there. Thread =
+// (channel, group of positions); each thread keeps its channel's 9 taps in registers.
 __global__ void __launch_bounds__(256) sub_front_kernel(const float* __restrict__ feats, int f0,
                                                         const SubTask* __restrict__ tasks, int ch,
                                                         const float* __restrict__ w0, const float* __restrict__ b0,
@@ -35,7 +35,6 @@ __global__ void __launch_bounds__(256) sub_front_kernel(const float* __restrict_
                                                         float* __restrict__ out) {
     extern __shared__ float smf[];
     const SubTask t = tasks[blockIdx.x];
-    const int c0 = blockIdx.y * kSubCh;
     const int c = threadIdx.x % kSubCh, grp = threadIdx.x / kSubCh;
     constexpr int kGroups = 256 / kSubCh;
     const int f1n = (f0 - 1) / 2 + 1, f2n = (f1n - 1) / 2 + 1;
@@ -50,69 +49,72 @@ __global__ void __launch_bounds__(256) sub_front_kernel(const float* __restrict_
     float* h1 = smf + (4 * kSubRows + 3) * f0;           // [t1_rows][f1n][kSubCh]
     for (int i = threadIdx.x; i < t0_rows * f0; i += 256)
         stage[i] = feats[static_cast<int64_t>(t.feat_row + t0_base) * f0 + i];
-    const bool live = c0 + c < ch;
-    float w[9];
+    for (int c0 = 0; c0 < ch; c0 += kSubCh) {
+        const bool live = c0 + c < ch;
+        float w[9];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) w[k] = live ? w0[k * ch + c0 + c] : 0.0f;
-    const float bias0 = live ? b0[c0 + c] : 0.0f;
-    __syncthreads();
-    // conv0 + ReLU: h1[t1][f1][c], row by row (no index division), frequencies strided by group.
-    for (int r = 0; r < t1_rows; ++r) {
-        const int t1 = t1_base + r;
-        const float* rows[3];
-        bool ok[3];
-#pragma unroll
-        for (int dt = 0; dt < 3; ++dt) {
-            const int t0 = 2 * t1 + dt - 1;
-            ok[dt] = t0 >= 0 && t0 < t.t0;
-            rows[dt] = stage + (ok[dt] ? t0 - t0_base : 0) * f0;
-        }
-        float* hrow = h1 + r * f1n * kSubCh + c;
-        for (int f1 = grp; f1 < f1n; f1 += kGroups) {
-            float o = bias0;
+        for (int k = 0; k < 9; ++k) w[k] = live ? w0[k * ch + c0 + c] : 0.0f;
+        const float bias0 = live ? b0[c0 + c] : 0.0f;
+        __syncthreads();
+        // conv0 + ReLU: h1[t1][f1][c], row by row (no index division), frequencies strided by group.
+        for (int r = 0; r < t1_rows; ++r) {
+            const int t1 = t1_base + r;
+            const float* rows[3];
+            bool ok[3];
 #pragma unroll
             for (int dt = 0; dt < 3; ++dt) {
-                if (!ok[dt]) continue;
-#pragma unroll
-                for (int df = 0; df < 3; ++df) {
-                    const int ff = 2 * f1 + df - 1;
-                    if (ff < 0 || ff >= f0) continue;
-                    o = madd(o, w[dt * 3 + df], rows[dt][ff]);
-                }
+                const int t0 = 2 * t1 + dt - 1;
+                ok[dt] = t0 >= 0 && t0 < t.t0;
+                rows[dt] = stage + (ok[dt] ? t0 - t0_base : 0) * f0;
             }
-            hrow[f1 * kSubCh] = fmaxf(o, 0.0f);
-        }
-    }
+            float* hrow = h1 + r * f1n * kSubCh + c;
+            for (int f1 = grp; f1 < f1n; f1 += kGroups) {
+                float o = bias0;
 #pragma unroll
-    for (int k = 0; k < 9; ++k) w[k] = live ? w1[k * ch + c0 + c] : 0.0f;
-    const float bias1 = live ? b1[c0 + c] : 0.0f;
-    __syncthreads();
-    // Depthwise conv1: out[t2][f2][c]
-    for (int r = 0; r < t.t2_count; ++r) {
-        const int t2 = t.t2_first + r;
-        const float* rows[3];
-        bool ok[3];
+                for (int dt = 0; dt < 3; ++dt) {
+                    if (!ok[dt]) continue;
 #pragma unroll
-        for (int dt = 0; dt < 3; ++dt) {
-            const int t1 = 2 * t2 + dt - 1;
-            ok[dt] = t1 >= 0 && t1 < t1n;
-            rows[dt] = h1 + (ok[dt] ? t1 - t1_base : 0) * f1n * kSubCh + c;
+                    for (int df = 0; df < 3; ++df) {
+                        const int ff = 2 * f1 + df - 1;
+                        if (ff < 0 || ff >= f0) continue;
+                        o = madd(o, w[dt * 3 + df], rows[dt][ff]);
+                    }
+                }
+                hrow[f1 * kSubCh] = fmaxf(o, 0.0f);
+            }
         }
-        float* orow = out + (static_cast<int64_t>(t.out_row) + static_cast<int64_t>(r) * f2n) * ch + c0 + c;
-        for (int f2 = grp; f2 < f2n; f2 += kGroups) {
-            float acc = bias1;
+#pragma unroll
+        for (int k = 0; k < 9; ++k) w[k] = live ? w1[k * ch + c0 + c] : 0.0f;
+        const float bias1 = live ? b1[c0 + c] : 0.0f;
+        __syncthreads();
+        // Depthwise conv1: out[t2][f2][c]
+        for (int r = 0; r < t.t2_count; ++r) {
+            const int t2 = t.t2_first + r;
+            const float* rows[3];
+            bool ok[3];
 #pragma unroll
             for (int dt = 0; dt < 3; ++dt) {
-                if (!ok[dt]) continue;
-#pragma unroll
-                for (int df = 0; df < 3; ++df) {
-                    const int f1 = 2 * f2 + df - 1;
-                    if (f1 < 0 || f1 >= f1n) continue;
-                    acc = madd(acc, w[dt * 3 + df], rows[dt][f1 * kSubCh]);
-                }
+                const int t1 = 2 * t2 + dt - 1;
+                ok[dt] = t1 >= 0 && t1 < t1n;
+                rows[dt] = h1 + (ok[dt] ? t1 - t1_base : 0) * f1n * kSubCh + c;
             }
-            if (live) orow[static_cast<int64_t>(f2) * ch] = acc;
+            float* orow = out + (static_cast<int64_t>(t.out_row) + static_cast<int64_t>(r) * f2n) * ch + c0 + c;
+            for (int f2 = grp; f2 < f2n; f2 += kGroups) {
+                float acc = bias1;
+#pragma unroll
+                for (int dt = 0; dt < 3; ++dt) {
+                    if (!ok[dt]) continue;
+#pragma unroll
+                    for (int df = 0; df < 3; ++df) {
+                        const int f1 = 2 * f2 + df - 1;
+                        if (f1 < 0 || f1 >= f1n) continue;
+                        acc = madd(acc, w[dt * 3 + df], rows[dt][f1 * kSubCh]);
+                    }
+                }
+                if (live) orow[static_cast<int64_t>(f2) * ch] = acc;
+            }
         }
+        __syncthreads();  // the next channel block's conv0 overwrites h1
     }
 }
 
@@ -604,8 +606,7 @@ cudaError_t sub_front(const float* feats, int f0, const SubTask* tasks, int n_ta
     const cudaError_t e =
         cudaFuncSetAttribute(sub_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    dim3 grid(n_tasks, (ch + kSubCh - 1) / kSubCh);
-    sub_front_kernel<<<grid, 256, smem, s>>>(feats, f0, tasks, ch, w0, b0, w1, b1, out);
+    sub_front_kernel<<<n_tasks, 256, smem, s>>>(feats, f0, tasks, ch, w0, b0, w1, b1, out);
     return cudaGetLastError();
 }
 
