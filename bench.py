@@ -8,7 +8,8 @@ Workloads (seeded synthetic data, telmo_b200/synthetic.py):
            audio), through the config-2 Granite-shaped int8 CTC model: log-mel front end,
            16-block encoder, CTC head, greedy argmax and collapse. Utterances are sharded across
            ranks by longest-first greedy assignment (no collective; each rank keeps its tokens)
-           and processed in length-sorted batches of up to --batch-seconds of audio. A step is
+           and processed in length-sorted batches of about equal audio, at most 4500 s each
+           (ceil(shard seconds / 4500) of them). A step is
            one pass over the whole set. metric = RTFx (audio seconds / wall second), whole job.
   parakeet config 4: 256 utterances, lengths uniform in 1-30 s (about 4,000 s of audio), through
            the Parakeet-TDT-shaped int8 model: 128-bin log-mel, 8x convolutional subsampling,
@@ -119,7 +120,7 @@ class GraniteWorkload:
     unit = "audio-s/s"
     POOL = 64  # distinct 30 s base waveforms; utterance u is a slice of waveform u % 64
 
-    def __init__(self, rank, world, n_utt=4096, batch_seconds=2048.0, precision="int8"):
+    def __init__(self, rank, world, n_utt=4096, batch_seconds=4500.0, precision="int8"):
         from telmo_b200 import sharding, synthetic
         self.synthetic = synthetic
         self.n_utt = n_utt
@@ -191,8 +192,9 @@ class GraniteWorkload:
         self.bo = 0
         # End to end: the whole shard in one telmo_granite_transcribe call with host buffers; it
         # transcribes in groups of batch_seconds (the same cut as self.batches, since self.mine is
-        # length-sorted) and copies each group's audio up while the previous group runs.
-        self.model.set_transcribe_group(self.batch_seconds)
+        # length-sorted) and copies each group's audio up while the previous group runs -- in at
+        # least two groups, so that a copy overlaps compute even when the shard fits one batch.
+        self.model.set_transcribe_group(min(self.batch_seconds, self.rank_seconds / 2 + 1.0))
         self.mine_lengths = np.ascontiguousarray(self.samples[self.mine], dtype=np.int64)
         all_frames = sum(self.model.frames_for_samples(int(x)) for x in self.mine_lengths)
         self.host_tokens_all = torch.empty(3 * all_frames + 3, dtype=torch.int32).pin_memory()

@@ -200,8 +200,11 @@ class Granite:
         of tokens."""
         lengths = np.ascontiguousarray(lengths, dtype=np.int64)
         n = lengths.size
-        cap = sum(self.frames_for_samples(int(x)) for x in lengths)
-        tokens = tokens_buf if tokens_buf is not None else np.zeros(3 * max(cap, 1), np.uint32)
+        if tokens_buf is not None:  # the caller sized it (3 x the utterances' frames)
+            tokens = tokens_buf
+        else:
+            cap = sum(self.frames_for_samples(int(x)) for x in lengths)
+            tokens = np.zeros(3 * max(cap, 1), np.uint32)
         counts = np.zeros(n, np.int32)
         frames = np.zeros(n, np.int32)
         ptr = samples.data_ptr() if hasattr(samples, "data_ptr") else samples.ctypes.data

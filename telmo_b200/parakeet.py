@@ -159,8 +159,11 @@ class Parakeet:
         the triples packed utterance after utterance."""
         lengths = np.ascontiguousarray(lengths, dtype=np.int64)
         n = lengths.size
-        cap = 3 * self.config["max_symbols"] * sum(frames_for_samples(int(x)) for x in lengths) + 3
-        tokens = tokens_buf if tokens_buf is not None else np.zeros(cap, np.uint32)
+        if tokens_buf is not None:  # the caller sized it (3 x max_symbols x the frames, + 3)
+            tokens = tokens_buf
+        else:
+            cap = 3 * self.config["max_symbols"] * sum(frames_for_samples(int(x)) for x in lengths) + 3
+            tokens = np.zeros(cap, np.uint32)
         counts = np.zeros(n, np.int32)
         frames = np.zeros(n, np.int32)
         ptr = samples.data_ptr() if hasattr(samples, "data_ptr") else samples.ctypes.data
