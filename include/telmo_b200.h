@@ -226,8 +226,9 @@ size_t telmo_granite_frames_for_samples(const telmo_granite *g, int64_t samples)
  * group's audio (2048 s unless set below; ceil(total / group) groups of about equal audio, an
  * utterance longer than a group alone in its own): while one group is transcribed on `stream`,
  * the next group's samples go up on the model's own copy stream (staged through pinned memory
- * when `samples` is pageable), and each group's tokens come back behind it. Returns once the
- * tokens, counts and frames are in host memory. */
+ * when `samples` is pageable); the tokens and counts of all groups stay on the device and come
+ * back in one copy after the last group. Returns once the tokens, counts and frames are in host
+ * memory. */
 int telmo_granite_transcribe(telmo_granite *g, const float *samples, const int64_t *lengths,
                              int n_utt, uint32_t *tokens, int *counts, int *frames, void *stream);
 /* The audio per group of telmo_granite_transcribe, in seconds (at least 0.02). */

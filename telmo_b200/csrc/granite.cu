@@ -67,6 +67,11 @@ void Granite::release_pipeline() {
     tokens_pinned = nullptr;
     counts_pinned = nullptr;
     tokens_pinned_cap = counts_pinned_cap = 0;
+    if (call_tokens_dev) cudaFree(call_tokens_dev);
+    if (call_counts_dev) cudaFree(call_counts_dev);
+    call_tokens_dev = nullptr;
+    call_counts_dev = nullptr;
+    call_tokens_cap = call_counts_cap = 0;
     if (copy_stream) cudaStreamDestroy(copy_stream);
     copy_stream = nullptr;
 }
@@ -184,6 +189,19 @@ int Granite::transcribe_host(const float* samples, const int64_t* lengths, int n
             return rc;
         counts_pinned_cap = static_cast<size_t>(n_utt);
     }
+    if (tok_need > call_tokens_cap || static_cast<size_t>(n_utt) > call_counts_cap) {
+        cudaDeviceSynchronize();
+        if (call_tokens_dev) cudaFree(call_tokens_dev);
+        if (call_counts_dev) cudaFree(call_counts_dev);
+        call_tokens_dev = nullptr;
+        call_counts_dev = nullptr;
+        call_tokens_cap = call_counts_cap = 0;
+        const size_t tc = std::max(tok_need, call_tokens_cap), uc = std::max<size_t>(n_utt, call_counts_cap);
+        if (int rc = ctx->cuda(cudaMalloc(&call_tokens_dev, sizeof(uint32_t) * tc), "transcribe")) return rc;
+        if (int rc = ctx->cuda(cudaMalloc(&call_counts_dev, sizeof(int) * uc), "transcribe")) return rc;
+        call_tokens_cap = tc;
+        call_counts_cap = uc;
+    }
     uint32_t* tok_out = pinned_tokens ? tokens : tokens_pinned;
     int* cnt_out = pinned_counts ? counts : counts_pinned;
 
@@ -212,23 +230,22 @@ int Granite::transcribe_host(const float* samples, const int64_t* lengths, int n
     for (int g = 0; g < groups; ++g) {
         const int b = g % 2, u0 = first[g], n = first[g + 1] - first[g];
         if (int rc = ctx->cuda(cudaStreamWaitEvent(s, group_copied[b], 0), "transcribe")) return rc;
-        if (int rc = transcribe_device(group_audio[b], lengths + u0, n, tokens_dev, counts_dev, frames + u0, s))
+        if (int rc = transcribe_device(group_audio[b], lengths + u0, n, call_tokens_dev + 3 * tok_at,
+                                       call_counts_dev + u0, frames + u0, s))
             return rc;
         if (int rc = ctx->cuda(cudaEventRecord(group_read[b], s), "transcribe")) return rc;
-        int64_t f = 0;
-        for (int u = u0; u < u0 + n; ++u) f += frames[u];
-        if (int rc = ctx->cuda(cudaMemcpyAsync(tok_out + 3 * tok_at, tokens_dev, sizeof(uint32_t) * 3 * f,
-                                               cudaMemcpyDeviceToHost, s),
-                               "transcribe"))
-            return rc;
-        if (int rc = ctx->cuda(cudaMemcpyAsync(cnt_out + u0, counts_dev, sizeof(int) * n, cudaMemcpyDeviceToHost, s),
-                               "transcribe"))
-            return rc;
-        tok_at += f;
+        for (int u = u0; u < u0 + n; ++u) tok_at += frames[u];
         // The next group's audio goes up while this one is transcribed.
         if (g + 1 < groups)
             if (int rc = put(g + 1)) return rc;
     }
+    if (int rc = ctx->cuda(cudaMemcpyAsync(tok_out, call_tokens_dev, sizeof(uint32_t) * 3 * tok_at,
+                                           cudaMemcpyDeviceToHost, s),
+                           "transcribe"))
+        return rc;
+    if (int rc = ctx->cuda(cudaMemcpyAsync(cnt_out, call_counts_dev, sizeof(int) * n_utt, cudaMemcpyDeviceToHost, s),
+                           "transcribe"))
+        return rc;
     if (int rc = ctx->cuda(cudaStreamSynchronize(s), "transcribe")) return rc;
     if (!pinned_tokens) std::memcpy(tokens, tokens_pinned, sizeof(uint32_t) * 3 * tok_at);
     if (!pinned_counts) std::memcpy(counts, counts_pinned, sizeof(int) * n_utt);

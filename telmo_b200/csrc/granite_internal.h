@@ -87,6 +87,12 @@ struct Granite {
     size_t tokens_pinned_cap = 0;
     int* counts_pinned = nullptr;
     size_t counts_pinned_cap = 0;
+    // A call's tokens and counts stay on the device until its last group is done, then come back
+    // in one copy each.
+    uint32_t* call_tokens_dev = nullptr;
+    size_t call_tokens_cap = 0;
+    int* call_counts_dev = nullptr;
+    size_t call_counts_cap = 0;
     float* feats_dev = nullptr;
     float* enc_dev = nullptr;
     uint32_t* ids_dev = nullptr;
