@@ -97,6 +97,37 @@ __device__ __forceinline__ float rcp_approx(float x) {
 __device__ __forceinline__ float mul_sigmoid(float a, float b) {
     return __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(b, -1.44269504f)))));
 }
+
+// sm_100's packed two-wide f32 multiply and add, each lane rounded to nearest even as the scalar
+// mul.rn / add.rn. Unlike the scalar forms they are not kept out of contraction: the compiler
+// turns a packed multiply whose result feeds a packed add into one packed fused multiply-add,
+// even under -fmad=false (measured on B200: every lane of such a chain gave the fma chain's
+// bits; a packed add fed by scalar __fmul_rn products, or a packed multiply whose products a
+// scalar __fadd_rn adds, gave the scalar chain's), so callers that must round the product keep
+// one side of each multiply-add scalar.
+__device__ __forceinline__ uint64_t pack_f2(float2 v) {
+    return (static_cast<uint64_t>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 unpack_f2(uint64_t v) {
+    return make_float2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
+}
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a)), "l"(pack_f2(b)));
+    return unpack_f2(d);
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a)), "l"(pack_f2(b)));
+    return unpack_f2(d);
+}
+
+// mul_sigmoid on two lanes: the same bits per lane.
+__device__ __forceinline__ float2 mul_sigmoid2(float2 a, float2 b) {
+    const float2 t = fmul2_rn(b, make_float2(-1.44269504f, -1.44269504f));
+    const float2 s = fadd2_rn(make_float2(1.0f, 1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+    return fmul2_rn(a, make_float2(rcp_approx(s.x), rcp_approx(s.y)));
+}
 #endif
 
 cudaError_t quantize_x2(const float* x, int64_t ldx, int m, int k, const QuantAct& q,

@@ -25,6 +25,8 @@ SHAPES = [  # channels, kernel, stride, frames
     (200, 3, 2, 3),
     (1536, 15, 2, 130),
     (64, 11, 1, 35),
+    (301, 7, 1, 40),
+    (1535, 15, 1, 70),
 ]
 
 
@@ -83,3 +85,33 @@ def test_conv_module_rows_refusals(ctx):
     with pytest.raises(TelmoError):  # no output
         kern.conv_module_rows(x, 8, 1024, 15, 1, w, b, None)
     ctx.check()
+
+
+@pytest.mark.parametrize("channels,kernel,frames", [(2048, 15, 100), (1024, 9, 65), (256, 5, 7)])
+def test_two_channel_kernel_gives_the_one_channel_kernels_bits(ctx, channels, kernel, frames):
+    # 8-byte aligned rows of an even channel count take the two-channel kernel; the same rows one
+    # float into a larger buffer (4-byte aligned) take the one-channel kernel. Same bits.
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(channels + kernel + frames)
+    kern = Kernels(ctx)
+
+    def run(offset):
+        x = torch.empty(frames * 2 * channels + 1, device="cuda")
+        w = torch.empty(kernel * channels + 1, device="cuda")
+        b = torch.empty(channels + 1, device="cuda")
+        o = torch.empty(frames * channels + 1, device="cuda")
+        xs, ws, bs, os_ = (t[offset:offset + n] for t, n in ((x, frames * 2 * channels), (w, kernel * channels),
+                                                             (b, channels), (o, frames * channels)))
+        xs.copy_(xin.reshape(-1))
+        ws.copy_(win.reshape(-1))
+        bs.copy_(bin_)
+        kern.conv_module_rows(xs, frames, channels, kernel, 1, ws, bs, os_)
+        return os_.clone()
+
+    xin = torch.randn(frames, 2 * channels, device="cuda", generator=g)
+    win = 0.3 * torch.randn(kernel, channels, device="cuda", generator=g)
+    bin_ = 0.1 * torch.randn(channels, device="cuda", generator=g)
+    pair, single = run(0), run(1)
+    torch.cuda.synchronize()
+    ctx.check()
+    assert torch.equal(pair.view(torch.int32), single.view(torch.int32))
