@@ -13,17 +13,18 @@
 // bits of each operand, so the sums match the reference's f32 sums to about 1e-6 relative.
 //
 // Structure: a persistent, warp-specialised kernel, one CTA per SM, one (block, head) at a time.
-//   warp 0      TMA producer: Q as soon as the previous products no longer read Q's buffer, K once
-//               the previous softmax is done with K's buffer (its position windows), the
-//               relative table once the previous O product is done with V, V once the position
-//               product is done with the table (V takes the table's buffer)
+//   warp 0      TMA producer: Q and K as soon as the previous S and position products no longer
+//               read their buffers (so they load during the previous softmax), the relative
+//               table once the previous O product is done with V, V once the position product is
+//               done with the table (V takes the table's buffer)
 //   warp 1      MMA issuer: S, then pos (which waits for the previous O product: P lives in pos's
 //               columns), then O once P is in TMEM
 //   warps 2-9   softmax and output, two warps per TMEM lane quarter (warp w reads lanes
-//               32 (w % 4) ..), each on half of a query row's keys: S and the position window
-//               from TMEM, the shifted position term through a per-warp shared-memory window (a
-//               row's positions start at a column that differs per lane, which one TMEM load
-//               cannot address), the row maximum and sum across the pair through shared memory,
+//               32 (w % 4) ..), each on half of a query row's keys: S and a 64-column span of
+//               the positions from TMEM, the row's own 32 positions brought to the front of the
+//               registers by a five-stage shift on the bits of 31 - lane (a row's positions start
+//               at a column that differs per lane, which one TMEM load cannot address), the row
+//               maximum and sum across the pair through shared memory,
 //               P split to fp16 planes into TMEM (the O product's A operand), then O to global
 //               memory.
 // TMEM: S in columns 0..127, pos in 128..383 (then P: hi 128..191, lo 192..255), O in 384..511;
@@ -54,8 +55,6 @@ constexpr int kRelHalf = 2 * kBox;           // 256 positions x 64 fp16
 constexpr uint32_t kColS = 0, kColPos = 128, kColP = 128, kColO = 384, kTmemCols = 512;
 constexpr int kSmemBytes = 3 * kOperand + 256 * 4 + 2 * 2 * 128 * 8 + 128 + 1024;
 
-static_assert(kEpiWarps * kWindowBytes <= kOperand, "the position windows live in K's buffer");
-
 struct Bars {
     uint64_t q_full, k_full, r_full, v_full, s_done, p_full, o_done, o_free;
 };
@@ -69,7 +68,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* buf_q = smem;                 // Q
-    uint8_t* buf_k = smem + kOperand;      // K, then the position windows
+    uint8_t* buf_k = smem + kOperand;      // K
     uint8_t* buf_r = smem + 2 * kOperand;  // the relative table, then V
     float* rs = reinterpret_cast<float*>(smem + 3 * kOperand);
     float* red_max = rs + 256;                                   // [2 halves][128 rows]
@@ -128,12 +127,11 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 const bool short_block = tk.len <= 64;
                 const CUtensorMap* mq = short_block ? &map_qkv64 : &map_qkv;
                 const uint32_t bytes = short_block ? kOperand / 2 : kOperand;
-                // Q: the previous S and position products are done with Q's buffer.
+                // Q and K: the previous S and position products (one commit) are done with their
+                // buffers, so both load while the previous softmax runs.
                 if (it > 0 && !mbar_wait(&bars->s_done, prev)) { fail(); break; }
                 mbar_arrive_expect_tx(&bars->q_full, bytes);
                 load_operand(mq, &bars->q_full, buf_q, h * HD, y_hi, y_lo);
-                // K: the previous softmax is done with its position windows in K's buffer.
-                if (it > 0 && !mbar_wait(&bars->p_full, prev)) { fail(); break; }
                 mbar_arrive_expect_tx(&bars->k_full, bytes);
                 load_operand(mq, &bars->k_full, buf_k, D + h * HD, y_hi, y_lo);
                 // The relative table: the previous O product is done with V in the table's buffer.
@@ -212,7 +210,7 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
         const int quad = warp & 3, half = (warp - 2) >> 2;
         const int row = quad * 32 + lane;
         const uint32_t lanes = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-        float* win = reinterpret_cast<float*>(buf_k + (warp - 2) * kWindowBytes);
+        const int sh = 31 - lane;  // where this lane's positions start in its warp's span
         int it = 0;
         for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x, ++it) {
             const AttnTask tk = tasks[w / heads];
@@ -227,32 +225,36 @@ granite_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const _
                 const int c = 2 * half + cc;
                 // Keys 32c .. 32c + 31 of row i read positions 127 - i + 32c + j: for this warp's rows
                 // the columns 96 - 32 quad + 32c .. + 63 hold them all; lane l's 32 start at element
-                // 31 - l of that window.
+                // 31 - l of that span, brought to the front of the lane's registers by shifts of
+                // 16, 8, 4, 2 and 1 on the bits of 31 - l (each stage keeps what the later ones
+                // can still reach).
+                uint32_t p0[32], p1[32], pw[64];
+                tmem_ld32(lanes + kColPos + 96 - 32 * quad + 32 * c, p0);
+                tmem_ld32(lanes + kColPos + 128 - 32 * quad + 32 * c, p1);
+                tmem_ld_wait();
 #pragma unroll
-                for (int wh = 0; wh < 2; ++wh) {
-                    uint32_t pw[32];
-                    tmem_ld32(lanes + kColPos + 96 + 32 * wh - 32 * quad + 32 * c, pw);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        *reinterpret_cast<uint4*>(win + win_index(lane, 32 * wh + 4 * m)) =
-                            make_uint4(pw[4 * m], pw[4 * m + 1], pw[4 * m + 2], pw[4 * m + 3]);
+                for (int k = 0; k < 32; ++k) {
+                    pw[k] = p0[k];
+                    pw[32 + k] = p1[k];
                 }
+                shift_down<47, 16>(pw, (sh & 16) != 0);
+                shift_down<39, 8>(pw, (sh & 8) != 0);
+                shift_down<35, 4>(pw, (sh & 4) != 0);
+                shift_down<33, 2>(pw, (sh & 2) != 0);
+                shift_down<32, 1>(pw, (sh & 1) != 0);
                 uint32_t sv[32];
                 tmem_ld32(lanes + kColS + 32 * c, sv);
                 tmem_ld_wait();
-                __syncwarp();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int key = 32 * c + j;
-                    const float pos = win[win_index(lane, 31 - lane + j)];
+                    const float pos = __uint_as_float(pw[j]);
                     const float ps = rs[T - 1 - row + key];
                     float v = __fadd_rn(__fmul_rn(__uint_as_float(sv[j]), scale), __fmul_rn(pos, ps));
                     if (key >= len) v = -INFINITY;
                     lg[32 * cc + j] = v;
                     mx = fmaxf(mx, v);
                 }
-                __syncwarp();
             }
             red_max[half * T + row] = mx;
             epi_sync<32 * kEpiWarps>();

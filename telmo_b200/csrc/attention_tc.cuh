@@ -1,6 +1,6 @@
 // attention_tc.cuh -- device helpers shared by the tcgen05 attention kernels (attention_tc.cu,
 // txl_attention_tc.cu): operand staging from the QKV product's fp16 planes, the fp16 split of
-// probabilities, the softmax warps' barrier and their position windows.
+// probabilities, the softmax warps' barrier and the register shift of their position spans.
 #pragma once
 
 #include "ptx.cuh"
@@ -12,7 +12,6 @@ namespace tc_attention {
 
 constexpr int kBox = 128 * 128;     // one 128-row x 64-fp16 box, 128-byte swizzle (16 KB)
 constexpr int kOperand = 4 * kBox;  // hi and lo planes, two 64-column halves each
-constexpr int kWindowBytes = 32 * 64 * 4;  // one warp's position window: 32 rows x 64 f32
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void record_error(uint32_t* error, uint32_t code) {
@@ -49,10 +48,14 @@ __device__ __forceinline__ void epi_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kThreadsInBarrier) : "memory");
 }
 
-// A warp's position window: row l (a lane) holds 64 f32 with 16-byte chunk m at chunk m ^ (l % 8),
-// which keeps both the lanes' row writes and their diagonal reads free of bank conflicts.
-__device__ __forceinline__ int win_index(int l, int e) {
-    return l * 64 + ((((e >> 2) ^ l) & 7) | (e >> 2 & 8)) * 4 + (e & 3);
+// v[k] = v[k + D] for k < N when `on` (N + D <= 64), else v unchanged: one stage of a shift by a
+// per-lane amount, done on values already in registers (ascending k reads each v[k + D] before
+// this stage overwrites it).
+template <int N, int D>
+__device__ __forceinline__ void shift_down(uint32_t (&v)[64], bool on) {
+    static_assert(N + D <= 64, "the stage reads inside the array");
+#pragma unroll
+    for (int k = 0; k < N; ++k) v[k] = on ? v[k + D] : v[k];
 }
 
 }  // namespace tc_attention

@@ -22,15 +22,17 @@
 //
 // Structure: persistent and warp-specialised, one CTA per SM.
 //   warp 0      TMA producer: Q once per task; per chunk the first position half (once the
-//               previous softmax is done with the position buffer), K (once the previous O
+//               previous chunk's position products are done with the position buffer, so it
+//               loads during the previous softmax), K (once the previous O
 //               product is done with V, which shares K's buffer), the second position half
 //               (once the first half's product is done), V (once the S product is done with K)
 //   warp 1      MMA issuer: BD first half, S, BD second half, then O once P is in TMEM
 //   warps 2-9   softmax and output: warp w reads TMEM lanes 32 (w % 4) ..; warps 2-5 take keys
-//               0..63 of a chunk and output columns 0..63, warps 6-9 the rest
+//               0..63 of a chunk and output columns 0..63, warps 6-9 the rest; a row's own
+//               positions come out of a 64-column span of BD by a five-stage register shift on
+//               the bits of 31 - lane (one TMEM load cannot start at a per-lane column)
 // TMEM: S in columns 0..127, BD in 128..383 (then P: hi 128..191, lo 192..255), O in 384..511.
-// Shared memory: Q, K then V, and the position window then the softmax warps' shifted-position
-// windows, 64 KB each. Every wait is bounded; on timeout the kernel records kErrWaitTimeout in the
+// Shared memory: Q, K then V, and the two position halves in turn, 64 KB each. Every wait is bounded; on timeout the kernel records kErrWaitTimeout in the
 // error word and returns.
 #include "attention_tc.cuh"
 #include "kernels.h"
@@ -56,8 +58,6 @@ constexpr int kThreads = 64 + kEpiThreads;
 constexpr uint32_t kColS = 0, kColBD = 128, kColP = 128, kColO = 384, kTmemCols = 512;
 constexpr int kSmemBytes = 3 * kOperand + (256 + 128 + 2 * 128 + 2 * 128) * 4 + 256 + 1024;
 
-static_assert(kEpiWarps * kWindowBytes <= kOperand, "the position windows live in the position buffer");
-
 struct Bars {
     uint64_t q_full, k_full, pa_full, pb_full, v_full, k_free, pa_free, s_done, p_full, o_done, o_free;
 };
@@ -71,7 +71,7 @@ txl_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __gri
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* buf_q = smem;                  // Q of the task
     uint8_t* buf_kv = smem + kOperand;      // K, then V of the chunk
-    uint8_t* buf_pos = smem + 2 * kOperand; // a position half, then the other, then the windows
+    uint8_t* buf_pos = smem + 2 * kOperand; // a position half, then the other
     float* cvw = reinterpret_cast<float*>(smem + 3 * kOperand);  // cv over the chunk's window [256]
     float* ukw = cvw + 256;                                       // uk over the chunk's keys [128]
     float* red_max = ukw + 128;                                   // [2 halves][128 rows]
@@ -132,7 +132,9 @@ txl_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __gri
                     const int j0 = c * T;
                     const int pw = tk.pos_row + t - 1 - i0 - (T - 1) + j0;  // the window's first row
                     const uint32_t prev = (it - 1) & 1;
-                    if (it > 0 && !mbar_wait(&bars->p_full, prev)) { fail(); ok = false; break; }
+                    // The first position half: the previous chunk's second position product (the
+                    // s_done commit) is done with the position buffer.
+                    if (it > 0 && !mbar_wait(&bars->s_done, prev)) { fail(); ok = false; break; }
                     mbar_arrive_expect_tx(&bars->pa_full, kOperand);
                     load_operand(&map_pos, &bars->pa_full, buf_pos, h * HD, pw, npos + pw);
                     if (it > 0 && !mbar_wait(&bars->o_done, prev)) { fail(); ok = false; break; }
@@ -224,7 +226,7 @@ txl_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __gri
         const int row = quad * 32 + lane;
         const int et = threadIdx.x - 64;  // 0 .. 255
         const uint32_t lanes = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-        float* win = reinterpret_cast<float*>(buf_pos + (warp - 2) * kWindowBytes);
+        const int sh = 31 - lane;  // where this lane's positions start in its warp's span
         int it = 0;
         bool ok = true;
         for (int w = blockIdx.x; ok && w < total && !*abort_flag; w += gridDim.x) {
@@ -255,33 +257,36 @@ txl_attention_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __gri
                     const int kc = 2 * half + cc;  // 32-key group of the chunk
                     // Keys 32 kc .. + 31 of row r read window rows 127 - r + 32 kc + j: for this warp's
                     // rows the columns 96 - 32 quad + 32 kc .. + 63 of BD hold them all; lane l's 32
-                    // start at element 31 - l of that window.
+                    // start at element 31 - l of that span, brought to the front of the lane's
+                    // registers by shifts of 16, 8, 4, 2 and 1 on the bits of 31 - l.
+                    uint32_t p0[32], p1[32], pv[64];
+                    tmem_ld32(lanes + kColBD + 96 - 32 * quad + 32 * kc, p0);
+                    tmem_ld32(lanes + kColBD + 128 - 32 * quad + 32 * kc, p1);
+                    tmem_ld_wait();
 #pragma unroll
-                    for (int wh = 0; wh < 2; ++wh) {
-                        uint32_t pv[32];
-                        tmem_ld32(lanes + kColBD + 96 + 32 * wh - 32 * quad + 32 * kc, pv);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int m = 0; m < 8; ++m)
-                            *reinterpret_cast<uint4*>(win + win_index(lane, 32 * wh + 4 * m)) =
-                                make_uint4(pv[4 * m], pv[4 * m + 1], pv[4 * m + 2], pv[4 * m + 3]);
+                    for (int k = 0; k < 32; ++k) {
+                        pv[k] = p0[k];
+                        pv[32 + k] = p1[k];
                     }
+                    shift_down<47, 16>(pv, (sh & 16) != 0);
+                    shift_down<39, 8>(pv, (sh & 8) != 0);
+                    shift_down<35, 4>(pv, (sh & 4) != 0);
+                    shift_down<33, 2>(pv, (sh & 2) != 0);
+                    shift_down<32, 1>(pv, (sh & 1) != 0);
                     uint32_t sv[32];
                     tmem_ld32(lanes + kColS + 32 * kc, sv);
                     tmem_ld_wait();
-                    __syncwarp();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int key = 32 * kc + j;
                         const int wcol = T - 1 - row + key;
                         const float ac = __fadd_rn(__uint_as_float(sv[j]), ukw[key]);
-                        const float bd = __fadd_rn(win[win_index(lane, 31 - lane + j)], cvw[wcol]);
+                        const float bd = __fadd_rn(__uint_as_float(pv[j]), cvw[wcol]);
                         float v = __fmul_rn(__fadd_rn(ac, bd), scale);
                         if (j0 + key >= t) v = -INFINITY;
                         lg[32 * cc + j] = v;
                         mx = fmaxf(mx, v);
                     }
-                    __syncwarp();
                 }
                 red_max[half * T + row] = mx;
                 epi_sync<kEpiThreads>();
